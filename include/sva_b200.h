@@ -1,0 +1,144 @@
+/*
+ * sva_b200.h -- C ABI of the B200 (sm_100a) summon -> verify decode path.
+ *
+ * Every entry point takes device pointers, sizes in elements, and a cudaStream_t passed as
+ * void*.  Nothing here allocates device memory: callers pass outputs and a workspace sized by
+ * the matching *_workspace_size() call.  No entry point synchronises the stream.  Each returns
+ * SVA_OK or an sva_status error code; sva_last_error() gives a one-line message for the last
+ * failure on the calling thread.
+ *
+ * Reference interfaces replaced (asystemoffields/sva):
+ *   sva_catalog_encode      sva/llama.py:578-624 (_key_catalog: k_low einsum + encode_product_keys)
+ *                           sva/ops.py:24-47 (encode_product_keys), sva/ops.py:10-21 (assign_to_centroids)
+ *   sva_assign_centroids    sva/ops.py:10-21 (assign_to_centroids)
+ *   sva_pq_scores           sva/ops.py:50-71 (product_quantized_scores)
+ *   sva_decode              sva/llama.py:171-328 (SVALlamaAttention.sva_attention, scan summon path)
+ *   sva_postings_build      sva/llama.py:626-657 (_rebuild_postings)
+ *   sva_decode_inverted     sva/llama.py:427-576 (_inverted_static_decode_attention) and
+ *                           sva/llama.py:330-425 (_inverted_decode_attention)
+ *   sva_top_unique          sva/llama.py:83-116 (_top_unique_candidates)
+ */
+#ifndef SVA_B200_H_
+#define SVA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum sva_status {
+  SVA_OK = 0,
+  SVA_ERR_SHAPE = 1,     /* unsupported or inconsistent sizes */
+  SVA_ERR_WORKSPACE = 2, /* workspace smaller than *_workspace_size() */
+  SVA_ERR_TIMEOUT = 3,   /* a bounded wait gave up */
+  SVA_ERR_CUDA = 4,      /* a CUDA launch or runtime call failed */
+  SVA_ERR_ALIGN = 5,     /* pointer or stride alignment not supported */
+  SVA_ERR_DTYPE = 6      /* unsupported dtype code */
+} sva_status;
+
+typedef enum sva_dtype { SVA_DTYPE_F32 = 0, SVA_DTYPE_BF16 = 1, SVA_DTYPE_F16 = 2 } sva_dtype;
+
+/* Device counters accumulated by the decode entry points (unsigned 64-bit). */
+enum {
+  SVA_STAT_QUERIES = 0,
+  SVA_STAT_SUMMONED = 1,
+  SVA_STAT_REFILL_POOL = 2,
+  SVA_STAT_EXACT_SCORED = 3,
+  SVA_STAT_VERIFIED = 4,
+  SVA_STAT_CELL_VISITS = 5,
+  SVA_STAT_COUNT = 8
+};
+
+/* Library version string and last error message (thread-local). */
+const char* sva_version(void);
+const char* sva_last_error(void);
+
+/* ---------------------------------------------------------------------------------------
+ * Write path: key catalog.
+ * k_low[h][l][:] = K[h / (H/Hkv)][l][:] . k_proj[h]        (fp32, sequential order over D)
+ * codes[h][l][s] = argmin_c (|x|^2 - 2 x.c) + |c|^2,  x = k_low[h][l][s*R/S:(s+1)*R/S]
+ * for l in [start, start + count).  Layouts: keys [Hkv][*][D] with the given strides;
+ * k_proj [H][D][R]; codebooks [H][S][C][R/S]; k_low [H][*][R] (row stride R);
+ * codes [H][*][S] uint8 (row stride S).  Either k_low or codes may be NULL to skip it
+ * (codes still need k_low values, which are then kept in registers only).
+ * Replaces sva/llama.py:578-624 and sva/ops.py:10-47.
+ * ------------------------------------------------------------------------------------- */
+int sva_catalog_encode(const void* keys, int32_t key_dtype, int64_t key_head_stride, int64_t key_row_stride,
+                       int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t rank_dim,
+                       const float* k_proj, const float* codebooks, int32_t subspaces, int32_t codewords,
+                       int64_t start, int64_t count, float* k_low, int64_t k_low_head_stride, uint8_t* codes,
+                       int64_t codes_head_stride, void* stream);
+
+/* Nearest centroid of each row of x [n][dim] (row stride x_row_stride) among centroids
+ * [C][dim]; labels as int64.  Replaces sva/ops.py:10-21. */
+int sva_assign_centroids(const float* x, int64_t n, int32_t dim, int64_t x_row_stride, const float* centroids,
+                         int32_t codewords, int64_t* labels, void* stream);
+
+/* ADC scores: scores[h][t][l] = (sum_s lut[h][t][s][codes[h][l][s]]) / sqrt(R) with
+ * lut[h][t][s][c] = q_low[h][t][s-part] . codebooks[h][s][c].  q_low [H][T][R];
+ * codes [H][L][S] uint8; scores [H][T][L] fp32.  Replaces sva/ops.py:50-71. */
+int sva_pq_scores(const float* q_low, int32_t n_heads, int32_t n_queries, int32_t rank_dim, const float* codebooks,
+                  int32_t subspaces, int32_t codewords, const uint8_t* codes, int64_t key_len, float* scores,
+                  void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Scan summon -> rank rescore -> exact verify for H heads x T query tokens.
+ * Replaces sva/llama.py:171-328.  Per (head h, token t):
+ *   q_low = (q . q_proj[h]) * scale[h]; lut = q_low parts . codebooks;
+ *   shortlist = top-min(shortlist, allowed) allowed keys by ADC score (score desc, index asc);
+ *   final = top-min(budget, |shortlist|) of the shortlist by q_low . k_low / sqrt(R);
+ *   out = softmax(q . K[final] * softmax_scale) @ V[final].
+ * ------------------------------------------------------------------------------------- */
+typedef struct sva_decode_args {
+  int32_t n_heads;
+  int32_t n_kv_heads;
+  int32_t n_queries;
+  int32_t head_dim;
+  int32_t rank_dim;
+  int32_t subspaces;
+  int32_t codewords;
+  int32_t shortlist;
+  int32_t budget;
+  int32_t qkv_dtype;   /* sva_dtype of query, keys, values and out */
+  int32_t logits_mode; /* 0: fp32 logits; 1: logits rounded like the value dtype (scan path) */
+  float softmax_scale;
+  int64_t key_len;
+  /* query side */
+  const void* query; /* [H][T][D] */
+  int64_t q_head_stride, q_row_stride;
+  const float* q_proj;       /* [H][D][R] */
+  const float* scale;        /* [H], clamp(exp(logit_scale), 0.01, 100) */
+  const float* codebooks;    /* [H][S][C][R/S] */
+  const float* lut_override; /* [H][T][S][C] or NULL */
+  /* catalog and cache */
+  const uint8_t* codes; /* [H][L][S] */
+  int64_t codes_head_stride;
+  const float* k_low; /* [H][L][R] */
+  int64_t k_low_head_stride;
+  const void* keys; /* [Hkv][L][D] */
+  int64_t k_head_stride, k_row_stride;
+  const void* values; /* [Hkv][L][D] */
+  int64_t v_head_stride, v_row_stride;
+  /* masking: key l is allowed for token t iff l < allowed_len[t] (NULL: L - T + t + 1) and
+   * (allowed_mask == NULL or allowed_mask[t * mask_row_stride + l] != 0) */
+  const int64_t* allowed_len;
+  const uint8_t* allowed_mask;
+  int64_t mask_row_stride;
+  /* outputs */
+  void* out; /* [H][T][D] */
+  int64_t out_head_stride, out_row_stride;
+  int32_t* shortlist_out;    /* [H][T][shortlist] ascending key index, -1 padded, or NULL */
+  int32_t* final_out;        /* [H][T][budget] ascending key index, -1 padded, or NULL */
+  unsigned long long* stats; /* [SVA_STAT_COUNT] accumulated, or NULL */
+} sva_decode_args;
+
+size_t sva_decode_workspace_size(const sva_decode_args* args);
+int sva_decode(const sva_decode_args* args, void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SVA_B200_H_ */

@@ -193,12 +193,15 @@ def build_catalog(keys_f32: np.ndarray, k_proj: np.ndarray, codebooks: np.ndarra
 # summon (reference sva/llama.py:211, sva/ops.py:50-71, sva/llama.py:270-302)
 # ----------------------------------------------------------------------------------------
 
-def query_low(q_f32: np.ndarray, q_proj: np.ndarray, logit_scale: np.ndarray) -> np.ndarray:
+def query_low(q_f32: np.ndarray, q_proj: np.ndarray, logit_scale: np.ndarray, scale: np.ndarray | None = None) -> np.ndarray:
     """q_low[h, t, :] = (q[h, t, :] . Qproj[h]) * clamp(exp(logit_scale[h]), 0.01, 100).
 
-    Reference sva/llama.py:69-73 (scale buffer) and :211 (einsum then scale).
+    Reference sva/llama.py:69-73 (scale buffer) and :211 (einsum then scale).  ``scale`` may be
+    given precomputed (the reference computes it once with torch at patch time).
     """
-    scale = np.clip(np.exp(np.asarray(logit_scale, dtype=np.float32)), np.float32(0.01), np.float32(100.0)).astype(np.float32)
+    if scale is None:
+        scale = sva_scale(logit_scale)
+    scale = np.asarray(scale, dtype=np.float32)
     n_heads, n_q, head_dim = q_f32.shape
     rank = q_proj.shape[-1]
     out = np.empty((n_heads, n_q, rank), dtype=np.float32)
@@ -286,7 +289,7 @@ def scan_decode(q_f32: np.ndarray, q_proj: np.ndarray, logit_scale: np.ndarray, 
                 codes: np.ndarray, k_low: np.ndarray, keys_f32: np.ndarray, values_f32: np.ndarray,
                 shortlist: int, budget: int, scaling: float, dtype: str = "f32", logits_mode: int = 0,
                 allowed_len: np.ndarray | None = None, allowed_mask: np.ndarray | None = None,
-                lut_override: np.ndarray | None = None) -> DecodeResult:
+                lut_override: np.ndarray | None = None, scale: np.ndarray | None = None) -> DecodeResult:
     """Scan summon -> rank-64 rescore -> exact verify (reference sva/llama.py:171-328).
 
     q_f32 [H, T, D]; codes [H, L, S]; k_low [H, L, R]; keys/values [Hkv, L, D] (float32 copies
@@ -297,7 +300,7 @@ def scan_decode(q_f32: np.ndarray, q_proj: np.ndarray, logit_scale: np.ndarray, 
     n_kv = keys_f32.shape[0]
     groups = n_heads // n_kv
     key_len = codes.shape[1]
-    ql = query_low(q_f32, q_proj, logit_scale)
+    ql = query_low(q_f32, q_proj, logit_scale, scale)
     lut = build_lut(ql, codebooks) if lut_override is None else np.asarray(lut_override, dtype=np.float32)
     scores = adc_scores(lut, codes, rank)
     sl_cap = min(shortlist, key_len)

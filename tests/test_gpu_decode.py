@@ -1,0 +1,197 @@
+"""GPU parity of the write path and the scan summon -> verify decode (sva_catalog_encode, sva_decode).
+
+The CUDA path and the CPU oracle implement the same canonical arithmetic and tie rule, so
+codes, k_low, shortlists and final indices must be bit-identical; attention outputs are
+compared within 1e-3 (fp32) / 2e-2 (bf16).  The reference's own golden outputs are checked
+directly as well (tests/golden/golden_v1.npz).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import sva_oracle as O
+from tests.golden.inputs import config1, config2
+from tests.helpers import (cached_case, gpu_catalog, gpu_decode, oracle_decode, to_np, tolerance, unpad)
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = np.load(__file__.replace("test_gpu_decode.py", "golden/golden_v1.npz"))
+CASES = ["cfg1", "cfg2s_1x256", "cfg2s_4x64"]
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_catalog_bit_exact(name):
+    case, (k_low_ref, codes_ref) = cached_case(name)
+    k_low, codes = gpu_catalog(case)
+    np.testing.assert_array_equal(k_low.cpu().numpy(), k_low_ref)
+    np.testing.assert_array_equal(codes.cpu().numpy(), codes_ref.astype(np.uint8))
+    np.testing.assert_array_equal(codes.cpu().numpy(), GOLDEN[f"{name}_codes"])
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_decode_matches_oracle_and_reference(name):
+    case, (k_low_ref, codes_ref) = cached_case(name)
+    k_low, codes = gpu_catalog(case)
+    out, sl, fin = gpu_decode(case, k_low, codes)
+    torch.cuda.synchronize()
+    ref = oracle_decode(case, k_low_ref, codes_ref)
+    sl, fin = sl.cpu().numpy(), fin.cpu().numpy()
+    rtol, atol = tolerance(case)
+    for h in range(case.n_heads):
+        np.testing.assert_array_equal(unpad(sl[h, 0]), ref.shortlist[h][0])
+        np.testing.assert_array_equal(unpad(fin[h, 0]), np.sort(ref.final[h][0]))
+        # and the reference's golden selection (canonical tie rule on its own scores)
+        np.testing.assert_array_equal(unpad(sl[h, 0]), GOLDEN[f"{name}_shortlist_canon"][h])
+        np.testing.assert_array_equal(unpad(fin[h, 0]), np.sort(GOLDEN[f"{name}_final_canon"][h]))
+    got = to_np(out)[:, 0]
+    np.testing.assert_allclose(got, ref.out[:, 0], rtol=rtol, atol=atol)
+    np.testing.assert_allclose(got, GOLDEN[f"{name}_out_canon"], rtol=rtol, atol=atol)
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_shortlist_bit_exact_with_reference_lut(name):
+    """Staged parity: the reference's own fp32 LUT and codes in, the reference shortlist out."""
+    case, (k_low_ref, _) = cached_case(name)
+    k_low = torch.from_numpy(k_low_ref).cuda()
+    codes = torch.from_numpy(GOLDEN[f"{name}_codes"]).cuda()
+    lut = torch.from_numpy(GOLDEN[f"{name}_lut"]).cuda().contiguous()
+    _, sl, _ = gpu_decode(case, k_low, codes, lut_override=lut)
+    sl = sl.cpu().numpy()
+    for h in range(case.n_heads):
+        np.testing.assert_array_equal(unpad(sl[h, 0]), GOLDEN[f"{name}_shortlist_canon"][h])
+
+
+@pytest.mark.parametrize("logits_mode", [0, 1])
+def test_fp32_and_dtype_logits_modes(logits_mode):
+    case, (k_low_ref, codes_ref) = cached_case("cfg2s_4x64")
+    k_low, codes = gpu_catalog(case)
+    out, _, fin = gpu_decode(case, k_low, codes, logits_mode=logits_mode)
+    ref = oracle_decode(case, k_low_ref, codes_ref, logits_mode=logits_mode)
+    np.testing.assert_allclose(to_np(out)[:, 0], ref.out[:, 0], rtol=2e-2, atol=2e-2)
+
+
+def _small_case(key_len, n_heads=3, n_kv=1, seed=3, dtype=torch.float32, subspaces=2, codewords=16, head_dim=64,
+                rank=64):
+    gen = torch.Generator().manual_seed(seed)
+    q = torch.randn(1, n_heads, 1, head_dim, generator=gen).to(dtype)
+    keys = torch.randn(1, n_kv, key_len, head_dim, generator=gen).to(dtype)
+    values = torch.randn(1, n_kv, key_len, head_dim, generator=gen).to(dtype)
+    from tests.golden.inputs import DecodeCase
+
+    return DecodeCase("small", q, keys, values, torch.randn(n_heads, head_dim, rank, generator=gen) * 0.125,
+                      torch.randn(n_heads, head_dim, rank, generator=gen) * 0.125, torch.randn(n_heads, generator=gen) * 0.3,
+                      torch.randn(n_heads, subspaces, codewords, rank // subspaces, generator=gen), 64, 16,
+                      torch.zeros(n_kv, 0, dtype=torch.long))
+
+
+@pytest.mark.parametrize("key_len,shortlist,budget", [(1, 4, 2), (5, 4, 2), (37, 64, 16), (300, 64, 80), (3000, 200, 50)])
+def test_edge_sizes(key_len, shortlist, budget):
+    case = _small_case(key_len)
+    k_low_ref, codes_ref = O.build_catalog(to_np(case.keys[0]), case.k_proj.numpy(), case.codebooks.numpy(), 3)
+    k_low, codes = gpu_catalog(case)
+    np.testing.assert_array_equal(codes.cpu().numpy(), codes_ref)
+    out, sl, fin = gpu_decode(case, k_low, codes, shortlist=shortlist, budget=budget)
+    ref = oracle_decode(case, k_low_ref, codes_ref, shortlist=shortlist, budget=budget)
+    for h in range(case.n_heads):
+        np.testing.assert_array_equal(unpad(sl.cpu().numpy()[h, 0]), ref.shortlist[h][0])
+        np.testing.assert_array_equal(unpad(fin.cpu().numpy()[h, 0]), np.sort(ref.final[h][0]))
+    np.testing.assert_allclose(to_np(out)[:, 0], ref.out[:, 0], rtol=1e-4, atol=1e-5)
+
+
+def test_tiny_shapes_head_dim_8_rank_4():
+    """The reference unit-test geometry: head_dim 8, rank 4, 2x8 codes."""
+    case = _small_case(6, n_heads=2, n_kv=2, head_dim=8, rank=4, subspaces=2, codewords=8)
+    k_low_ref, codes_ref = O.build_catalog(to_np(case.keys[0]), case.k_proj.numpy(), case.codebooks.numpy(), 1)
+    k_low, codes = gpu_catalog(case)
+    np.testing.assert_array_equal(k_low.cpu().numpy(), k_low_ref)
+    np.testing.assert_array_equal(codes.cpu().numpy(), codes_ref)
+    out, sl, fin = gpu_decode(case, k_low, codes, shortlist=4, budget=2)
+    ref = oracle_decode(case, k_low_ref, codes_ref, shortlist=4, budget=2)
+    for h in range(2):
+        np.testing.assert_array_equal(unpad(sl.cpu().numpy()[h, 0]), ref.shortlist[h][0])
+        np.testing.assert_array_equal(unpad(fin.cpu().numpy()[h, 0]), np.sort(ref.final[h][0]))
+    np.testing.assert_allclose(to_np(out)[:, 0], ref.out[:, 0], rtol=1e-4, atol=1e-5)
+
+
+def test_prefill_causal_and_mask():
+    """T > 1 query tokens with the default causal rule and with an explicit allowed mask."""
+    case = _small_case(400, n_heads=2, n_kv=1)
+    gen = torch.Generator().manual_seed(9)
+    q = torch.randn(2, 24, 64, generator=gen)
+    k_low_ref, codes_ref = O.build_catalog(to_np(case.keys[0]), case.k_proj.numpy(), case.codebooks.numpy(), 2)
+    k_low, codes = gpu_catalog(case)
+    out, sl, fin = gpu_decode(case, k_low, codes, q=q, shortlist=64, budget=16)
+    ref = oracle_decode(case, k_low_ref, codes_ref, q=q, shortlist=64, budget=16)
+    for h in range(2):
+        for t in range(24):
+            np.testing.assert_array_equal(unpad(sl.cpu().numpy()[h, t]), ref.shortlist[h][t])
+            np.testing.assert_array_equal(unpad(fin.cpu().numpy()[h, t]), np.sort(ref.final[h][t]))
+    np.testing.assert_allclose(to_np(out), ref.out, rtol=1e-4, atol=1e-5)
+    mask = torch.rand(24, 400, generator=gen) > 0.7
+    mask_dev = mask.to(torch.uint8).cuda()
+    out, sl, fin = gpu_decode(case, k_low, codes, q=q, shortlist=64, budget=16, allowed_mask=mask_dev,
+                              allowed_len=torch.full((24,), 400, dtype=torch.int64, device="cuda"))
+    ref = oracle_decode(case, k_low_ref, codes_ref, q=q, shortlist=64, budget=16, allowed_mask=mask.numpy())
+    for h in range(2):
+        for t in range(24):
+            np.testing.assert_array_equal(unpad(sl.cpu().numpy()[h, t]), ref.shortlist[h][t])
+            np.testing.assert_array_equal(unpad(fin.cpu().numpy()[h, t]), np.sort(ref.final[h][t]))
+    np.testing.assert_allclose(to_np(out), ref.out, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("key_len", [20000, 70000])
+def test_all_scores_tied_picks_lowest_indices(key_len):
+    """A zero query makes every ADC and rank score 0: the canonical rule keeps the lowest key
+    indices.  At 70000 keys (grid schedule) the tie overflows the candidate buffer and exercises
+    the exact streaming fallback."""
+    case = _small_case(key_len, n_heads=1, n_kv=1)
+    k_low, codes = gpu_catalog(case)
+    q = torch.zeros(1, 1, 64)
+    _, sl, fin = gpu_decode(case, k_low, codes, q=q, shortlist=2048, budget=512)
+    np.testing.assert_array_equal(unpad(sl.cpu().numpy()[0, 0]), np.arange(2048))
+    np.testing.assert_array_equal(unpad(fin.cpu().numpy()[0, 0]), np.arange(512))
+
+
+@pytest.mark.parametrize("subspaces,codewords", [(1, 256), (4, 64)])
+def test_million_keys(subspaces, codewords):
+    """Config 2 at full size (2^20 keys, bf16): GPU catalog, oracle decode on the GPU catalog,
+    a sampled nearest-codeword check of the codes, and the planted near-duplicates recovered."""
+    case = config2(key_len=1 << 20, subspaces=subspaces, codewords=codewords)
+    k_low, codes = gpu_catalog(case)
+    out, sl, fin = gpu_decode(case, k_low, codes)
+    kl, cd = k_low.cpu().numpy(), codes.cpu().numpy().astype(np.int64)
+    rng = np.random.default_rng(0)
+    rows = rng.choice(case.key_len, 4096, replace=False)
+    sub = 64 // subspaces
+    for s in range(subspaces):
+        lab = O.assign_to_centroids(kl[0, rows, s * sub:(s + 1) * sub], case.codebooks.numpy()[0, s])
+        np.testing.assert_array_equal(cd[0, rows, s], lab)
+    proj = O.project_keys(to_np(case.keys[0])[:, rows], case.k_proj.numpy(), 1)
+    np.testing.assert_array_equal(kl[0, rows], proj[0])
+    ref = oracle_decode(case, kl, cd)
+    np.testing.assert_array_equal(unpad(sl.cpu().numpy()[0, 0]), ref.shortlist[0][0])
+    np.testing.assert_array_equal(unpad(fin.cpu().numpy()[0, 0]), np.sort(ref.final[0][0]))
+    np.testing.assert_allclose(to_np(out)[:, 0], ref.out[:, 0], rtol=2e-2, atol=2e-2)
+    planted = set(case.planted[0].tolist())
+    assert len(planted & set(unpad(fin.cpu().numpy()[0, 0]).tolist())) >= 48
+
+
+def test_stats_counters():
+    case, (k_low_ref, codes_ref) = cached_case("cfg1")
+    k_low, codes = gpu_catalog(case)
+    stats = torch.zeros(8, dtype=torch.int64, device="cuda")
+    gpu_decode(case, k_low, codes, stats=stats)
+    s = stats.cpu().tolist()
+    assert s[0] == 9 and s[1] == 9 * 2048 and s[3] == 9 * 512 and s[4] == 9 * 512
+
+
+def test_cpu_tensors_are_rejected():
+    from sva_b200 import kernels
+
+    case, _ = cached_case("cfg1")
+    with pytest.raises(RuntimeError, match="CUDA"):
+        kernels.decode(case.q[0], case.q_proj, case.logit_scale, case.codebooks, torch.zeros(9, 8, 2, dtype=torch.uint8),
+                       torch.zeros(9, 8, 64), case.keys[0], case.values[0], 4, 2)
