@@ -55,6 +55,12 @@ enum {
 const char* sva_version(void);
 const char* sva_last_error(void);
 
+/* Timing hook (no reference counterpart; measurement only).  When set on the calling thread,
+ * every multi-kernel entry point records events[i] (a cudaEvent_t created with timing enabled)
+ * on its stream right after its i-th internal kernel launch, for i < n.  Events are recorded as
+ * external events, so the hook also works inside CUDA-graph capture.  Pass n = 0 to clear. */
+int sva_profile_events(void* const* events, int32_t n);
+
 /* ---------------------------------------------------------------------------------------
  * Write path: key catalog.
  * k_low[h][l][:] = K[h / (H/Hkv)][l][:] . k_proj[h]        (fp32, sequential order over D)

@@ -37,6 +37,7 @@ STAT_COUNT = 8
 EXPORTED = (
     "sva_version",
     "sva_last_error",
+    "sva_profile_events",
     "sva_catalog_encode",
     "sva_assign_centroids",
     "sva_pq_scores",
@@ -170,6 +171,7 @@ def load() -> ctypes.CDLL:
         lib.sva_version.restype = ctypes.c_char_p
         lib.sva_last_error.restype = ctypes.c_char_p
         sigs = {
+            "sva_profile_events": ([c_vp, c_i32], ctypes.c_int),
             "sva_catalog_encode": ([c_vp, c_i32, c_i64, c_i64, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_i32, c_i32,
                                     c_i64, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp], ctypes.c_int),
             "sva_assign_centroids": ([c_vp, c_i64, c_i32, c_i64, c_vp, c_i32, c_vp, c_vp], ctypes.c_int),

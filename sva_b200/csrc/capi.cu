@@ -32,7 +32,21 @@ int ensure_smem_attr(const void* kernel, int bytes) {
   return SVA_OK;
 }
 
+static thread_local void* const* g_prof_events = nullptr;
+static thread_local int g_prof_n = 0;
+
+void profile_mark(int i, cudaStream_t stream) {
+  if (g_prof_events && i < g_prof_n && g_prof_events[i])
+    cudaEventRecordWithFlags(static_cast<cudaEvent_t>(g_prof_events[i]), stream, cudaEventRecordExternal);
+}
+
 }  // namespace sva
+
+extern "C" int sva_profile_events(void* const* events, int32_t n) {
+  sva::g_prof_events = (n > 0) ? events : nullptr;
+  sva::g_prof_n = (n > 0) ? n : 0;
+  return SVA_OK;
+}
 
 extern "C" const char* sva_version(void) { return "sva_b200 0.1.0 (sm_100a)"; }
 

@@ -685,13 +685,17 @@ static int launch_decode(DecodePlan& plan, void* ws, cudaStream_t stream) {
     p.ws_part = reinterpret_cast<int32_t*>(base + reinterpret_cast<size_t>(p.ws_part));
     p.ws_cand = reinterpret_cast<uint2*>(base + reinterpret_cast<size_t>(p.ws_cand));
     decode_qlut_kernel<T><<<P, 256, 0, stream>>>(p);
+    profile_mark(0, stream);
     dim3 grid(p.nseg, P);
     decode_hist_kernel<<<grid, 256, 0, stream>>>(p);
+    profile_mark(1, stream);
     decode_collect_kernel<<<grid, 256, 0, stream>>>(p);
+    profile_mark(2, stream);
   }
   int rc = ensure_smem_attr(reinterpret_cast<const void*>(decode_problem_kernel<T>), kMaxDynSmem);
   if (rc != SVA_OK) return rc;
   decode_problem_kernel<T><<<P, kThreads, plan.smem_bytes, stream>>>(p);
+  profile_mark(p.grid_mode ? 3 : 0, stream);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
   return SVA_OK;

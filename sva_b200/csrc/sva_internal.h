@@ -20,4 +20,7 @@ int set_error(int code, const char* msg);
 // Raises a kernel's dynamic shared-memory limit once per (kernel, device).
 int ensure_smem_attr(const void* kernel, int bytes);
 
+// Records the calling thread's i-th profiling event (sva_profile_events) on `stream`, if set.
+void profile_mark(int i, cudaStream_t stream);
+
 }  // namespace sva

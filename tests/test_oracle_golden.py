@@ -173,3 +173,25 @@ def test_tree_dot_matches_definition():
             parts = [np.float32(parts[j] + parts[j ^ step]) for j in range(16)]
         assert got[r] == parts[0]
     del lanes
+
+
+def test_cpu_baseline_decoder_matches_oracle():
+    """The threaded CPU decoder used for the timed baseline computes the oracle's result."""
+    from oracle.cpu_baseline import CpuDecoder, topk_canonical_fast
+
+    rng = np.random.default_rng(1)
+    s = rng.integers(0, 50, 5000).astype(np.float32)
+    for k in (1, 7, 100, 4999, 5000):
+        np.testing.assert_array_equal(topk_canonical_fast(s, k), O.topk_canonical(s, k))
+    case = config2(key_len=1 << 14, subspaces=4, codewords=64, n_heads=3, n_planted=8)
+    keys, values, q = _np(case.keys[0]), _np(case.values[0]), _np(case.q[0])
+    k_low, codes = O.build_catalog(keys, case.k_proj.numpy(), case.codebooks.numpy(), 1)
+    ref = O.scan_decode(q, case.q_proj.numpy(), case.logit_scale.numpy(), case.codebooks.numpy(), codes, k_low, keys,
+                        values, 2048, 512, 0.125, "bf16", logits_mode=1)
+    kb = case.keys[0].view(torch.int16).numpy().view(np.uint16)
+    vb = case.values[0].view(torch.int16).numpy().view(np.uint16)
+    dec = CpuDecoder(case.q_proj.numpy(), O.sva_scale(case.logit_scale.numpy()), case.codebooks.numpy(),
+                     codes.astype(np.uint8), k_low, kb, vb, groups=1)
+    got = dec(q[:, 0], 2048, 512, 0.125, "bf16", 1)
+    dec.close()
+    np.testing.assert_array_equal(got, ref.out[:, 0])
