@@ -344,7 +344,12 @@ def gpu_arm(args):
 
     n_prof = 4
     prof = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(n_prof + 1)]
-    handles = (ctypes_voidp_array([e.cuda_event for e in prof[1:]]))
+    for e in prof:  # torch creates the CUDA event on its first record
+        e.record()
+    torch.cuda.synchronize()
+    handles = ctypes_voidp_array([e.cuda_event for e in prof[1:]])
+    if not all(e.cuda_event for e in prof):
+        raise RuntimeError("profiling events were not created")
     graph = torch.cuda.CUDAGraph()
     qps = args.queries_per_step
     stream = torch.cuda.Stream(device)

@@ -143,6 +143,93 @@ typedef struct sva_decode_args {
 size_t sva_decode_workspace_size(const sva_decode_args* args);
 int sva_decode(const sva_decode_args* args, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------------------------------------------------
+ * Posting lists of the static inverted index.  Replaces sva/llama.py:626-657.
+ * For every (head, subspace): counts [H][S][C], offsets [H][S][C+1] (CSR) and ids
+ * [H][S][ids_sub_stride] holding the keys [0, key_len) grouped by code, ascending inside a cell.
+ * *max_bucket (device int32) receives the largest cell size over all heads and subspaces.
+ * ------------------------------------------------------------------------------------- */
+size_t sva_postings_workspace_size(int32_t n_heads, int32_t subspaces, int32_t codewords, int64_t key_len);
+int sva_postings_build(const uint8_t* codes, int64_t codes_head_stride, int32_t n_heads, int32_t subspaces,
+                       int32_t codewords, int64_t key_len, int32_t* counts, int32_t* offsets, int32_t* ids,
+                       int64_t ids_sub_stride, int32_t* max_bucket, void* workspace, size_t workspace_bytes,
+                       void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Inverted-index summon -> rank rescore -> verify for one query token per head.
+ * static  (dynamic == 0), replaces sva/llama.py:427-576: candidates are the posting lists of the
+ *         top `cells` codewords per subspace (code score desc, codeword asc) plus the tail keys
+ *         [postings_len, key_len) (or the current key key_len-1 when there is no tail); the
+ *         refill window is the first min(W, max(budget, budget * refill_factor)) entries in
+ *         (rank score desc, key asc) order counting duplicates, W the reference's padded width;
+ *         the window's unique keys, best first, are the selection (sva/llama.py:83-116).
+ * dynamic (dynamic == 1), replaces sva/llama.py:330-425: all unique candidates plus the current
+ *         key are ranked; no tail, no window.
+ * Both then apply the adaptive budget rule (margin between the best and the min_budget-th
+ * rank score) and verify with fp32 logits.  `budget` is the already clamped max budget,
+ * min_budget / mid_budget are clamped as the reference clamps them.
+ * ------------------------------------------------------------------------------------- */
+typedef struct sva_inverted_args {
+  int32_t n_heads;
+  int32_t n_kv_heads;
+  int32_t head_dim;
+  int32_t rank_dim;
+  int32_t subspaces;
+  int32_t codewords;
+  int32_t budget;
+  int32_t cells;
+  int32_t refill_factor;
+  int32_t dynamic;
+  int32_t min_budget;
+  int32_t mid_budget;
+  int32_t qkv_dtype;
+  float low_margin;
+  float high_margin;
+  float softmax_scale;
+  int64_t key_len;      /* keys in k_low / K / V */
+  int64_t postings_len; /* keys covered by the posting lists */
+  int64_t allowed_len;  /* keys [0, allowed_len) are allowed */
+  const void* query;    /* [H][D], one token per head */
+  int64_t q_head_stride;
+  const float* q_proj;
+  const float* scale;
+  const float* codebooks;
+  const uint8_t* codes; /* [H][>= postings_len][S] */
+  int64_t codes_head_stride;
+  const int32_t* post_counts;  /* [H][S][C] */
+  const int32_t* post_offsets; /* [H][S][C+1] */
+  const int32_t* post_ids;     /* [H][S][post_ids_sub_stride] */
+  int64_t post_ids_sub_stride;
+  const int32_t* max_bucket; /* device int32 from sva_postings_build */
+  const float* k_low;        /* [H][key_len][R] */
+  int64_t k_low_head_stride;
+  const void* keys; /* [Hkv][key_len][D] */
+  int64_t k_head_stride, k_row_stride;
+  const void* values;
+  int64_t v_head_stride, v_row_stride;
+  void* out; /* [H][D] */
+  int64_t out_head_stride;
+  int32_t* sel_idx_out;      /* [H][budget] selection, best first (0 in invalid slots), or NULL */
+  uint8_t* sel_valid_out;    /* [H][budget] refill validity before the budget cut, or NULL */
+  float* sel_score_out;      /* [H][budget] rank scores (float min in invalid slots), or NULL */
+  int32_t* budget_out;       /* [H] adaptive budget per head, or NULL */
+  unsigned long long* stats; /* [SVA_STAT_COUNT] accumulated, or NULL */
+} sva_inverted_args;
+
+size_t sva_inverted_workspace_size(const sva_inverted_args* args);
+int sva_decode_inverted(const sva_inverted_args* args, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Refill-and-dedupe selection on explicit candidate rows.  Replaces sva/llama.py:83-116
+ * (_top_unique_candidates).  idx [rows][width] int64, scores [rows][width] fp32, valid
+ * [rows][width] uint8; outputs [rows][min(budget, refill)] best first: sel_idx int64 (0 in
+ * invalid slots), sel_scores (float min in invalid slots), sel_valid uint8; *refill_out (host
+ * int32) receives the refill count.  width <= 8192.
+ * ------------------------------------------------------------------------------------- */
+int sva_top_unique(const int64_t* idx, const float* scores, const uint8_t* valid, int32_t rows, int32_t width,
+                   int32_t budget, int32_t refill_factor, int64_t* sel_idx, float* sel_scores, uint8_t* sel_valid,
+                   int32_t* refill_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -120,11 +120,9 @@ class InvertedArgs(ctypes.Structure):
         ("min_budget", c_i32),
         ("mid_budget", c_i32),
         ("qkv_dtype", c_i32),
-        ("max_bucket", c_i32),
         ("low_margin", c_f32),
         ("high_margin", c_f32),
         ("softmax_scale", c_f32),
-        ("pad0", c_i32),
         ("key_len", c_i64),
         ("postings_len", c_i64),
         ("allowed_len", c_i64),
@@ -138,7 +136,8 @@ class InvertedArgs(ctypes.Structure):
         ("post_counts", c_vp),
         ("post_offsets", c_vp),
         ("post_ids", c_vp),
-        ("post_head_stride", c_i64),
+        ("post_ids_sub_stride", c_i64),
+        ("max_bucket", c_vp),
         ("k_low", c_vp),
         ("k_low_head_stride", c_i64),
         ("keys", c_vp),
@@ -151,6 +150,8 @@ class InvertedArgs(ctypes.Structure):
         ("out_head_stride", c_i64),
         ("sel_idx_out", c_vp),
         ("sel_valid_out", c_vp),
+        ("sel_score_out", c_vp),
+        ("budget_out", c_vp),
         ("stats", c_vp),
     ]
 
@@ -183,8 +184,8 @@ def load() -> ctypes.CDLL:
                                     c_sz, c_vp], ctypes.c_int),
             "sva_inverted_workspace_size": ([ctypes.POINTER(InvertedArgs)], c_sz),
             "sva_decode_inverted": ([ctypes.POINTER(InvertedArgs), c_vp, c_sz, c_vp], ctypes.c_int),
-            "sva_top_unique": ([c_vp, c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp],
-                               ctypes.c_int),
+            "sva_top_unique": ([c_vp, c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp,
+                                ctypes.POINTER(ctypes.c_int32), c_vp], ctypes.c_int),
         }
         for name, (argtypes, restype) in sigs.items():
             fn = getattr(lib, name, None)

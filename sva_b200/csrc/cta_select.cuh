@@ -1,17 +1,18 @@
 // Exact top-k selection inside one CTA under the canonical tie rule.
 //
-// Items are (key32, idx32) pairs produced by a functor; key32 is an ordered score key
-// (sva::ordered_key) and key32 == 0 marks an item that is not a candidate.  The selection
-// order is the 64-bit composite  (key32 << 32) | ~idx32  taken in descending order, i.e.
-// score descending, then key index ascending -- the rule the CPU oracle applies to every
-// torch.topk of the reference (sva/llama.py:278, :295, :100, :113).
+// Items are 64-bit composites produced by a functor, c = (key32 << 32) | ~idx32, where key32 is
+// an ordered score key (sva::ordered_key); c == 0 marks an item that is not a candidate.  The
+// selection order is c descending, i.e. score descending, then key index ascending -- the rule
+// the CPU oracle applies to every torch.topk of the reference (sva/llama.py:278, :295, :100,
+// :113).  A caller whose items share their top bits may pass a left-shifted composite that
+// keeps only the varying bits, as long as the order is preserved and real items stay non-zero.
 //
-// The select is an MSB-first radix select with 8-bit digits.  Each level makes one pass over
-// the items (a functor call per item, so the items may live in shared memory or be recomputed
-// from global memory), builds a 256-bin histogram of the digit among items that still match
-// the prefix, and fixes one digit.  It stops as soon as the boundary bin holds exactly the
-// number of items still needed.  An item is selected iff key32 != 0 and
-// (composite & mask) >= prefix.
+// The select is an MSB-first radix select with 8-bit digits starting at bit `top_bit`.  Each
+// level makes one pass over the items (a functor call per item, so items may live in shared
+// memory or be re-read from global memory), builds a 256-bin histogram of the digit among the
+// items that still match the prefix, and fixes one digit.  It stops as soon as the boundary
+// digit holds exactly the number of items still needed.  An item is selected iff c != 0 and
+// (c & mask) >= prefix.
 #pragma once
 
 #include "sva_common.cuh"
@@ -27,8 +28,8 @@ __device__ __forceinline__ unsigned long long composite(uint32_t key, uint32_t i
   return (static_cast<unsigned long long>(key) << 32) | static_cast<unsigned long long>(~idx);
 }
 
-__device__ __forceinline__ bool is_selected(const SelectThreshold& t, uint32_t key, uint32_t idx) {
-  return key != 0u && (composite(key, idx) & t.mask) >= t.prefix;
+__device__ __forceinline__ bool is_selected(const SelectThreshold& t, unsigned long long c) {
+  return c != 0ull && (c & t.mask) >= t.prefix;
 }
 
 // Shared scratch for cta_radix_select: 256-bin histogram plus a few broadcast slots.
@@ -40,36 +41,35 @@ struct SelectScratch {
   int count;
 };
 
-// Requires blockDim.x >= 256 and a multiple of 32.  `k` must not exceed the number of items
-// with key32 != 0.  All threads of the block must call it.
+// Requires blockDim.x >= 256 and a multiple of 32.  `k` must not exceed the number of non-zero
+// items.  All threads of the block must call it.  Digits are bits [top_bit-7, top_bit],
+// [top_bit-15, top_bit-8], ... (top_bit in 7..63, the last digit may be narrower).
 template <class ItemFn>
-__device__ SelectThreshold cta_radix_select(const ItemFn& item, int n, int k, SelectScratch* sc) {
+__device__ SelectThreshold cta_radix_select(const ItemFn& item, int n, int k, SelectScratch* sc, int top_bit = 63) {
   SelectThreshold thr;
   thr.prefix = 0ull;
   thr.mask = 0ull;
   if (k <= 0) {
-    thr.prefix = ~0ull;  // selects nothing: (c & 0) >= ~0 is false
-    thr.mask = 0ull;
+    thr.prefix = ~0ull;  // (c & 0) >= ~0 is false for every item
     return thr;
   }
   int remaining = k;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
-  for (int level = 0; level < 8; ++level) {
-    const int shift = 56 - 8 * level;
+  for (int hi = top_bit; hi >= 0; hi -= 8) {
+    const int lo = hi >= 7 ? hi - 7 : 0;
+    const int width = hi - lo + 1;
+    const unsigned long long dmask = ((1ull << width) - 1ull) << lo;
     for (int b = tid; b < 256; b += blockDim.x) sc->hist[b] = 0u;
     __syncthreads();
     for (int i = tid; i < n; i += blockDim.x) {
-      uint32_t key, idx;
-      item(i, key, idx);
-      if (key == 0u) continue;
-      unsigned long long c = composite(key, idx);
-      if ((c & thr.mask) != thr.prefix) continue;
-      atomicAdd(&sc->hist[(c >> shift) & 0xFFull], 1u);
+      const unsigned long long c = item(i);
+      if (c == 0ull || (c & thr.mask) != thr.prefix) continue;
+      atomicAdd(&sc->hist[(c >> lo) & ((1ull << width) - 1ull)], 1u);
     }
     __syncthreads();
-    // Descending suffix scan over the 256 digits with warps 0..7 (thread t owns digit 255-t):
-    // the owner of the first digit whose running count reaches `remaining` is the boundary.
+    // Descending suffix scan over the digits with warps 0..7 (thread t owns digit 255-t): the
+    // owner of the first digit whose running count reaches `remaining` is the boundary.
     int v = 0, incl = 0;
     if (tid < 256) {
       v = static_cast<int>(sc->hist[255 - tid]);
@@ -88,20 +88,20 @@ __device__ SelectThreshold cta_radix_select(const ItemFn& item, int n, int k, Se
       }
     }
     __syncthreads();
-    const int d = sc->digit;
+    const unsigned long long d = static_cast<unsigned long long>(sc->digit);
     remaining -= sc->above;
     const int cnt = sc->count;
-    thr.prefix |= static_cast<unsigned long long>(d) << shift;
-    thr.mask |= 0xFFull << shift;
+    thr.prefix |= d << lo;
+    thr.mask |= dmask;
     __syncthreads();
     if (cnt == remaining) break;
   }
   return thr;
 }
 
-// Stable compaction of the selected items in item order: emit(pos, i, key, idx) is called once
-// per selected item with consecutive positions starting at 0.  Returns the number emitted.
-// Warps own contiguous item ranges, so output order equals item order.
+// Stable compaction of the selected items in item order: emit(pos, i, c) is called once per
+// selected item with consecutive positions from 0.  Returns the number emitted.  Warps own
+// contiguous item ranges, so output order equals item order.
 template <class ItemFn, class EmitFn>
 __device__ int cta_compact(const ItemFn& item, int n, const SelectThreshold& thr, const EmitFn& emit, int* scratch) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
@@ -112,15 +112,9 @@ __device__ int cta_compact(const ItemFn& item, int n, const SelectThreshold& thr
   int cnt = 0;
   for (int base = lo; base < hi; base += 32) {
     const int i = base + lane;
-    bool sel = false;
-    if (i < hi) {
-      uint32_t key, idx;
-      item(i, key, idx);
-      sel = is_selected(thr, key, idx);
-    }
+    const bool sel = (i < hi) && is_selected(thr, item(i));
     cnt += __popc(__ballot_sync(0xFFFFFFFFu, sel));
   }
-  // exclusive scan over warps
   if (lane == 0) scratch[warp] = cnt;
   __syncthreads();
   if (warp == 0) {
@@ -135,14 +129,14 @@ __device__ int cta_compact(const ItemFn& item, int n, const SelectThreshold& thr
   const unsigned lt = (1u << lane) - 1u;
   for (int base = lo; base < hi; base += 32) {
     const int i = base + lane;
+    unsigned long long c = 0ull;
     bool sel = false;
-    uint32_t key = 0, idx = 0;
     if (i < hi) {
-      item(i, key, idx);
-      sel = is_selected(thr, key, idx);
+      c = item(i);
+      sel = is_selected(thr, c);
     }
     const unsigned b = __ballot_sync(0xFFFFFFFFu, sel);
-    if (sel) emit(off + __popc(b & lt), i, key, idx);
+    if (sel) emit(off + __popc(b & lt), i, c);
     off += __popc(b);
   }
   __syncthreads();
@@ -150,7 +144,7 @@ __device__ int cta_compact(const ItemFn& item, int n, const SelectThreshold& thr
 }
 
 // In-place ascending bitonic sort of n <= cap 64-bit keys in shared memory (cap a power of two;
-// entries n..cap-1 are padded with ~0ull by the caller or here).
+// entries n..cap-1 are padded with ~0ull here).
 __device__ __forceinline__ void cta_bitonic_sort_u64(unsigned long long* v, int n, int cap) {
   for (int i = n + threadIdx.x; i < cap; i += blockDim.x) v[i] = ~0ull;
   __syncthreads();

@@ -13,19 +13,21 @@
 //     hist    : one CTA per segment builds a 4096-bin histogram of the top 12 bits of the
 //               ordered ADC key and adds it to the problem's global histogram; the last CTA to
 //               finish (ticket counter, no waiting) finds the boundary bin b* of the shortlist;
-//     collect : one CTA per segment re-reads its codes; keys above b* go straight to the
-//               shortlist, keys in b* go to a candidate buffer;
-//     problem : one CTA per problem selects the missing shortlist entries from the candidate
-//               buffer (exact, canonical), then rescores / selects / verifies as in the fused
-//               schedule.  If the candidate buffer overflowed (huge score ties), it falls back
-//               to an exact streaming select over all keys of the problem.
+//     collect : one CTA per segment re-reads its codes (now in L2); keys above b* go straight
+//               to the shortlist, keys in b* go to an edge buffer sized for the whole range;
+//     problem : one CTA per problem selects the missing shortlist entries from the edge buffer
+//               (exact, canonical; in shared memory when it fits, else streamed from L2), then
+//               rescores / selects / verifies as in the fused schedule.
 //
+// Codes are read four keys per vector load (S bytes per key), four loads in flight per thread.
 // Selection rule everywhere: score descending, key index ascending (see cta_select.cuh).
 // ADC score: ((0 + lut[0][c0]) + lut[1][c1]) + ... in subspace order, then / sqrt(R)
 // (reference sva/ops.py:64-71).  Rank score: tree_dot(k_low, q_low) / sqrt(R)
 // (reference sva/llama.py:286-292).
 #include "cta_select.cuh"
+#include "qlut.cuh"
 #include "sva_internal.h"
+#include "verify.cuh"
 
 namespace sva {
 
@@ -33,9 +35,11 @@ constexpr int kThreads = 512;
 constexpr int kBins = 4096;
 constexpr int kSegKeys = 16384;
 constexpr int kFusedMaxKeys = 32768;
-constexpr int kCandCap = 16384;
+constexpr int kEdgeSmem = 12288;  // edge entries resolved in shared memory
+constexpr int kScanThreads = 256;
+constexpr int kGroupsInFlight = 4;
 
-enum { CTRL_T_HIST = 0, CTRL_T_COLLECT, CTRL_K, CTRL_BSTAR, CTRL_NABOVE, CTRL_NOUT, CTRL_NCAND, CTRL_NVALID, CTRL_WORDS };
+enum { CTRL_T_HIST = 0, CTRL_K, CTRL_BSTAR, CTRL_NABOVE, CTRL_NOUT, CTRL_NEDGE, CTRL_NVALID, CTRL_WORDS = 8 };
 
 struct DecodeSmem {
   int qf, ql, lut, sc, scratch, sl, rk, fin, lg, acc, cache, total;
@@ -72,13 +76,14 @@ struct DecodeParams {
   int b_cap;
   int grid_mode;
   int nseg;
+  int vec_codes;  // codes aligned for 4-key vector loads
   DecodeSmem lay;
   float* ws_qlow;
   float* ws_lut;
   uint32_t* ws_hist;
   uint32_t* ws_ctrl;
   int32_t* ws_part;
-  uint2* ws_cand;
+  uint2* ws_edge;
 };
 
 // ---------------------------------------------------------------------------------------
@@ -101,58 +106,75 @@ __device__ __forceinline__ bool key_allowed(const DecodeParams& p, int t, int64_
   return true;
 }
 
-// Ordered ADC key of key i (0 when not allowed).
+// Ordered ADC key of key i (0 when not allowed), scalar code loads.
 __device__ __forceinline__ uint32_t adc_key(const DecodeParams& p, const uint8_t* __restrict__ codes,
                                             const float* __restrict__ lut, int t, int64_t i, int64_t len_t) {
   if (!key_allowed(p, t, i, len_t)) return 0u;
   const int S = p.a.subspaces, C = p.a.codewords;
   const uint8_t* row = codes + i * S;
   float sum = 0.f;
-  if (S == 4) {
-    const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(row));
-    sum = __fadd_rn(sum, lut[(w & 0xFFu)]);
-    sum = __fadd_rn(sum, lut[C + ((w >> 8) & 0xFFu)]);
-    sum = __fadd_rn(sum, lut[2 * C + ((w >> 16) & 0xFFu)]);
-    sum = __fadd_rn(sum, lut[3 * C + (w >> 24)]);
+  for (int s = 0; s < S; ++s) sum = __fadd_rn(sum, lut[s * C + __ldg(row + s)]);
+  return ordered_key(finish_score(sum, p));
+}
+
+// Codes of four consecutive keys in one vector load (S = 1, 2, 4 or 8 bytes per key).
+template <int S>
+struct Codes4 {
+  uint4 a, b;
+};
+
+template <int S>
+__device__ __forceinline__ Codes4<S> load_codes4(const uint8_t* base, int64_t i) {
+  Codes4<S> r;
+  if (S == 1) {
+    r.a.x = __ldg(reinterpret_cast<const uint32_t*>(base + i));
+  } else if (S == 2) {
+    const uint2 w = __ldg(reinterpret_cast<const uint2*>(base + 2 * i));
+    r.a.x = w.x;
+    r.a.y = w.y;
+  } else if (S == 4) {
+    r.a = __ldg(reinterpret_cast<const uint4*>(base + 4 * i));
   } else {
-    for (int s = 0; s < S; ++s) sum = __fadd_rn(sum, lut[s * C + __ldg(row + s)]);
+    r.a = __ldg(reinterpret_cast<const uint4*>(base + 8 * i));
+    r.b = __ldg(reinterpret_cast<const uint4*>(base + 8 * i + 16));
   }
+  return r;
+}
+
+// Code of key j (0..3) in subspace s.
+template <int S>
+__device__ __forceinline__ uint32_t code_at(const Codes4<S>& c, int j, int s) {
+  if (S == 1) return (c.a.x >> (8 * j)) & 0xFFu;
+  if (S == 2) {
+    const uint32_t w = (j < 2) ? c.a.x : c.a.y;
+    return (w >> (16 * (j & 1) + 8 * s)) & 0xFFu;
+  }
+  if (S == 4) {
+    const uint32_t w = (j == 0) ? c.a.x : (j == 1) ? c.a.y : (j == 2) ? c.a.z : c.a.w;
+    return (w >> (8 * s)) & 0xFFu;
+  }
+  const uint4& v = (j < 2) ? c.a : c.b;
+  const uint32_t w = ((j & 1) == 0) ? (s < 4 ? v.x : v.y) : (s < 4 ? v.z : v.w);
+  return (w >> (8 * (s & 3))) & 0xFFu;
+}
+
+template <int S>
+__device__ __forceinline__ uint32_t adc_key4(const DecodeParams& p, const Codes4<S>& c, int j,
+                                             const float* __restrict__ lut) {
+  const int C = p.a.codewords;
+  float sum = 0.f;
+#pragma unroll
+  for (int s = 0; s < S; ++s) sum = __fadd_rn(sum, lut[s * C + code_at<S>(c, j, s)]);
   return ordered_key(finish_score(sum, p));
 }
 
 template <typename T>
-__device__ void build_qlut(const DecodeParams& p, int h, int t, float* qf, float* ql, float* lut) {
-  const int D = p.a.head_dim, R = p.a.rank_dim, S = p.a.subspaces, C = p.a.codewords, sub = p.sub;
+__device__ void build_qlut(const DecodeParams& p, int h, int t, float* qf, float* ql, float* lut, float* stage) {
+  const int D = p.a.head_dim, R = p.a.rank_dim, S = p.a.subspaces, C = p.a.codewords;
   const T* q = reinterpret_cast<const T*>(p.a.query) + h * p.a.q_head_stride + t * p.a.q_row_stride;
-  for (int d = threadIdx.x; d < D; d += blockDim.x) qf[d] = to_f32<T>(q[d]);
-  __syncthreads();
-  for (int r = threadIdx.x; r < R; r += blockDim.x) {
-    const float* P = p.a.q_proj + (size_t)h * D * R + r;
-    float acc = 0.f;
-    for (int d = 0; d < D; ++d) acc = mac(acc, qf[d], __ldg(P + (size_t)d * R));
-    ql[r] = __fmul_rn(acc, __ldg(p.a.scale + h));
-  }
-  __syncthreads();
-  const int SC = S * C;
-  if (p.a.lut_override) {
-    const float* lo = p.a.lut_override + ((size_t)h * p.a.n_queries + t) * SC;
-    for (int e = threadIdx.x; e < SC; e += blockDim.x) lut[e] = lo[e];
-  } else {
-    for (int e = threadIdx.x; e < SC; e += blockDim.x) {
-      const int s = e / C;
-      const float* cb = p.a.codebooks + (((size_t)h * S + s) * C + (e - s * C)) * sub;
-      const float* qs = ql + s * sub;
-      float acc = 0.f;
-      for (int j = 0; j < sub; ++j) acc = mac(acc, qs[j], __ldg(cb + j));
-      lut[e] = acc;
-    }
-  }
-  __syncthreads();
-}
-
-template <typename T>
-__device__ __forceinline__ const T* kv_row(const void* base, int64_t head_stride, int64_t row_stride, int kvh, int64_t i) {
-  return reinterpret_cast<const T*>(base) + kvh * head_stride + i * row_stride;
+  const float* lo = p.a.lut_override ? p.a.lut_override + ((size_t)h * p.a.n_queries + t) * S * C : nullptr;
+  build_query_lut<T>(q, D, R, S, C, p.a.q_proj + (size_t)h * D * R, __ldg(p.a.scale + h),
+                     p.a.codebooks + (size_t)h * S * C * (R / S), lo, qf, ql, lut, stage);
 }
 
 // Block-wide sum of an int (all threads get the result).
@@ -190,11 +212,10 @@ __global__ void __launch_bounds__(kThreads) decode_problem_kernel(const DecodePa
   const int R = p.a.rank_dim, D = p.a.head_dim;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
 
-  build_qlut<T>(p, h, t, qf, ql, lut);
-
   // ---- shortlist -------------------------------------------------------------------------
   int n_sl = 0;
   if (!p.grid_mode) {
+    build_qlut<T>(p, h, t, qf, ql, lut, reinterpret_cast<float*>(smem + p.lay.cache));
     uint32_t* cache = reinterpret_cast<uint32_t*>(smem + p.lay.cache);
     int nv = 0;
     for (int64_t i = tid; i < L; i += blockDim.x) {
@@ -204,54 +225,55 @@ __global__ void __launch_bounds__(kThreads) decode_problem_kernel(const DecodePa
     }
     const int n_valid = block_sum_int(nv, scratch);
     const int k = min(p.sl_cap, n_valid);
-    auto item = [&](int i, uint32_t& key, uint32_t& idx) {
-      key = cache[i];
-      idx = static_cast<uint32_t>(i);
+    auto item = [&](int i) -> unsigned long long {
+      return cache[i] ? composite(cache[i], static_cast<uint32_t>(i)) : 0ull;
     };
     const SelectThreshold thr = cta_radix_select(item, static_cast<int>(L), k, sc);
-    n_sl = cta_compact(item, static_cast<int>(L), thr,
-                       [&](int pos, int i, uint32_t, uint32_t) { sl[pos] = i; }, scratch);
+    n_sl = cta_compact(item, static_cast<int>(L), thr, [&](int pos, int i, unsigned long long) { sl[pos] = i; },
+                       scratch);
   } else {
+    const T* q = reinterpret_cast<const T*>(p.a.query) + h * p.a.q_head_stride + t * p.a.q_row_stride;
+    for (int d = tid; d < D; d += blockDim.x) qf[d] = to_f32<T>(q[d]);
+    for (int r = tid; r < R; r += blockDim.x) ql[r] = __ldcg(p.ws_qlow + (size_t)prob * kMaxRank + r);
     const uint32_t* ctrl = p.ws_ctrl + (size_t)prob * CTRL_WORDS;
     const int k = static_cast<int>(__ldcg(ctrl + CTRL_K));
-    const int n_part = static_cast<int>(__ldcg(ctrl + CTRL_NOUT));
-    const int n_cand = static_cast<int>(__ldcg(ctrl + CTRL_NCAND));
+    const int n_part = min(static_cast<int>(__ldcg(ctrl + CTRL_NOUT)), k);
+    const int64_t n_edge64 = __ldcg(ctrl + CTRL_NEDGE);
+    const int n_edge = static_cast<int>(n_edge64 < L ? n_edge64 : L);
     const int32_t* part = p.ws_part + (size_t)prob * p.sl_cap;
-    if (n_cand <= kCandCap && n_part <= k) {
-      for (int i = tid; i < n_part; i += blockDim.x) sl[i] = __ldcg(part + i);
-      uint2* cand = reinterpret_cast<uint2*>(smem + p.lay.cache);
-      const uint2* gc = p.ws_cand + (size_t)prob * kCandCap;
-      for (int i = tid; i < n_cand; i += blockDim.x) cand[i] = __ldcg(gc + i);
+    for (int i = tid; i < n_part; i += blockDim.x) sl[i] = __ldcg(part + i);
+    const uint2* ge = p.ws_edge + (size_t)prob * L;
+    // edge entries share the top 12 key bits: order them by the low 20 key bits, then index
+    auto local = [](uint2 v) -> unsigned long long {
+      return (static_cast<unsigned long long>(v.x & 0xFFFFFu) << 44) |
+             (static_cast<unsigned long long>(~v.y) << 12) | 1ull;
+    };
+    const int need = k - n_part;
+    if (n_edge <= kEdgeSmem) {
+      uint2* edge = reinterpret_cast<uint2*>(smem + p.lay.cache);
+      for (int i = tid; i < n_edge; i += blockDim.x) edge[i] = __ldcg(ge + i);
       __syncthreads();
-      auto item = [&](int i, uint32_t& key, uint32_t& idx) {
-        key = cand[i].x;
-        idx = cand[i].y;
-      };
-      const SelectThreshold thr = cta_radix_select(item, n_cand, k - n_part, sc);
-      const int got = cta_compact(item, n_cand, thr,
-                                  [&](int pos, int, uint32_t, uint32_t idx) { sl[n_part + pos] = static_cast<int32_t>(idx); },
-                                  scratch);
-      n_sl = n_part + got;
+      auto item = [&](int i) -> unsigned long long { return local(edge[i]); };
+      const SelectThreshold thr = cta_radix_select(item, n_edge, need, sc);
+      cta_compact(item, n_edge, thr, [&](int pos, int i, unsigned long long) { sl[n_part + pos] = edge[i].y; },
+                  scratch);
     } else {
-      // Exact streaming select over every key of the problem (candidate buffer overflow).
-      auto item = [&](int i, uint32_t& key, uint32_t& idx) {
-        key = adc_key(p, codes, lut, t, i, len_t);
-        idx = static_cast<uint32_t>(i);
-      };
-      const SelectThreshold thr = cta_radix_select(item, static_cast<int>(L), k, sc);
-      n_sl = cta_compact(item, static_cast<int>(L), thr,
-                         [&](int pos, int i, uint32_t, uint32_t) { sl[pos] = i; }, scratch);
+      auto item = [&](int i) -> unsigned long long { return local(__ldcg(ge + i)); };
+      const SelectThreshold thr = cta_radix_select(item, n_edge, need, sc);
+      cta_compact(item, n_edge, thr,
+                  [&](int pos, int i, unsigned long long) { sl[n_part + pos] = __ldcg(ge + i).y; }, scratch);
     }
+    n_sl = k;
   }
   __syncthreads();
 
-  // ---- rank rescore: two rows per warp step (one per half-warp), 4 steps in flight ---------
+  // ---- rank rescore: two rows per warp step (one per half-warp), 16 steps in flight -------
   {
     const int half = lane >> 4, l16 = lane & 15;
     const float4 q4 = (4 * l16 < R) ? make_float4(ql[4 * l16], ql[4 * l16 + 1], ql[4 * l16 + 2], ql[4 * l16 + 3])
                                     : make_float4(0.f, 0.f, 0.f, 0.f);
     const float* klb = p.a.k_low + h * p.a.k_low_head_stride;
-    constexpr int U = 4;
+    constexpr int U = 16;
     for (int base = warp * 2 * U; base < n_sl; base += nwarps * 2 * U) {
       float4 r[U];
 #pragma unroll
@@ -274,138 +296,15 @@ __global__ void __launch_bounds__(kThreads) decode_problem_kernel(const DecodePa
   const int b = min(p.b_cap, n_sl);
   int n_fin;
   {
-    auto item = [&](int j, uint32_t& key, uint32_t& idx) {
-      key = rk[j];
-      idx = static_cast<uint32_t>(sl[j]);
-    };
+    auto item = [&](int j) -> unsigned long long { return composite(rk[j], static_cast<uint32_t>(sl[j])); };
     const SelectThreshold thr = cta_radix_select(item, n_sl, b, sc);
-    n_fin = cta_compact(item, n_sl, thr,
-                        [&](int pos, int, uint32_t, uint32_t idx) { fin[pos] = static_cast<int32_t>(idx); }, scratch);
+    n_fin = cta_compact(item, n_sl, thr, [&](int pos, int j, unsigned long long) { fin[pos] = sl[j]; }, scratch);
   }
 
-  // ---- verify: logits -------------------------------------------------------------------
-  {
-    const int half = lane >> 4, l16 = lane & 15;
-    constexpr int U = 4;
-    for (int base = warp * 2 * U; base < n_fin; base += nwarps * 2 * U) {
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int j = base + 2 * u + half;
-        const bool ok = j < n_fin;
-        const T* krow = ok ? kv_row<T>(p.a.keys, p.a.k_head_stride, p.a.k_row_stride, kvh, fin[j]) : nullptr;
-        float part = 0.f;
-        for (int c0 = 0; c0 < D; c0 += 64) {
-          const int e = c0 + 4 * l16;
-          if (!ok || e >= D) continue;
-          const float4 k4 = load4<T>(krow, e, D);
-          const float4 qv = make_float4(qf[e], (e + 1 < D) ? qf[e + 1] : 0.f, (e + 2 < D) ? qf[e + 2] : 0.f,
-                                        (e + 3 < D) ? qf[e + 3] : 0.f);
-          if (p.a.logits_mode == 1) {
-            float s = round_to<T>(__fmul_rn(k4.x, qv.x));
-            s = __fadd_rn(s, round_to<T>(__fmul_rn(k4.y, qv.y)));
-            s = __fadd_rn(s, round_to<T>(__fmul_rn(k4.z, qv.z)));
-            s = __fadd_rn(s, round_to<T>(__fmul_rn(k4.w, qv.w)));
-            part = __fadd_rn(part, s);
-          } else {
-            part = __fadd_rn(part, lane4(k4, qv));
-          }
-        }
-        float s = tree16(part);
-        if (p.a.logits_mode == 1) {
-          s = round_to<T>(s);
-          s = round_to<T>(__fmul_rn(s, p.a.softmax_scale));
-        } else {
-          s = __fmul_rn(s, p.a.softmax_scale);
-        }
-        if (ok && l16 == 0) lg[j] = s;
-      }
-    }
-  }
-  __syncthreads();
-
-  // ---- softmax (fp32 max, fp64 denominator) -------------------------------------------------
-  float mx = -INFINITY;
-  for (int j = tid; j < n_fin; j += blockDim.x) mx = fmaxf(mx, lg[j]);
-  mx = warp_max(mx);
-  float* redf = reinterpret_cast<float*>(scratch);
-  if (lane == 0) redf[warp] = mx;
-  __syncthreads();
-  if (tid < 32) {
-    float v = (tid < nwarps) ? redf[tid] : -INFINITY;
-    v = warp_max(v);
-    if (tid == 0) redf[32] = v;
-  }
-  __syncthreads();
-  mx = redf[32];
-  double se = 0.0;
-  for (int j = tid; j < n_fin; j += blockDim.x) se += static_cast<double>(expf(lg[j] - mx));
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) se += __shfl_xor_sync(0xFFFFFFFFu, se, o);
-  if (lane == 0) acc[warp] = se;
-  __syncthreads();
-  if (tid == 0) {
-    double tot = 0.0;
-    for (int w = 0; w < nwarps; ++w) tot += acc[w];
-    acc[nwarps] = tot;
-  }
-  __syncthreads();
-  const float denom = static_cast<float>(acc[nwarps]);
-  __syncthreads();
-  for (int j = tid; j < n_fin; j += blockDim.x) lg[j] = round_to<T>(expf(lg[j] - mx) / denom);
-  __syncthreads();
-
-  // ---- aggregate: half-warp per row, lane owns 4 dims per 64-wide chunk; fp64 sums ----------
-  {
-    const int half = lane >> 4, l16 = lane & 15;
-    const int nchunks = (D + 63) / 64;
-    for (int c = 0; c < nchunks; ++c) {
-      const int e = c * 64 + 4 * l16;
-      double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
-      constexpr int U = 4;
-      for (int base = warp * 2 * U; base < n_fin; base += nwarps * 2 * U) {
-        float4 v[U];
-        float w[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const int j = base + 2 * u + half;
-          v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-          w[u] = 0.f;
-          if (j < n_fin && e < D) {
-            v[u] = load4<T>(kv_row<T>(p.a.values, p.a.v_head_stride, p.a.v_row_stride, kvh, fin[j]), e, D);
-            w[u] = lg[j];
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-          a0 += static_cast<double>(round_to<T>(__fmul_rn(w[u], v[u].x)));
-          a1 += static_cast<double>(round_to<T>(__fmul_rn(w[u], v[u].y)));
-          a2 += static_cast<double>(round_to<T>(__fmul_rn(w[u], v[u].z)));
-          a3 += static_cast<double>(round_to<T>(__fmul_rn(w[u], v[u].w)));
-        }
-      }
-      // combine the two half-warps, then the warps
-      a0 += __shfl_xor_sync(0xFFFFFFFFu, a0, 16);
-      a1 += __shfl_xor_sync(0xFFFFFFFFu, a1, 16);
-      a2 += __shfl_xor_sync(0xFFFFFFFFu, a2, 16);
-      a3 += __shfl_xor_sync(0xFFFFFFFFu, a3, 16);
-      double* wacc = acc;  // [nwarps][64]
-      __syncthreads();
-      if (half == 0) {
-        wacc[warp * 64 + 4 * l16 + 0] = a0;
-        wacc[warp * 64 + 4 * l16 + 1] = a1;
-        wacc[warp * 64 + 4 * l16 + 2] = a2;
-        wacc[warp * 64 + 4 * l16 + 3] = a3;
-      }
-      __syncthreads();
-      if (tid < 64 && c * 64 + tid < D) {
-        double tot = 0.0;
-        for (int w2 = 0; w2 < nwarps; ++w2) tot += wacc[w2 * 64 + tid];
-        T* out = reinterpret_cast<T*>(p.a.out) + h * p.a.out_head_stride + t * p.a.out_row_stride;
-        out[c * 64 + tid] = from_f32<T>(n_fin > 0 ? static_cast<float>(tot) : 0.f);
-      }
-      __syncthreads();
-    }
-  }
+  // ---- verify ----------------------------------------------------------------------------
+  verify_rows<T>(p.a.keys, p.a.k_head_stride, p.a.k_row_stride, p.a.values, p.a.v_head_stride, p.a.v_row_stride, kvh,
+                 qf, D, fin, n_fin, p.a.softmax_scale, p.a.logits_mode, lg, acc, scratch,
+                 reinterpret_cast<T*>(p.a.out) + h * p.a.out_head_stride + t * p.a.out_row_stride);
 
   // ---- debug outputs and counters -------------------------------------------------------
   if (p.a.shortlist_out || p.a.final_out) {
@@ -445,12 +344,13 @@ __global__ void __launch_bounds__(kThreads) decode_problem_kernel(const DecodePa
 
 template <typename T>
 __global__ void __launch_bounds__(256) decode_qlut_kernel(const DecodeParams p) {
+  extern __shared__ __align__(16) float stage[];
   __shared__ float qf[kMaxHeadDim];
   __shared__ float ql[kMaxRank];
   __shared__ float lut[kMaxLut];
   const int prob = blockIdx.x;
   const int h = prob / p.a.n_queries, t = prob - h * p.a.n_queries;
-  build_qlut<T>(p, h, t, qf, ql, lut);
+  build_qlut<T>(p, h, t, qf, ql, lut, stage);
   const int SC = p.a.subspaces * p.a.codewords;
   float* gl = p.ws_lut + (size_t)prob * kMaxLut;
   for (int e = threadIdx.x; e < SC; e += blockDim.x) gl[e] = lut[e];
@@ -460,12 +360,59 @@ __global__ void __launch_bounds__(256) decode_qlut_kernel(const DecodeParams p) 
   if (threadIdx.x < CTRL_WORDS) p.ws_ctrl[(size_t)prob * CTRL_WORDS + threadIdx.x] = 0u;
 }
 
-__global__ void __launch_bounds__(256) decode_hist_kernel(const DecodeParams p) {
+// Calls f(i, key) for every key of [i0, i1) (key = 0 when not allowed).  With S > 0 each
+// thread handles groups of four consecutive keys, kGroupsInFlight vector loads at a time.
+// Iteration is warp-uniform: every lane calls f the same number of times (slots past the end
+// come with i == i1 and key 0), so f may use warp collectives.
+template <int S, class F>
+__device__ __forceinline__ void scan_segment(const DecodeParams& p, const uint8_t* codes, const float* lut, int t,
+                                             int64_t len_t, int64_t i0, int64_t i1, const F& f) {
+  const int lane = threadIdx.x & 31;
+  if constexpr (S > 0) {
+    const int64_t ngroups = (i1 - i0 + 3) >> 2;
+    const bool dense = (p.a.allowed_mask == nullptr) && (i1 <= len_t);
+    for (int64_t gb = (threadIdx.x & ~31); gb < ngroups; gb += (int64_t)blockDim.x * kGroupsInFlight) {
+      Codes4<S> c[kGroupsInFlight];
+#pragma unroll
+      for (int u = 0; u < kGroupsInFlight; ++u) {
+        const int64_t g = gb + lane + (int64_t)u * blockDim.x;
+        if (g < ngroups && i0 + 4 * g + 3 < i1) c[u] = load_codes4<S>(codes, i0 + 4 * g);
+      }
+#pragma unroll
+      for (int u = 0; u < kGroupsInFlight; ++u) {
+        const int64_t g = gb + lane + (int64_t)u * blockDim.x;
+        const int64_t ib = i0 + 4 * g;
+        const bool full = g < ngroups && ib + 3 < i1;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int64_t i = ib + j;
+          const bool live = g < ngroups && i < i1;
+          uint32_t key = 0u;
+          if (full) {
+            key = (dense || key_allowed(p, t, i, len_t)) ? adc_key4<S>(p, c[u], j, lut) : 0u;
+          } else if (live) {
+            key = adc_key(p, codes, lut, t, i, len_t);
+          }
+          f(live ? i : i1, key);
+        }
+      }
+    }
+  } else {
+    for (int64_t wb = i0 + (threadIdx.x & ~31); wb < i1; wb += blockDim.x) {
+      const int64_t i = wb + lane;
+      const uint32_t key = (i < i1) ? adc_key(p, codes, lut, t, i, len_t) : 0u;
+      f(i < i1 ? i : i1, key);
+    }
+  }
+}
+
+template <int S>
+__global__ void __launch_bounds__(kScanThreads) decode_hist_kernel(const DecodeParams p) {
   __shared__ float lut[kMaxLut];
   __shared__ uint32_t hist[kBins];
   __shared__ int is_last;
-  __shared__ int wsum[9];
-  __shared__ int boundary[3];
+  __shared__ int wsum[kScanThreads / 32];
+  __shared__ int boundary[2];
   const int prob = blockIdx.y, seg = blockIdx.x;
   const int h = prob / p.a.n_queries, t = prob - h * p.a.n_queries;
   const int SC = p.a.subspaces * p.a.codewords;
@@ -476,10 +423,9 @@ __global__ void __launch_bounds__(256) decode_hist_kernel(const DecodeParams p) 
   const uint8_t* codes = p.a.codes + h * p.a.codes_head_stride;
   const int64_t i0 = (int64_t)seg * kSegKeys;
   const int64_t i1 = min(p.a.key_len, i0 + kSegKeys);
-  for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
-    const uint32_t key = adc_key(p, codes, lut, t, i, len_t);
+  scan_segment<S>(p, codes, lut, t, len_t, i0, i1, [&](int64_t, uint32_t key) {
     if (key) atomicAdd(&hist[key >> 20], 1u);
-  }
+  });
   __syncthreads();
   uint32_t* gh = p.ws_hist + (size_t)prob * kBins;
   for (int b = threadIdx.x; b < kBins; b += blockDim.x)
@@ -503,9 +449,13 @@ __global__ void __launch_bounds__(256) decode_hist_kernel(const DecodeParams p) 
   }
   int incl = warp_incl_scan(s);
   if (lane == 31) wsum[tid >> 5] = incl;
+  if (tid == 0) {
+    boundary[0] = kBins;  // no key qualifies unless overwritten below
+    boundary[1] = 0;
+  }
   __syncthreads();
   int base = 0, total = 0;
-  for (int w = 0; w < 8; ++w) {
+  for (int w = 0; w < kScanThreads / 32; ++w) {
     if (w < (tid >> 5)) base += wsum[w];
     total += wsum[w];
   }
@@ -524,10 +474,6 @@ __global__ void __launch_bounds__(256) decode_hist_kernel(const DecodeParams p) 
       run += v;
     }
   }
-  if (tid == 0 && k == 0) {
-    boundary[0] = kBins;  // no key qualifies
-    boundary[1] = 0;
-  }
   __syncthreads();
   if (tid == 0) {
     ctrl[CTRL_K] = static_cast<uint32_t>(k);
@@ -537,7 +483,8 @@ __global__ void __launch_bounds__(256) decode_hist_kernel(const DecodeParams p) 
   }
 }
 
-__global__ void __launch_bounds__(256) decode_collect_kernel(const DecodeParams p) {
+template <int S>
+__global__ void __launch_bounds__(kScanThreads) decode_collect_kernel(const DecodeParams p) {
   __shared__ float lut[kMaxLut];
   const int prob = blockIdx.y, seg = blockIdx.x;
   const int h = prob / p.a.n_queries, t = prob - h * p.a.n_queries;
@@ -552,23 +499,20 @@ __global__ void __launch_bounds__(256) decode_collect_kernel(const DecodeParams 
   const int64_t i0 = (int64_t)seg * kSegKeys;
   const int64_t i1 = min(p.a.key_len, i0 + kSegKeys);
   int32_t* part = p.ws_part + (size_t)prob * p.sl_cap;
-  uint2* cand = p.ws_cand + (size_t)prob * kCandCap;
+  uint2* edge = p.ws_edge + (size_t)prob * p.a.key_len;
   const int lane = threadIdx.x & 31;
   const unsigned lt = (1u << lane) - 1u;
-  // warp-uniform loop so the ballots below see all 32 lanes
-  for (int64_t wb = i0 + (threadIdx.x & ~31); wb < i1; wb += blockDim.x) {
-    const int64_t i = wb + lane;
-    uint32_t key = 0u;
-    if (i < i1) key = adc_key(p, codes, lut, t, i, len_t);
+  scan_segment<S>(p, codes, lut, t, len_t, i0, i1, [&](int64_t i, uint32_t key) {
     const uint32_t bin = key >> 20;
     const bool above = key != 0u && bin > bstar;
-    const bool edge = key != 0u && bin == bstar;
+    const bool on = key != 0u && bin == bstar;
     const unsigned ba = __ballot_sync(0xFFFFFFFFu, above);
-    const unsigned be = __ballot_sync(0xFFFFFFFFu, edge);
+    const unsigned be = __ballot_sync(0xFFFFFFFFu, on);
+    if ((ba | be) == 0u) return;
     uint32_t pa = 0, pe = 0;
     if (lane == 0) {
       if (ba) pa = atomicAdd(ctrl + CTRL_NOUT, static_cast<uint32_t>(__popc(ba)));
-      if (be) pe = atomicAdd(ctrl + CTRL_NCAND, static_cast<uint32_t>(__popc(be)));
+      if (be) pe = atomicAdd(ctrl + CTRL_NEDGE, static_cast<uint32_t>(__popc(be)));
     }
     pa = __shfl_sync(0xFFFFFFFFu, pa, 0);
     pe = __shfl_sync(0xFFFFFFFFu, pe, 0);
@@ -576,11 +520,11 @@ __global__ void __launch_bounds__(256) decode_collect_kernel(const DecodeParams 
       const uint32_t pos = pa + __popc(ba & lt);
       if (pos < static_cast<uint32_t>(p.sl_cap)) part[pos] = static_cast<int32_t>(i);
     }
-    if (edge) {
+    if (on) {
       const uint32_t pos = pe + __popc(be & lt);
-      if (pos < static_cast<uint32_t>(kCandCap)) cand[pos] = make_uint2(key, static_cast<uint32_t>(i));
+      if (static_cast<int64_t>(pos) < p.a.key_len) edge[pos] = make_uint2(key, static_cast<uint32_t>(i));
     }
-  }
+  });
 }
 
 // ---------------------------------------------------------------------------------------
@@ -617,8 +561,6 @@ static int plan_decode(const sva_decode_args* a, DecodePlan* plan) {
   if (a->qkv_dtype < 0 || a->qkv_dtype > 2) return set_error(SVA_ERR_DTYPE, "qkv_dtype must be 0 (f32), 1 (bf16) or 2 (f16)");
   if (!a->query || !a->q_proj || !a->scale || !a->codebooks || !a->codes || !a->k_low || !a->keys || !a->values || !a->out)
     return set_error(SVA_ERR_SHAPE, "a required pointer is null");
-  if (a->subspaces == 4 && ((reinterpret_cast<uintptr_t>(a->codes) & 3u) || (a->codes_head_stride & 3)))
-    return set_error(SVA_ERR_ALIGN, "codes must be 4-byte aligned when subspaces == 4");
   DecodeParams& p = plan->p;
   memset(&p, 0, sizeof(p));
   p.a = *a;
@@ -630,15 +572,18 @@ static int plan_decode(const sva_decode_args* a, DecodePlan* plan) {
   p.inv_sqrt_r = 1.0f / p.sqrt_r;
   p.sl_cap = static_cast<int>(std::min<int64_t>(a->shortlist, a->key_len));
   p.b_cap = std::min(a->budget, p.sl_cap);
+  const int S = a->subspaces;
+  const bool vec_s = (S == 1 || S == 2 || S == 4 || S == 8);
+  const uintptr_t align = static_cast<uintptr_t>(4 * S);
+  p.vec_codes = (vec_s && (reinterpret_cast<uintptr_t>(a->codes) % align == 0) &&
+                 (a->codes_head_stride % (4 * S)) == 0)
+                    ? 1
+                    : 0;
   const int64_t P = static_cast<int64_t>(a->n_heads) * a->n_queries;
   p.grid_mode = a->key_len > kFusedMaxKeys ? 1 : 0;
   p.nseg = static_cast<int>((a->key_len + kSegKeys - 1) / kSegKeys);
-  int cache_bytes;
-  if (!p.grid_mode) {
-    cache_bytes = static_cast<int>(4 * a->key_len);
-  } else {
-    cache_bytes = 8 * kCandCap;
-  }
+  const int stage_bytes = 4 * a->head_dim * a->rank_dim;
+  int cache_bytes = p.grid_mode ? 8 * kEdgeSmem : std::max<int>(static_cast<int>(4 * a->key_len), stage_bytes);
   // debug outputs reuse the cache region for a 64-bit sort of up to pow2(shortlist) entries
   if (a->shortlist_out || a->final_out) {
     int cap = 1;
@@ -647,7 +592,7 @@ static int plan_decode(const sva_decode_args* a, DecodePlan* plan) {
   }
   p.lay = decode_smem_layout(a->head_dim, p.sl_cap, p.b_cap, cache_bytes);
   plan->smem_bytes = static_cast<size_t>(p.lay.total);
-  if (plan->smem_bytes > 227 * 1024) return set_error(SVA_ERR_SHAPE, "shared memory plan exceeds 227 KB");
+  if (plan->smem_bytes > static_cast<size_t>(kMaxDynSmem)) return set_error(SVA_ERR_SHAPE, "shared memory plan exceeds 227 KB");
   size_t ws = 0;
   if (p.grid_mode) {
     auto take = [&](size_t bytes) {
@@ -660,16 +605,25 @@ static int plan_decode(const sva_decode_args* a, DecodePlan* plan) {
     const size_t o_hist = take(sizeof(uint32_t) * kBins * P);
     const size_t o_ctrl = take(sizeof(uint32_t) * CTRL_WORDS * P);
     const size_t o_part = take(sizeof(int32_t) * p.sl_cap * P);
-    const size_t o_cand = take(sizeof(uint2) * kCandCap * P);
+    const size_t o_edge = take(sizeof(uint2) * static_cast<size_t>(a->key_len) * P);
     p.ws_qlow = reinterpret_cast<float*>(o_ql);
     p.ws_lut = reinterpret_cast<float*>(o_lut);
     p.ws_hist = reinterpret_cast<uint32_t*>(o_hist);
     p.ws_ctrl = reinterpret_cast<uint32_t*>(o_ctrl);
     p.ws_part = reinterpret_cast<int32_t*>(o_part);
-    p.ws_cand = reinterpret_cast<uint2*>(o_cand);
+    p.ws_edge = reinterpret_cast<uint2*>(o_edge);
   }
   plan->ws_bytes = ws;
   return SVA_OK;
+}
+
+template <int S>
+static void launch_scan_kernels(const DecodeParams& p, int P, cudaStream_t stream) {
+  dim3 grid(p.nseg, P);
+  decode_hist_kernel<S><<<grid, kScanThreads, 0, stream>>>(p);
+  profile_mark(1, stream);
+  decode_collect_kernel<S><<<grid, kScanThreads, 0, stream>>>(p);
+  profile_mark(2, stream);
 }
 
 template <typename T>
@@ -683,14 +637,19 @@ static int launch_decode(DecodePlan& plan, void* ws, cudaStream_t stream) {
     p.ws_hist = reinterpret_cast<uint32_t*>(base + reinterpret_cast<size_t>(p.ws_hist));
     p.ws_ctrl = reinterpret_cast<uint32_t*>(base + reinterpret_cast<size_t>(p.ws_ctrl));
     p.ws_part = reinterpret_cast<int32_t*>(base + reinterpret_cast<size_t>(p.ws_part));
-    p.ws_cand = reinterpret_cast<uint2*>(base + reinterpret_cast<size_t>(p.ws_cand));
-    decode_qlut_kernel<T><<<P, 256, 0, stream>>>(p);
+    p.ws_edge = reinterpret_cast<uint2*>(base + reinterpret_cast<size_t>(p.ws_edge));
+    const int stage = 4 * p.a.head_dim * p.a.rank_dim;
+    int rc = ensure_smem_attr(reinterpret_cast<const void*>(decode_qlut_kernel<T>), kMaxDynSmem - 16 * 1024);
+    if (rc != SVA_OK) return rc;
+    decode_qlut_kernel<T><<<P, 256, stage, stream>>>(p);
     profile_mark(0, stream);
-    dim3 grid(p.nseg, P);
-    decode_hist_kernel<<<grid, 256, 0, stream>>>(p);
-    profile_mark(1, stream);
-    decode_collect_kernel<<<grid, 256, 0, stream>>>(p);
-    profile_mark(2, stream);
+    switch (p.vec_codes ? p.a.subspaces : 0) {
+      case 1: launch_scan_kernels<1>(p, P, stream); break;
+      case 2: launch_scan_kernels<2>(p, P, stream); break;
+      case 4: launch_scan_kernels<4>(p, P, stream); break;
+      case 8: launch_scan_kernels<8>(p, P, stream); break;
+      default: launch_scan_kernels<0>(p, P, stream); break;
+    }
   }
   int rc = ensure_smem_attr(reinterpret_cast<const void*>(decode_problem_kernel<T>), kMaxDynSmem);
   if (rc != SVA_OK) return rc;

@@ -1,0 +1,173 @@
+// Posting lists of the static inverted index (replaces sva/llama.py:626-657, _rebuild_postings).
+//
+// For every (head h, subspace s) the keys [0, L) are grouped by their code into CSR posting
+// lists: counts[h][s][c], offsets[h][s][c] (offsets[..][C] = L) and ids[h][s][offsets..] with key
+// ids ascending inside each cell (a stable counting sort, so the layout is deterministic).  The
+// reference stores the same lists padded to the largest bucket; it also needs that largest
+// bucket size, which is written to *max_bucket (a device int).
+//
+// Three passes over the codes, no atomics on the ids:
+//   1. per chunk of kChunk keys: histogram of codes -> chunk_hist[hs][chunk][c]
+//   2. per (h, s): counts, offsets, and the base of every (chunk, c) run (in place)
+//   3. per chunk: stable scatter; within a round of 256 keys the rank of a key among same-code
+//      keys comes from a warp match plus per-warp counters, so ids keep key order.
+#include "sva_common.cuh"
+#include "sva_internal.h"
+
+namespace sva {
+
+constexpr int kPostChunk = 4096;
+constexpr int kPostThreads = 256;
+
+struct PostParams {
+  const uint8_t* codes;
+  int64_t codes_head_stride;
+  int H, S, C;
+  int64_t L;
+  int nchunks;
+  int32_t* counts;   // [H][S][C]
+  int32_t* offsets;  // [H][S][C+1]
+  int32_t* ids;      // [H][S][ids_sub_stride]
+  int64_t ids_sub_stride;
+  int32_t* max_bucket;
+  int32_t* chunk_hist;  // [H*S][nchunks][C]
+};
+
+__global__ void __launch_bounds__(kPostThreads) post_hist_kernel(const PostParams p) {
+  __shared__ int hist[kMaxCodewords];
+  const int hs = blockIdx.y, chunk = blockIdx.x;
+  const int h = hs / p.S, s = hs - h * p.S;
+  for (int c = threadIdx.x; c < p.C; c += blockDim.x) hist[c] = 0;
+  __syncthreads();
+  const uint8_t* cb = p.codes + h * p.codes_head_stride + s;
+  const int64_t i0 = (int64_t)chunk * kPostChunk;
+  const int64_t i1 = min(p.L, i0 + kPostChunk);
+  for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+    const int c = __ldg(cb + i * p.S);
+    if (c < p.C) atomicAdd(&hist[c], 1);
+  }
+  __syncthreads();
+  int32_t* out = p.chunk_hist + ((size_t)hs * p.nchunks + chunk) * p.C;
+  for (int c = threadIdx.x; c < p.C; c += blockDim.x) out[c] = hist[c];
+}
+
+__global__ void __launch_bounds__(kPostThreads) post_scan_kernel(const PostParams p) {
+  __shared__ int tot[kMaxCodewords];
+  __shared__ int scratch[kPostThreads / 32 + 1];
+  const int hs = blockIdx.x;
+  const int c = threadIdx.x;
+  int32_t* ch = p.chunk_hist + (size_t)hs * p.nchunks * p.C;
+  int total = 0;
+  if (c < p.C)
+    for (int k = 0; k < p.nchunks; ++k) total += ch[(size_t)k * p.C + c];
+  int all;
+  const int excl = block_excl_scan(c < p.C ? total : 0, scratch, &all);
+  if (c < p.C) {
+    tot[c] = total;
+    p.counts[(size_t)hs * p.C + c] = total;
+    p.offsets[(size_t)hs * (p.C + 1) + c] = excl;
+    if (c == p.C - 1) p.offsets[(size_t)hs * (p.C + 1) + p.C] = excl + total;
+    int run = excl;
+    for (int k = 0; k < p.nchunks; ++k) {
+      const int v = ch[(size_t)k * p.C + c];
+      ch[(size_t)k * p.C + c] = run;  // becomes the base of (chunk k, code c)
+      run += v;
+    }
+    if (total > 0) atomicMax(p.max_bucket, total);
+  }
+}
+
+__global__ void __launch_bounds__(kPostThreads) post_scatter_kernel(const PostParams p) {
+  __shared__ int base[kMaxCodewords];     // running position per code inside this chunk
+  __shared__ int wcnt[kPostThreads / 32][kMaxCodewords];
+  const int hs = blockIdx.y, chunk = blockIdx.x;
+  const int h = hs / p.S, s = hs - h * p.S;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  const int32_t* cbase = p.chunk_hist + ((size_t)hs * p.nchunks + chunk) * p.C;
+  for (int c = tid; c < p.C; c += blockDim.x) base[c] = cbase[c];
+  const uint8_t* cb = p.codes + h * p.codes_head_stride + s;
+  int32_t* ids = p.ids + (size_t)hs * p.ids_sub_stride;
+  const int64_t i0 = (int64_t)chunk * kPostChunk;
+  const int64_t i1 = min(p.L, i0 + kPostChunk);
+  const unsigned lt = (1u << lane) - 1u;
+  for (int64_t r0 = i0; r0 < i1; r0 += blockDim.x) {
+    for (int e = tid; e < nwarps * p.C; e += blockDim.x) wcnt[e / p.C][e % p.C] = 0;
+    __syncthreads();
+    const int64_t i = r0 + tid;
+    const bool ok = i < i1;
+    int c = ok ? static_cast<int>(__ldg(cb + i * p.S)) : -1;
+    if (c >= p.C) c = -1;
+    const unsigned same = __match_any_sync(0xFFFFFFFFu, c);
+    const int rank_in_warp = __popc(same & lt);
+    if (c >= 0 && rank_in_warp == 0) wcnt[warp][c] = __popc(same);
+    __syncthreads();
+    if (c >= 0) {
+      int pos = base[c] + rank_in_warp;
+      for (int w = 0; w < warp; ++w) pos += wcnt[w][c];
+      ids[pos] = static_cast<int32_t>(i);
+    }
+    __syncthreads();
+    for (int cc = tid; cc < p.C; cc += blockDim.x) {
+      int add = 0;
+      for (int w = 0; w < nwarps; ++w) add += wcnt[w][cc];
+      base[cc] += add;
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace sva
+
+using namespace sva;
+
+extern "C" size_t sva_postings_workspace_size(int32_t n_heads, int32_t subspaces, int32_t codewords, int64_t key_len) {
+  if (n_heads <= 0 || subspaces <= 0 || codewords <= 0 || key_len <= 0) return 0;
+  const int64_t nchunks = (key_len + kPostChunk - 1) / kPostChunk;
+  return sizeof(int32_t) * (size_t)n_heads * subspaces * nchunks * codewords;
+}
+
+extern "C" int sva_postings_build(const uint8_t* codes, int64_t codes_head_stride, int32_t n_heads, int32_t subspaces,
+                                  int32_t codewords, int64_t key_len, int32_t* counts, int32_t* offsets, int32_t* ids,
+                                  int64_t ids_sub_stride, int32_t* max_bucket, void* workspace, size_t workspace_bytes,
+                                  void* stream) {
+  if (n_heads <= 0 || subspaces <= 0 || subspaces > kMaxSubspaces || codewords <= 0 || codewords > kMaxCodewords)
+    return set_error(SVA_ERR_SHAPE, "bad postings shape");
+  if (key_len < 0 || key_len > 0x7FFFFFFFll) return set_error(SVA_ERR_SHAPE, "key_len out of range");
+  if (ids_sub_stride < key_len) return set_error(SVA_ERR_SHAPE, "ids_sub_stride must be >= key_len");
+  if (!counts || !offsets || !ids || !max_bucket || (key_len > 0 && !codes))
+    return set_error(SVA_ERR_SHAPE, "null pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(max_bucket, 0, sizeof(int32_t), st);
+  if (e != cudaSuccess) return set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
+  const size_t need = sva_postings_workspace_size(n_heads, subspaces, codewords, key_len);
+  if (key_len == 0) {
+    e = cudaMemsetAsync(counts, 0, sizeof(int32_t) * n_heads * subspaces * codewords, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(offsets, 0, sizeof(int32_t) * n_heads * subspaces * (codewords + 1), st);
+    return e == cudaSuccess ? SVA_OK : set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
+  }
+  if (workspace_bytes < need || !workspace) return set_error(SVA_ERR_WORKSPACE, "postings workspace too small");
+  PostParams p;
+  p.codes = codes;
+  p.codes_head_stride = codes_head_stride;
+  p.H = n_heads;
+  p.S = subspaces;
+  p.C = codewords;
+  p.L = key_len;
+  p.nchunks = static_cast<int>((key_len + kPostChunk - 1) / kPostChunk);
+  p.counts = counts;
+  p.offsets = offsets;
+  p.ids = ids;
+  p.ids_sub_stride = ids_sub_stride;
+  p.max_bucket = max_bucket;
+  p.chunk_hist = static_cast<int32_t*>(workspace);
+  dim3 grid(p.nchunks, n_heads * subspaces);
+  post_hist_kernel<<<grid, kPostThreads, 0, st>>>(p);
+  profile_mark(0, st);
+  post_scan_kernel<<<n_heads * subspaces, kPostThreads, 0, st>>>(p);
+  profile_mark(1, st);
+  post_scatter_kernel<<<grid, kPostThreads, 0, st>>>(p);
+  profile_mark(2, st);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
+  return SVA_OK;
+}

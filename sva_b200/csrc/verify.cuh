@@ -1,0 +1,140 @@
+// Exact verify over selected keys, shared by the scan and inverted decode kernels
+// (replaces sva/llama.py:304-317 and :532-553).
+//
+// logits: q . K[key] * softmax_scale, one half-warp per key row (16 lanes x 4 elements per
+//         64-wide chunk, tree order).  logits_mode 1 reproduces the reference scan path for
+//         bf16 / fp16 models: every product rounded to the value dtype, the sum rounded, the
+//         scaled logit rounded.  logits_mode 0 keeps fp32 logits (static path, benchmark).
+// softmax: fp32 max, fp64 denominator; weights rounded to the value dtype (the reference casts
+//         the fp32 softmax to the query dtype).
+// output: sum_j round(w_j * V[j]) accumulated in fp64 (exact for bf16 products, so the result
+//         does not depend on the order of the selected keys), rounded to the value dtype.
+#pragma once
+
+#include "sva_common.cuh"
+
+namespace sva {
+
+// Shared-memory need: lg[n_fin] floats; acc[(nwarps * 64) + nwarps + 1] doubles; scratch[64] ints.
+template <typename T>
+__device__ void verify_rows(const void* keys, int64_t k_head_stride, int64_t k_row_stride, const void* values,
+                            int64_t v_head_stride, int64_t v_row_stride, int kvh, const float* qf, int D,
+                            const int32_t* fin, int n_fin, float softmax_scale, int logits_mode, float* lg,
+                            double* acc, int* scratch, T* out) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  const int half = lane >> 4, l16 = lane & 15;
+  const T* kb = reinterpret_cast<const T*>(keys) + kvh * k_head_stride;
+  const T* vb = reinterpret_cast<const T*>(values) + kvh * v_head_stride;
+  constexpr int U = 4;
+  for (int base = warp * 2 * U; base < n_fin; base += nwarps * 2 * U) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int j = base + 2 * u + half;
+      const bool ok = j < n_fin;
+      const T* krow = ok ? kb + (int64_t)fin[j] * k_row_stride : nullptr;
+      float part = 0.f;
+      for (int c0 = 0; c0 < D; c0 += 64) {
+        const int e = c0 + 4 * l16;
+        if (!ok || e >= D) continue;
+        const float4 k4 = load4<T>(krow, e, D);
+        const float4 qv = make_float4(qf[e], (e + 1 < D) ? qf[e + 1] : 0.f, (e + 2 < D) ? qf[e + 2] : 0.f,
+                                      (e + 3 < D) ? qf[e + 3] : 0.f);
+        if (logits_mode == 1) {
+          float s = round_to<T>(__fmul_rn(k4.x, qv.x));
+          s = __fadd_rn(s, round_to<T>(__fmul_rn(k4.y, qv.y)));
+          s = __fadd_rn(s, round_to<T>(__fmul_rn(k4.z, qv.z)));
+          s = __fadd_rn(s, round_to<T>(__fmul_rn(k4.w, qv.w)));
+          part = __fadd_rn(part, s);
+        } else {
+          part = __fadd_rn(part, lane4(k4, qv));
+        }
+      }
+      float s = tree16(part);
+      if (logits_mode == 1) {
+        s = round_to<T>(s);
+        s = round_to<T>(__fmul_rn(s, softmax_scale));
+      } else {
+        s = __fmul_rn(s, softmax_scale);
+      }
+      if (ok && l16 == 0) lg[j] = s;
+    }
+  }
+  __syncthreads();
+
+  float mx = -INFINITY;
+  for (int j = tid; j < n_fin; j += blockDim.x) mx = fmaxf(mx, lg[j]);
+  mx = warp_max(mx);
+  float* redf = reinterpret_cast<float*>(scratch);
+  if (lane == 0) redf[warp] = mx;
+  __syncthreads();
+  if (tid < 32) {
+    float v = (tid < nwarps) ? redf[tid] : -INFINITY;
+    v = warp_max(v);
+    if (tid == 0) redf[32] = v;
+  }
+  __syncthreads();
+  mx = redf[32];
+  double se = 0.0;
+  for (int j = tid; j < n_fin; j += blockDim.x) se += static_cast<double>(expf(lg[j] - mx));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) se += __shfl_xor_sync(0xFFFFFFFFu, se, o);
+  if (lane == 0) acc[warp] = se;
+  __syncthreads();
+  if (tid == 0) {
+    double tot = 0.0;
+    for (int w = 0; w < nwarps; ++w) tot += acc[w];
+    acc[nwarps] = tot;
+  }
+  __syncthreads();
+  const float denom = static_cast<float>(acc[nwarps]);
+  __syncthreads();
+  for (int j = tid; j < n_fin; j += blockDim.x) lg[j] = round_to<T>(expf(lg[j] - mx) / denom);
+  __syncthreads();
+
+  const int nchunks = (D + 63) / 64;
+  for (int c = 0; c < nchunks; ++c) {
+    const int e = c * 64 + 4 * l16;
+    double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+    for (int base = warp * 2 * U; base < n_fin; base += nwarps * 2 * U) {
+      float4 v[U];
+      float w[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int j = base + 2 * u + half;
+        v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        w[u] = 0.f;
+        if (j < n_fin && e < D) {
+          v[u] = load4<T>(vb + (int64_t)fin[j] * v_row_stride, e, D);
+          w[u] = lg[j];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        a0 += static_cast<double>(round_to<T>(__fmul_rn(w[u], v[u].x)));
+        a1 += static_cast<double>(round_to<T>(__fmul_rn(w[u], v[u].y)));
+        a2 += static_cast<double>(round_to<T>(__fmul_rn(w[u], v[u].z)));
+        a3 += static_cast<double>(round_to<T>(__fmul_rn(w[u], v[u].w)));
+      }
+    }
+    a0 += __shfl_xor_sync(0xFFFFFFFFu, a0, 16);
+    a1 += __shfl_xor_sync(0xFFFFFFFFu, a1, 16);
+    a2 += __shfl_xor_sync(0xFFFFFFFFu, a2, 16);
+    a3 += __shfl_xor_sync(0xFFFFFFFFu, a3, 16);
+    __syncthreads();
+    if (half == 0) {
+      acc[warp * 64 + 4 * l16 + 0] = a0;
+      acc[warp * 64 + 4 * l16 + 1] = a1;
+      acc[warp * 64 + 4 * l16 + 2] = a2;
+      acc[warp * 64 + 4 * l16 + 3] = a3;
+    }
+    __syncthreads();
+    if (tid < 64 && c * 64 + tid < D) {
+      double tot = 0.0;
+      for (int w2 = 0; w2 < nwarps; ++w2) tot += acc[w2 * 64 + tid];
+      out[c * 64 + tid] = from_f32<T>(n_fin > 0 ? static_cast<float>(tot) : 0.f);
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace sva

@@ -191,3 +191,120 @@ def sva_scale(logit_scale: torch.Tensor) -> torch.Tensor:
 
 def sqrt_rank(rank_dim: int) -> float:
     return math.sqrt(rank_dim)
+
+
+_post_ws = Workspace()
+_inv_ws = Workspace()
+
+
+class Postings:
+    """Device CSR posting lists of one catalog (see sva_postings_build)."""
+
+    def __init__(self, counts, offsets, ids, max_bucket, key_len: int):
+        self.counts, self.offsets, self.ids, self.max_bucket = counts, offsets, ids, max_bucket
+        self.key_len = int(key_len)
+
+
+def postings_build(codes: torch.Tensor, codewords: int, key_len: int | None = None) -> Postings:
+    """Posting lists of keys [0, key_len) of codes [H, L, S] uint8 (reference sva/llama.py:626-657)."""
+    _cuda(codes, "codes")
+    if codes.dtype != torch.uint8 or codes.stride(-1) != 1 or codes.stride(-2) != codes.shape[-1]:
+        raise ValueError("codes must be uint8 with contiguous [L, S] rows per head")
+    n_heads, cap, subspaces = codes.shape
+    key_len = cap if key_len is None else int(key_len)
+    dev = codes.device
+    counts = torch.empty(n_heads, subspaces, codewords, dtype=torch.int32, device=dev)
+    offsets = torch.empty(n_heads, subspaces, codewords + 1, dtype=torch.int32, device=dev)
+    ids = torch.empty(n_heads, subspaces, max(key_len, 1), dtype=torch.int32, device=dev)
+    max_bucket = torch.empty(1, dtype=torch.int32, device=dev)
+    lib = _lib.load()
+    ws_bytes = int(lib.sva_postings_workspace_size(n_heads, subspaces, codewords, key_len))
+    ws = _post_ws.get(dev, ws_bytes)
+    rc = lib.sva_postings_build(codes.data_ptr(), codes.stride(0), n_heads, subspaces, codewords, key_len,
+                                counts.data_ptr(), offsets.data_ptr(), ids.data_ptr(), ids.shape[-1],
+                                max_bucket.data_ptr(), _ptr(ws), ws_bytes, _stream(dev))
+    _lib.check(rc)
+    return Postings(counts, offsets, ids, max_bucket, key_len)
+
+
+def decode_inverted(q: torch.Tensor, q_proj: torch.Tensor, scale: torch.Tensor, codebooks: torch.Tensor,
+                    codes: torch.Tensor, postings: Postings, k_low: torch.Tensor, keys: torch.Tensor,
+                    values: torch.Tensor, budget: int, cells: int, min_budget: int, mid_budget: int,
+                    low_margin: float = 0.35, high_margin: float = 0.70, dynamic: bool = False,
+                    refill_factor: int = 2, allowed_len: int | None = None, softmax_scale: float | None = None,
+                    out: torch.Tensor | None = None, want_selection: bool = False, stats: torch.Tensor | None = None):
+    """Inverted-index decode of one token per head (reference sva/llama.py:427-576 / :330-425).
+
+    q [H, D]; codes [H, >=postings_len, S]; k_low [H, L, R]; keys/values [Hkv, L, D].  ``budget``,
+    ``min_budget`` and ``mid_budget`` are already clamped as the reference clamps them.
+    """
+    for name, t in (("q", q), ("codes", codes), ("k_low", k_low), ("keys", keys), ("values", values)):
+        _cuda(t, name)
+    dev = q.device
+    n_heads, head_dim = q.shape
+    key_len = int(k_low.shape[1])
+    if out is None:
+        out = torch.empty(n_heads, head_dim, dtype=q.dtype, device=dev)
+    a = _lib.InvertedArgs()
+    a.n_heads, a.n_kv_heads, a.head_dim = n_heads, int(keys.shape[0]), head_dim
+    a.rank_dim, a.subspaces, a.codewords = int(q_proj.shape[-1]), int(codebooks.shape[1]), int(codebooks.shape[2])
+    a.budget, a.cells, a.refill_factor, a.dynamic = int(budget), int(cells), int(refill_factor), int(bool(dynamic))
+    a.min_budget, a.mid_budget = int(min_budget), int(mid_budget)
+    a.qkv_dtype = dtype_code(q.dtype)
+    a.low_margin, a.high_margin = float(low_margin), float(high_margin)
+    a.softmax_scale = float(head_dim ** -0.5 if softmax_scale is None else softmax_scale)
+    a.key_len = key_len
+    a.postings_len = postings.key_len
+    a.allowed_len = key_len if allowed_len is None else int(allowed_len)
+    a.query, a.q_head_stride = q.data_ptr(), q.stride(0)
+    a.q_proj, a.scale, a.codebooks = q_proj.data_ptr(), scale.data_ptr(), codebooks.data_ptr()
+    a.codes, a.codes_head_stride = codes.data_ptr(), codes.stride(0)
+    a.post_counts, a.post_offsets = postings.counts.data_ptr(), postings.offsets.data_ptr()
+    a.post_ids, a.post_ids_sub_stride = postings.ids.data_ptr(), postings.ids.shape[-1]
+    a.max_bucket = postings.max_bucket.data_ptr()
+    a.k_low, a.k_low_head_stride = k_low.data_ptr(), k_low.stride(0)
+    a.keys, a.k_head_stride, a.k_row_stride = keys.data_ptr(), keys.stride(0), keys.stride(1)
+    a.values, a.v_head_stride, a.v_row_stride = values.data_ptr(), values.stride(0), values.stride(1)
+    a.out, a.out_head_stride = out.data_ptr(), out.stride(0)
+    sel = None
+    if want_selection:
+        sel = (torch.empty(n_heads, int(budget), dtype=torch.int32, device=dev),
+               torch.empty(n_heads, int(budget), dtype=torch.uint8, device=dev),
+               torch.empty(n_heads, int(budget), dtype=torch.float32, device=dev),
+               torch.empty(n_heads, dtype=torch.int32, device=dev))
+        a.sel_idx_out, a.sel_valid_out, a.sel_score_out, a.budget_out = (t.data_ptr() for t in sel)
+    a.stats = _ptr(stats)
+    lib = _lib.load()
+    ws_bytes = int(lib.sva_inverted_workspace_size(ctypes.byref(a)))
+    if ws_bytes == 0:
+        raise ValueError("sva_b200: invalid inverted decode arguments")
+    ws = _inv_ws.get(dev, ws_bytes)
+    rc = lib.sva_decode_inverted(ctypes.byref(a), _ptr(ws), ws_bytes, _stream(dev))
+    _lib.check(rc)
+    return (out, *sel) if want_selection else out
+
+
+def top_unique(candidate_idx: torch.Tensor, candidate_scores: torch.Tensor, candidate_valid: torch.Tensor,
+               budget: int, refill_factor: int = 2):
+    """Refill-and-dedupe selection on explicit rows (reference sva/llama.py:83-116)."""
+    for name, t in (("candidate_idx", candidate_idx), ("candidate_scores", candidate_scores),
+                    ("candidate_valid", candidate_valid)):
+        _cuda(t, name)
+    dev = candidate_idx.device
+    rows, width = candidate_idx.shape
+    idx = candidate_idx.to(torch.int64).contiguous()
+    scores = candidate_scores.to(torch.float32).contiguous()
+    valid = candidate_valid.to(torch.uint8).contiguous()
+    if width == 0 or budget <= 0:
+        return candidate_idx[:, :0], candidate_scores[:, :0], candidate_valid[:, :0], 0
+    refill = min(width, max(budget, budget * refill_factor))
+    sel_count = min(budget, refill)
+    sel_idx = torch.empty(rows, sel_count, dtype=torch.int64, device=dev)
+    sel_scores = torch.empty(rows, sel_count, dtype=torch.float32, device=dev)
+    sel_valid = torch.empty(rows, sel_count, dtype=torch.uint8, device=dev)
+    refill_out = ctypes.c_int32(0)
+    rc = _lib.load().sva_top_unique(idx.data_ptr(), scores.data_ptr(), valid.data_ptr(), rows, width, int(budget),
+                                    int(refill_factor), sel_idx.data_ptr(), sel_scores.data_ptr(), sel_valid.data_ptr(),
+                                    ctypes.byref(refill_out), _stream(dev))
+    _lib.check(rc)
+    return sel_idx, sel_scores.to(candidate_scores.dtype), sel_valid.bool(), int(refill_out.value)
