@@ -48,6 +48,7 @@ enum {
   SVA_STAT_EXACT_SCORED = 3,
   SVA_STAT_VERIFIED = 4,
   SVA_STAT_CELL_VISITS = 5,
+  SVA_STAT_SELECT_FALLBACKS = 6, /* million-key schedule: sampled threshold too high, exact rescan */
   SVA_STAT_COUNT = 8
 };
 
@@ -188,7 +189,8 @@ typedef struct sva_inverted_args {
   float softmax_scale;
   int64_t key_len;      /* keys in k_low / K / V */
   int64_t postings_len; /* keys covered by the posting lists */
-  int64_t allowed_len;  /* keys [0, allowed_len) are allowed */
+  int64_t allowed_len;  /* keys [0, allowed_len) are allowed ... */
+  const uint8_t* allowed_mask; /* ... and, if not NULL, only keys with allowed_mask[key] != 0 */
   const void* query;    /* [H][D], one token per head */
   int64_t q_head_stride;
   const float* q_proj;

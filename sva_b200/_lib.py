@@ -31,6 +31,7 @@ STAT_REFILL_POOL = 2
 STAT_EXACT_SCORED = 3
 STAT_VERIFIED = 4
 STAT_CELL_VISITS = 5
+STAT_SELECT_FALLBACKS = 6
 STAT_COUNT = 8
 
 # Every symbol include/sva_b200.h declares (checked by the CPU test suite).
@@ -126,6 +127,7 @@ class InvertedArgs(ctypes.Structure):
         ("key_len", c_i64),
         ("postings_len", c_i64),
         ("allowed_len", c_i64),
+        ("allowed_mask", c_vp),
         ("query", c_vp),
         ("q_head_stride", c_i64),
         ("q_proj", c_vp),

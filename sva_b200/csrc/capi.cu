@@ -19,14 +19,28 @@ int ensure_smem_attr(const void* kernel, int bytes) {
   static std::unordered_set<unsigned long long> done;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
+  }
   const unsigned long long key = (reinterpret_cast<unsigned long long>(kernel) << 6) ^ static_cast<unsigned long long>(dev);
   {
     std::lock_guard<std::mutex> lock(mu);
     if (done.count(key)) return SVA_OK;
   }
-  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e != cudaSuccess) return set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
+  // The dynamic limit may not exceed the opt-in maximum minus the kernel's static shared memory.
+  cudaFuncAttributes fa;
+  int optin = 0;
+  e = cudaFuncGetAttributes(&fa, kernel);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (e == cudaSuccess) {
+    const int room = optin - static_cast<int>(fa.sharedSizeBytes);
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes < room ? bytes : room);
+  }
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // do not leave the error for the next runtime call
+    return set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
+  }
   std::lock_guard<std::mutex> lock(mu);
   done.insert(key);
   return SVA_OK;

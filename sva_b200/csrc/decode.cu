@@ -7,23 +7,26 @@
 //   select over it; the CTA then rescores the shortlist against k_low, selects the budget and
 //   runs the verify.  One launch per call.
 //
-// * grid   (longer caches): the key range of each problem is cut into segments of kSegKeys.
-//     qlut    : one CTA per problem builds q_low and the LUT into the workspace and clears the
-//               problem's histogram / control block;
-//     hist    : one CTA per segment builds a 4096-bin histogram of the top 12 bits of the
-//               ordered ADC key and adds it to the problem's global histogram; the last CTA to
-//               finish (ticket counter, no waiting) finds the boundary bin b* of the shortlist;
-//     collect : one CTA per segment re-reads its codes (now in L2); keys above b* go straight
-//               to the shortlist, keys in b* go to an edge buffer sized for the whole range;
-//     problem : one CTA per problem selects the missing shortlist entries from the edge buffer
-//               (exact, canonical; in shared memory when it fits, else streamed from L2), then
-//               rescores / selects / verifies as in the fused schedule.
+// * grid   (longer caches), three launches:
+//     prep    : one CTA per problem builds q_low and the LUT into the workspace, scores a
+//               sample of 4096 keys (32 evenly spaced runs of 128) and takes the sample's r-th
+//               best key as a threshold T0 chosen so that about 3x the shortlist lies above it;
+//     scan    : one CTA per segment of kScanKeys keys, the single full pass over the codes:
+//               every allowed key with key >= T0 is appended to the problem's candidate list;
+//     finish  : a cluster of kCluster CTAs per problem.  CTA 0 selects the exact shortlist from
+//               the candidates (shared memory when they fit, else streamed from L2; if fewer
+//               than `shortlist` keys reached T0 it re-selects exactly over every key and counts
+//               a fallback), the rescore and the verify are split across the cluster through
+//               distributed shared memory, and CTA 0 merges the fp64 partial outputs.
+//   The threshold only decides how much work the finish does, never which keys are selected.
 //
 // Codes are read four keys per vector load (S bytes per key), four loads in flight per thread.
 // Selection rule everywhere: score descending, key index ascending (see cta_select.cuh).
 // ADC score: ((0 + lut[0][c0]) + lut[1][c1]) + ... in subspace order, then / sqrt(R)
 // (reference sva/ops.py:64-71).  Rank score: tree_dot(k_low, q_low) / sqrt(R)
 // (reference sva/llama.py:286-292).
+#include <cooperative_groups.h>
+
 #include "cta_select.cuh"
 #include "qlut.cuh"
 #include "sva_internal.h"
@@ -31,15 +34,20 @@
 
 namespace sva {
 
+namespace cg = cooperative_groups;
+
 constexpr int kThreads = 512;
-constexpr int kBins = 4096;
-constexpr int kSegKeys = 16384;
+constexpr int kScanKeys = 8192;          // keys per scan CTA
 constexpr int kFusedMaxKeys = 32768;
-constexpr int kEdgeSmem = 12288;  // edge entries resolved in shared memory
+constexpr int kCandSmem = 12288;         // candidates selected in shared memory
 constexpr int kScanThreads = 256;
 constexpr int kGroupsInFlight = 4;
+constexpr int kSampleRuns = 32;
+constexpr int kSampleRunKeys = 128;
+constexpr int kSample = kSampleRuns * kSampleRunKeys;
+constexpr int kCluster = 8;
 
-enum { CTRL_T_HIST = 0, CTRL_K, CTRL_BSTAR, CTRL_NABOVE, CTRL_NOUT, CTRL_NEDGE, CTRL_NVALID, CTRL_WORDS = 8 };
+enum { CTRL_NCAND = 0, CTRL_T0, CTRL_WORDS = 4 };
 
 struct DecodeSmem {
   int qf, ql, lut, sc, scratch, sl, rk, fin, lg, acc, cache, total;
@@ -59,7 +67,7 @@ __host__ __device__ inline DecodeSmem decode_smem_layout(int head_dim, int sl_ca
   s.rk = o;      o = align16(o + 4 * sl_cap);
   s.fin = o;     o = align16(o + 4 * b_cap);
   s.lg = o;      o = align16(o + 4 * b_cap);
-  s.acc = o;     o = align16(o + 8 * ((kThreads / 32) * 64 + kThreads / 32 + 1));
+  s.acc = o;     o = align16(o + 8 * ((kThreads / 32) * 64 + kMaxHeadDim));
   s.cache = o;   o = align16(o + cache_bytes);
   s.total = o;
   return s;
@@ -80,15 +88,15 @@ struct DecodeParams {
   DecodeSmem lay;
   float* ws_qlow;
   float* ws_lut;
-  uint32_t* ws_hist;
   uint32_t* ws_ctrl;
-  int32_t* ws_part;
-  uint2* ws_edge;
+  uint2* ws_cand;  // [P][key_len] (key32, index)
 };
 
 // ---------------------------------------------------------------------------------------
 // small device helpers
 // ---------------------------------------------------------------------------------------
+
+__host__ __device__ __forceinline__ int64_t imin64(int64_t x, int64_t y) { return x < y ? x : y; }
 
 __device__ __forceinline__ float finish_score(float sum, const DecodeParams& p) {
   return p.sqrt_r_pow2 ? __fmul_rn(sum, p.inv_sqrt_r) : __fdiv_rn(sum, p.sqrt_r);
@@ -185,11 +193,50 @@ __device__ __forceinline__ int block_sum_int(int v, int* scratch) {
 }
 
 // ---------------------------------------------------------------------------------------
-// per-problem kernel: (fused) shortlist + rescore + budget select + verify
+// fused schedule: one CTA per problem (key_len <= kFusedMaxKeys)
 // ---------------------------------------------------------------------------------------
 
+// Rank keys of shortlist rows [0, n): two rows per warp step (one per half-warp), U steps in
+// flight.  `rows` are key indices; rk[j] receives the ordered rank score of rows[j].
+template <int U>
+__device__ void rescore_rows(const DecodeParams& p, int h, const float* ql, const int32_t* rows, int n, uint32_t* rk) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int half = lane >> 4, l16 = lane & 15;
+  const int R = p.a.rank_dim;
+  const float4 q4 = (4 * l16 < R) ? make_float4(ql[4 * l16], ql[4 * l16 + 1], ql[4 * l16 + 2], ql[4 * l16 + 3])
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+  const float* klb = p.a.k_low + h * p.a.k_low_head_stride;
+  for (int base = warp * 2 * U; base < n; base += nwarps * 2 * U) {
+    float4 r[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int j = base + 2 * u + half;
+      r[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (j < n && 4 * l16 < R) r[u] = load4<float>(klb + (int64_t)rows[j] * R, 4 * l16, R);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int j = base + 2 * u + half;
+      const float s = tree16(lane4(r[u], q4));
+      if (j < n && l16 == 0) rk[j] = ordered_key(finish_score(s, p));
+    }
+  }
+  __syncthreads();
+}
+
+// Ascending copies of the shortlist / final index sets for the debug outputs.
+__device__ void write_sorted(const int32_t* src, int n, int width, int32_t* dst, unsigned long long* tmp) {
+  int cap = 1;
+  while (cap < n) cap <<= 1;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) tmp[i] = static_cast<unsigned long long>(static_cast<uint32_t>(src[i]));
+  __syncthreads();
+  cta_bitonic_sort_u64(tmp, n, cap);
+  for (int i = threadIdx.x; i < width; i += blockDim.x) dst[i] = (i < n) ? static_cast<int32_t>(tmp[i]) : -1;
+  __syncthreads();
+}
+
 template <typename T>
-__global__ void __launch_bounds__(kThreads) decode_problem_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(kThreads) decode_fused_kernel(const DecodeParams p) {
   extern __shared__ __align__(16) unsigned char smem[];
   float* qf = reinterpret_cast<float*>(smem + p.lay.qf);
   float* ql = reinterpret_cast<float*>(smem + p.lay.ql);
@@ -201,6 +248,7 @@ __global__ void __launch_bounds__(kThreads) decode_problem_kernel(const DecodePa
   int32_t* fin = reinterpret_cast<int32_t*>(smem + p.lay.fin);
   float* lg = reinterpret_cast<float*>(smem + p.lay.lg);
   double* acc = reinterpret_cast<double*>(smem + p.lay.acc);
+  uint32_t* cache = reinterpret_cast<uint32_t*>(smem + p.lay.cache);
 
   const int prob = blockIdx.x;
   const int h = prob / p.a.n_queries;
@@ -209,90 +257,27 @@ __global__ void __launch_bounds__(kThreads) decode_problem_kernel(const DecodePa
   const int64_t L = p.a.key_len;
   const int64_t len_t = allowed_length(p, t);
   const uint8_t* codes = p.a.codes + h * p.a.codes_head_stride;
-  const int R = p.a.rank_dim, D = p.a.head_dim;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  const int tid = threadIdx.x;
 
-  // ---- shortlist -------------------------------------------------------------------------
-  int n_sl = 0;
-  if (!p.grid_mode) {
-    build_qlut<T>(p, h, t, qf, ql, lut, reinterpret_cast<float*>(smem + p.lay.cache));
-    uint32_t* cache = reinterpret_cast<uint32_t*>(smem + p.lay.cache);
-    int nv = 0;
-    for (int64_t i = tid; i < L; i += blockDim.x) {
-      const uint32_t key = adc_key(p, codes, lut, t, i, len_t);
-      cache[i] = key;
-      nv += (key != 0u);
-    }
-    const int n_valid = block_sum_int(nv, scratch);
-    const int k = min(p.sl_cap, n_valid);
+  build_qlut<T>(p, h, t, qf, ql, lut, reinterpret_cast<float*>(cache));
+  int nv = 0;
+  for (int64_t i = tid; i < L; i += blockDim.x) {
+    const uint32_t key = adc_key(p, codes, lut, t, i, len_t);
+    cache[i] = key;
+    nv += (key != 0u);
+  }
+  const int n_valid = block_sum_int(nv, scratch);
+  const int k = min(p.sl_cap, n_valid);
+  int n_sl;
+  {
     auto item = [&](int i) -> unsigned long long {
       return cache[i] ? composite(cache[i], static_cast<uint32_t>(i)) : 0ull;
     };
     const SelectThreshold thr = cta_radix_select(item, static_cast<int>(L), k, sc);
     n_sl = cta_compact(item, static_cast<int>(L), thr, [&](int pos, int i, unsigned long long) { sl[pos] = i; },
                        scratch);
-  } else {
-    const T* q = reinterpret_cast<const T*>(p.a.query) + h * p.a.q_head_stride + t * p.a.q_row_stride;
-    for (int d = tid; d < D; d += blockDim.x) qf[d] = to_f32<T>(q[d]);
-    for (int r = tid; r < R; r += blockDim.x) ql[r] = __ldcg(p.ws_qlow + (size_t)prob * kMaxRank + r);
-    const uint32_t* ctrl = p.ws_ctrl + (size_t)prob * CTRL_WORDS;
-    const int k = static_cast<int>(__ldcg(ctrl + CTRL_K));
-    const int n_part = min(static_cast<int>(__ldcg(ctrl + CTRL_NOUT)), k);
-    const int64_t n_edge64 = __ldcg(ctrl + CTRL_NEDGE);
-    const int n_edge = static_cast<int>(n_edge64 < L ? n_edge64 : L);
-    const int32_t* part = p.ws_part + (size_t)prob * p.sl_cap;
-    for (int i = tid; i < n_part; i += blockDim.x) sl[i] = __ldcg(part + i);
-    const uint2* ge = p.ws_edge + (size_t)prob * L;
-    // edge entries share the top 12 key bits: order them by the low 20 key bits, then index
-    auto local = [](uint2 v) -> unsigned long long {
-      return (static_cast<unsigned long long>(v.x & 0xFFFFFu) << 44) |
-             (static_cast<unsigned long long>(~v.y) << 12) | 1ull;
-    };
-    const int need = k - n_part;
-    if (n_edge <= kEdgeSmem) {
-      uint2* edge = reinterpret_cast<uint2*>(smem + p.lay.cache);
-      for (int i = tid; i < n_edge; i += blockDim.x) edge[i] = __ldcg(ge + i);
-      __syncthreads();
-      auto item = [&](int i) -> unsigned long long { return local(edge[i]); };
-      const SelectThreshold thr = cta_radix_select(item, n_edge, need, sc);
-      cta_compact(item, n_edge, thr, [&](int pos, int i, unsigned long long) { sl[n_part + pos] = edge[i].y; },
-                  scratch);
-    } else {
-      auto item = [&](int i) -> unsigned long long { return local(__ldcg(ge + i)); };
-      const SelectThreshold thr = cta_radix_select(item, n_edge, need, sc);
-      cta_compact(item, n_edge, thr,
-                  [&](int pos, int i, unsigned long long) { sl[n_part + pos] = __ldcg(ge + i).y; }, scratch);
-    }
-    n_sl = k;
   }
-  __syncthreads();
-
-  // ---- rank rescore: two rows per warp step (one per half-warp), 16 steps in flight -------
-  {
-    const int half = lane >> 4, l16 = lane & 15;
-    const float4 q4 = (4 * l16 < R) ? make_float4(ql[4 * l16], ql[4 * l16 + 1], ql[4 * l16 + 2], ql[4 * l16 + 3])
-                                    : make_float4(0.f, 0.f, 0.f, 0.f);
-    const float* klb = p.a.k_low + h * p.a.k_low_head_stride;
-    constexpr int U = 16;
-    for (int base = warp * 2 * U; base < n_sl; base += nwarps * 2 * U) {
-      float4 r[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int j = base + 2 * u + half;
-        r[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (j < n_sl && 4 * l16 < R) r[u] = load4<float>(klb + (int64_t)sl[j] * R, 4 * l16, R);
-      }
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int j = base + 2 * u + half;
-        const float s = tree16(lane4(r[u], q4));
-        if (j < n_sl && l16 == 0) rk[j] = ordered_key(finish_score(s, p));
-      }
-    }
-  }
-  __syncthreads();
-
-  // ---- budget select ----------------------------------------------------------------------
+  rescore_rows<16>(p, h, ql, sl, n_sl, rk);
   const int b = min(p.b_cap, n_sl);
   int n_fin;
   {
@@ -300,36 +285,12 @@ __global__ void __launch_bounds__(kThreads) decode_problem_kernel(const DecodePa
     const SelectThreshold thr = cta_radix_select(item, n_sl, b, sc);
     n_fin = cta_compact(item, n_sl, thr, [&](int pos, int j, unsigned long long) { fin[pos] = sl[j]; }, scratch);
   }
-
-  // ---- verify ----------------------------------------------------------------------------
   verify_rows<T>(p.a.keys, p.a.k_head_stride, p.a.k_row_stride, p.a.values, p.a.v_head_stride, p.a.v_row_stride, kvh,
-                 qf, D, fin, n_fin, p.a.softmax_scale, p.a.logits_mode, lg, acc, scratch,
+                 qf, p.a.head_dim, fin, n_fin, p.a.softmax_scale, p.a.logits_mode, lg, acc, scratch,
                  reinterpret_cast<T*>(p.a.out) + h * p.a.out_head_stride + t * p.a.out_row_stride);
-
-  // ---- debug outputs and counters -------------------------------------------------------
-  if (p.a.shortlist_out || p.a.final_out) {
-    unsigned long long* tmp = reinterpret_cast<unsigned long long*>(smem + p.lay.cache);
-    if (p.a.shortlist_out) {
-      int cap = 1;
-      while (cap < n_sl) cap <<= 1;
-      for (int i = tid; i < n_sl; i += blockDim.x) tmp[i] = static_cast<unsigned long long>(static_cast<uint32_t>(sl[i]));
-      __syncthreads();
-      cta_bitonic_sort_u64(tmp, n_sl, cap);
-      int32_t* o = p.a.shortlist_out + (size_t)prob * p.a.shortlist;
-      for (int i = tid; i < p.a.shortlist; i += blockDim.x) o[i] = (i < n_sl) ? static_cast<int32_t>(tmp[i]) : -1;
-      __syncthreads();
-    }
-    if (p.a.final_out) {
-      int cap = 1;
-      while (cap < n_fin) cap <<= 1;
-      for (int i = tid; i < n_fin; i += blockDim.x) tmp[i] = static_cast<unsigned long long>(static_cast<uint32_t>(fin[i]));
-      __syncthreads();
-      cta_bitonic_sort_u64(tmp, n_fin, cap);
-      int32_t* o = p.a.final_out + (size_t)prob * p.a.budget;
-      for (int i = tid; i < p.a.budget; i += blockDim.x) o[i] = (i < n_fin) ? static_cast<int32_t>(tmp[i]) : -1;
-      __syncthreads();
-    }
-  }
+  unsigned long long* tmp = reinterpret_cast<unsigned long long*>(cache);
+  if (p.a.shortlist_out) write_sorted(sl, n_sl, p.a.shortlist, p.a.shortlist_out + (size_t)prob * p.a.shortlist, tmp);
+  if (p.a.final_out) write_sorted(fin, n_fin, p.a.budget, p.a.final_out + (size_t)prob * p.a.budget, tmp);
   if (p.a.stats && tid == 0) {
     atomicAdd(p.a.stats + SVA_STAT_QUERIES, 1ull);
     atomicAdd(p.a.stats + SVA_STAT_SUMMONED, static_cast<unsigned long long>(n_sl));
@@ -339,26 +300,8 @@ __global__ void __launch_bounds__(kThreads) decode_problem_kernel(const DecodePa
 }
 
 // ---------------------------------------------------------------------------------------
-// grid schedule kernels
+// grid schedule
 // ---------------------------------------------------------------------------------------
-
-template <typename T>
-__global__ void __launch_bounds__(256) decode_qlut_kernel(const DecodeParams p) {
-  extern __shared__ __align__(16) float stage[];
-  __shared__ float qf[kMaxHeadDim];
-  __shared__ float ql[kMaxRank];
-  __shared__ float lut[kMaxLut];
-  const int prob = blockIdx.x;
-  const int h = prob / p.a.n_queries, t = prob - h * p.a.n_queries;
-  build_qlut<T>(p, h, t, qf, ql, lut, stage);
-  const int SC = p.a.subspaces * p.a.codewords;
-  float* gl = p.ws_lut + (size_t)prob * kMaxLut;
-  for (int e = threadIdx.x; e < SC; e += blockDim.x) gl[e] = lut[e];
-  for (int r = threadIdx.x; r < p.a.rank_dim; r += blockDim.x) p.ws_qlow[(size_t)prob * kMaxRank + r] = ql[r];
-  uint32_t* hist = p.ws_hist + (size_t)prob * kBins;
-  for (int b = threadIdx.x; b < kBins; b += blockDim.x) hist[b] = 0u;
-  if (threadIdx.x < CTRL_WORDS) p.ws_ctrl[(size_t)prob * CTRL_WORDS + threadIdx.x] = 0u;
-}
 
 // Calls f(i, key) for every key of [i0, i1) (key = 0 when not allowed).  With S > 0 each
 // thread handles groups of four consecutive keys, kGroupsInFlight vector loads at a time.
@@ -369,18 +312,19 @@ __device__ __forceinline__ void scan_segment(const DecodeParams& p, const uint8_
                                              int64_t len_t, int64_t i0, int64_t i1, const F& f) {
   const int lane = threadIdx.x & 31;
   if constexpr (S > 0) {
-    const int64_t ngroups = (i1 - i0 + 3) >> 2;
+    const int ngroups = static_cast<int>((i1 - i0 + 3) >> 2);
     const bool dense = (p.a.allowed_mask == nullptr) && (i1 <= len_t);
-    for (int64_t gb = (threadIdx.x & ~31); gb < ngroups; gb += (int64_t)blockDim.x * kGroupsInFlight) {
+    const uint8_t* cbase = codes + i0 * S;
+    for (int gb = (threadIdx.x & ~31); gb < ngroups; gb += blockDim.x * kGroupsInFlight) {
       Codes4<S> c[kGroupsInFlight];
 #pragma unroll
       for (int u = 0; u < kGroupsInFlight; ++u) {
-        const int64_t g = gb + lane + (int64_t)u * blockDim.x;
-        if (g < ngroups && i0 + 4 * g + 3 < i1) c[u] = load_codes4<S>(codes, i0 + 4 * g);
+        const int g = gb + lane + u * blockDim.x;
+        if (g < ngroups && i0 + 4 * g + 3 < i1) c[u] = load_codes4<S>(cbase, 4 * g);
       }
 #pragma unroll
       for (int u = 0; u < kGroupsInFlight; ++u) {
-        const int64_t g = gb + lane + (int64_t)u * blockDim.x;
+        const int g = gb + lane + u * blockDim.x;
         const int64_t ib = i0 + 4 * g;
         const bool full = g < ngroups && ib + 3 < i1;
 #pragma unroll
@@ -406,125 +350,295 @@ __device__ __forceinline__ void scan_segment(const DecodeParams& p, const uint8_
   }
 }
 
-template <int S>
-__global__ void __launch_bounds__(kScanThreads) decode_hist_kernel(const DecodeParams p) {
+// prep: q_low + LUT, and the sampled threshold T0.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) decode_prep_kernel(const DecodeParams p) {
+  extern __shared__ __align__(16) unsigned char dyn[];
+  __shared__ float qf[kMaxHeadDim];
+  __shared__ float ql[kMaxRank];
   __shared__ float lut[kMaxLut];
-  __shared__ uint32_t hist[kBins];
-  __shared__ int is_last;
-  __shared__ int wsum[kScanThreads / 32];
-  __shared__ int boundary[2];
-  const int prob = blockIdx.y, seg = blockIdx.x;
+  __shared__ SelectScratch sc;
+  __shared__ int scratch[64];
+  __shared__ uint32_t t0_sh;
+  float* stage = reinterpret_cast<float*>(dyn);
+  const int prob = blockIdx.x;
   const int h = prob / p.a.n_queries, t = prob - h * p.a.n_queries;
+  const int tid = threadIdx.x;
+  build_qlut<T>(p, h, t, qf, ql, lut, stage);
   const int SC = p.a.subspaces * p.a.codewords;
-  for (int e = threadIdx.x; e < SC; e += blockDim.x) lut[e] = __ldcg(p.ws_lut + (size_t)prob * kMaxLut + e);
-  for (int b = threadIdx.x; b < kBins; b += blockDim.x) hist[b] = 0u;
-  __syncthreads();
+  float* gl = p.ws_lut + (size_t)prob * kMaxLut;
+  for (int e = tid; e < SC; e += blockDim.x) gl[e] = lut[e];
+  for (int r = tid; r < p.a.rank_dim; r += blockDim.x) p.ws_qlow[(size_t)prob * kMaxRank + r] = ql[r];
+  // sample: kSampleRuns evenly spaced runs of kSampleRunKeys keys over the allowed range
+  uint32_t* samp = reinterpret_cast<uint32_t*>(dyn);  // the stage is no longer needed
   const int64_t len_t = allowed_length(p, t);
   const uint8_t* codes = p.a.codes + h * p.a.codes_head_stride;
-  const int64_t i0 = (int64_t)seg * kSegKeys;
-  const int64_t i1 = min(p.a.key_len, i0 + kSegKeys);
-  scan_segment<S>(p, codes, lut, t, len_t, i0, i1, [&](int64_t, uint32_t key) {
-    if (key) atomicAdd(&hist[key >> 20], 1u);
-  });
+  int nv = 0;
+  for (int e = tid; e < kSample; e += blockDim.x) {
+    const int run = e / kSampleRunKeys, off = e - run * kSampleRunKeys;
+    const int64_t i = (len_t * run) / kSampleRuns + off;
+    const uint32_t key = (i < len_t) ? adc_key(p, codes, lut, t, i, len_t) : 0u;
+    samp[e] = key;
+    nv += key != 0u;
+  }
+  const int n_s = block_sum_int(nv, scratch);
+  const int64_t k_est = imin64(p.sl_cap, len_t);
+  // about 3x the shortlist above the threshold, plus a margin for small samples
+  const int64_t r = (3 * k_est * n_s + len_t - 1) / (len_t > 0 ? len_t : 1) + 8;
+  const bool sampled = n_s > 0 && r < n_s;
+  if (tid == 0) t0_sh = sampled ? 0xFFFFFFFFu : 1u;  // 1: every allowed key is a candidate
   __syncthreads();
-  uint32_t* gh = p.ws_hist + (size_t)prob * kBins;
-  for (int b = threadIdx.x; b < kBins; b += blockDim.x)
-    if (hist[b]) atomicAdd(gh + b, hist[b]);
-  __threadfence();
-  __syncthreads();
-  uint32_t* ctrl = p.ws_ctrl + (size_t)prob * CTRL_WORDS;
-  if (threadIdx.x == 0) is_last = (atomicAdd(ctrl + CTRL_T_HIST, 1u) == static_cast<uint32_t>(p.nseg - 1));
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
-  // Last CTA of this problem: find the boundary bin of the shortlist.  Thread j owns bins
-  // 4095-16j .. 4080-16j (descending).
-  const int tid = threadIdx.x, lane = tid & 31;
-  uint32_t mine[16];
-  int s = 0;
+  if (sampled) {
+    auto item = [&](int i) -> unsigned long long { return samp[i] ? composite(samp[i], static_cast<uint32_t>(i)) : 0ull; };
+    const SelectThreshold thr = cta_radix_select(item, kSample, static_cast<int>(r), &sc);
+    // T0 = smallest key among the r best samples
+    uint32_t mn = 0xFFFFFFFFu;
+    for (int e = tid; e < kSample; e += blockDim.x)
+      if (is_selected(thr, item(e))) mn = min(mn, samp[e]);
 #pragma unroll
-  for (int q = 0; q < 16; ++q) {
-    mine[q] = __ldcg(gh + (kBins - 1 - (16 * tid + q)));
-    s += static_cast<int>(mine[q]);
-  }
-  int incl = warp_incl_scan(s);
-  if (lane == 31) wsum[tid >> 5] = incl;
-  if (tid == 0) {
-    boundary[0] = kBins;  // no key qualifies unless overwritten below
-    boundary[1] = 0;
-  }
-  __syncthreads();
-  int base = 0, total = 0;
-  for (int w = 0; w < kScanThreads / 32; ++w) {
-    if (w < (tid >> 5)) base += wsum[w];
-    total += wsum[w];
-  }
-  const int k = min(p.sl_cap, total);
-  incl += base;
-  const int excl = incl - s;
-  if (k > 0 && excl < k && incl >= k) {
-    int run = excl;
-    for (int q = 0; q < 16; ++q) {
-      const int v = static_cast<int>(mine[q]);
-      if (run + v >= k) {
-        boundary[0] = kBins - 1 - (16 * tid + q);
-        boundary[1] = run;
-        break;
-      }
-      run += v;
-    }
+    for (int o = 16; o > 0; o >>= 1) mn = min(mn, __shfl_xor_sync(0xFFFFFFFFu, mn, o));
+    if ((tid & 31) == 0) atomicMin(&t0_sh, mn);
   }
   __syncthreads();
   if (tid == 0) {
-    ctrl[CTRL_K] = static_cast<uint32_t>(k);
-    ctrl[CTRL_BSTAR] = static_cast<uint32_t>(boundary[0]);
-    ctrl[CTRL_NABOVE] = static_cast<uint32_t>(boundary[1]);
-    ctrl[CTRL_NVALID] = static_cast<uint32_t>(total);
+    uint32_t* ctrl = p.ws_ctrl + (size_t)prob * CTRL_WORDS;
+    ctrl[CTRL_NCAND] = 0u;
+    ctrl[CTRL_T0] = t0_sh;
   }
 }
 
+// scan: the single pass over the codes; keys >= T0 become candidates.
 template <int S>
-__global__ void __launch_bounds__(kScanThreads) decode_collect_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(kScanThreads, 4) decode_scan_kernel(const DecodeParams p) {
   __shared__ float lut[kMaxLut];
   const int prob = blockIdx.y, seg = blockIdx.x;
   const int h = prob / p.a.n_queries, t = prob - h * p.a.n_queries;
   uint32_t* ctrl = p.ws_ctrl + (size_t)prob * CTRL_WORDS;
-  const uint32_t bstar = __ldcg(ctrl + CTRL_BSTAR);
-  if (bstar >= static_cast<uint32_t>(kBins)) return;
+  const uint32_t t0 = __ldcg(ctrl + CTRL_T0);
   const int SC = p.a.subspaces * p.a.codewords;
   for (int e = threadIdx.x; e < SC; e += blockDim.x) lut[e] = __ldcg(p.ws_lut + (size_t)prob * kMaxLut + e);
   __syncthreads();
   const int64_t len_t = allowed_length(p, t);
+  const int64_t i0 = (int64_t)seg * kScanKeys;
+  const int64_t i1 = min(len_t, i0 + kScanKeys);
+  if (i0 >= i1) return;
   const uint8_t* codes = p.a.codes + h * p.a.codes_head_stride;
-  const int64_t i0 = (int64_t)seg * kSegKeys;
-  const int64_t i1 = min(p.a.key_len, i0 + kSegKeys);
-  int32_t* part = p.ws_part + (size_t)prob * p.sl_cap;
-  uint2* edge = p.ws_edge + (size_t)prob * p.a.key_len;
+  uint2* cand = p.ws_cand + (size_t)prob * p.a.key_len;
   const int lane = threadIdx.x & 31;
   const unsigned lt = (1u << lane) - 1u;
   scan_segment<S>(p, codes, lut, t, len_t, i0, i1, [&](int64_t i, uint32_t key) {
-    const uint32_t bin = key >> 20;
-    const bool above = key != 0u && bin > bstar;
-    const bool on = key != 0u && bin == bstar;
-    const unsigned ba = __ballot_sync(0xFFFFFFFFu, above);
-    const unsigned be = __ballot_sync(0xFFFFFFFFu, on);
-    if ((ba | be) == 0u) return;
-    uint32_t pa = 0, pe = 0;
-    if (lane == 0) {
-      if (ba) pa = atomicAdd(ctrl + CTRL_NOUT, static_cast<uint32_t>(__popc(ba)));
-      if (be) pe = atomicAdd(ctrl + CTRL_NEDGE, static_cast<uint32_t>(__popc(be)));
-    }
-    pa = __shfl_sync(0xFFFFFFFFu, pa, 0);
-    pe = __shfl_sync(0xFFFFFFFFu, pe, 0);
-    if (above) {
-      const uint32_t pos = pa + __popc(ba & lt);
-      if (pos < static_cast<uint32_t>(p.sl_cap)) part[pos] = static_cast<int32_t>(i);
-    }
-    if (on) {
-      const uint32_t pos = pe + __popc(be & lt);
-      if (static_cast<int64_t>(pos) < p.a.key_len) edge[pos] = make_uint2(key, static_cast<uint32_t>(i));
+    const bool take = key != 0u && key >= t0;
+    const unsigned b = __ballot_sync(0xFFFFFFFFu, take);
+    if (b == 0u) return;
+    uint32_t base = 0;
+    if (lane == 0) base = atomicAdd(ctrl + CTRL_NCAND, static_cast<uint32_t>(__popc(b)));
+    base = __shfl_sync(0xFFFFFFFFu, base, 0);
+    if (take) {
+      const uint32_t pos = base + __popc(b & lt);
+      if (static_cast<int64_t>(pos) < p.a.key_len) cand[pos] = make_uint2(key, static_cast<uint32_t>(i));
     }
   });
+}
+
+struct FinishSmem {
+  int qf, ql, lut, sc, scratch, misc, sl, rk, fin, lg, acc, parts, cand, total;
+};
+
+__host__ __device__ inline FinishSmem finish_smem_layout(int head_dim, int sl_cap, int b_cap, int cand_entries) {
+  FinishSmem s;
+  int o = 0;
+  s.qf = o;      o = align16(o + 4 * head_dim);
+  s.ql = o;      o = align16(o + 4 * kMaxRank);
+  s.lut = o;     o = align16(o + 4 * kMaxLut);
+  s.sc = o;      o = align16(o + (int)sizeof(SelectScratch));
+  s.scratch = o; o = align16(o + 4 * 64);
+  s.misc = o;    o = align16(o + 4 * 16);
+  s.sl = o;      o = align16(o + 4 * sl_cap);
+  s.rk = o;      o = align16(o + 4 * sl_cap);
+  s.fin = o;     o = align16(o + 4 * b_cap);
+  s.lg = o;      o = align16(o + 4 * b_cap);
+  s.acc = o;     o = align16(o + 8 * ((kThreads / 32) * 64 + kMaxHeadDim));
+  s.parts = o;   o = align16(o + 8 * kCluster * head_dim);
+  s.cand = o;    o = align16(o + 8 * cand_entries);
+  s.total = o;
+  return s;
+}
+
+// finish: exact shortlist, rescore, budget select and verify for one problem per cluster.
+template <typename T>
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
+    decode_finish_kernel(const DecodeParams p, const FinishSmem lay) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  float* qf = reinterpret_cast<float*>(smem + lay.qf);
+  float* ql = reinterpret_cast<float*>(smem + lay.ql);
+  float* lut = reinterpret_cast<float*>(smem + lay.lut);
+  SelectScratch* sc = reinterpret_cast<SelectScratch*>(smem + lay.sc);
+  int* scratch = reinterpret_cast<int*>(smem + lay.scratch);
+  int* misc = reinterpret_cast<int*>(smem + lay.misc);
+  int32_t* sl = reinterpret_cast<int32_t*>(smem + lay.sl);
+  uint32_t* rk = reinterpret_cast<uint32_t*>(smem + lay.rk);
+  int32_t* fin = reinterpret_cast<int32_t*>(smem + lay.fin);
+  float* lg = reinterpret_cast<float*>(smem + lay.lg);
+  double* acc = reinterpret_cast<double*>(smem + lay.acc);
+  double* parts = reinterpret_cast<double*>(smem + lay.parts);
+  uint2* cand = reinterpret_cast<uint2*>(smem + lay.cand);
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const int crank = static_cast<int>(cluster.block_rank());
+  const int prob = blockIdx.x / kCluster;
+  const int h = prob / p.a.n_queries;
+  const int t = prob - h * p.a.n_queries;
+  const int kvh = h / p.groups;
+  const int64_t L = p.a.key_len;
+  const int64_t len_t = allowed_length(p, t);
+  const int D = p.a.head_dim, R = p.a.rank_dim;
+  const int tid = threadIdx.x;
+
+  {
+    const T* q = reinterpret_cast<const T*>(p.a.query) + h * p.a.q_head_stride + t * p.a.q_row_stride;
+    for (int d = tid; d < D; d += blockDim.x) qf[d] = to_f32<T>(q[d]);
+    for (int r = tid; r < R; r += blockDim.x) ql[r] = __ldcg(p.ws_qlow + (size_t)prob * kMaxRank + r);
+  }
+  __syncthreads();
+
+  // ---- phase 1 (CTA 0): the exact shortlist ------------------------------------------------
+  if (crank == 0) {
+    const uint32_t* ctrl = p.ws_ctrl + (size_t)prob * CTRL_WORDS;
+    const uint32_t t0 = __ldcg(ctrl + CTRL_T0);
+    const int64_t n_cand64 = __ldcg(ctrl + CTRL_NCAND);
+    const int n_cand = static_cast<int>(n_cand64 < L ? n_cand64 : L);
+    int64_t n_allowed = n_cand;
+    if (t0 > 1u && n_cand < p.sl_cap) {
+      if (!p.a.allowed_mask) {
+        n_allowed = len_t;
+      } else {
+        int c = 0;
+        for (int64_t i = tid; i < len_t; i += blockDim.x) c += p.a.allowed_mask[t * p.a.mask_row_stride + i] != 0;
+        n_allowed = block_sum_int(c, scratch);
+      }
+    }
+    const int k = static_cast<int>(imin64(p.sl_cap, n_allowed));
+    const uint2* gc = p.ws_cand + (size_t)prob * L;
+    int n_sl = 0;
+    if (n_cand >= k) {
+      if (n_cand <= kCandSmem) {
+        for (int i = tid; i < n_cand; i += blockDim.x) cand[i] = __ldcg(gc + i);
+        __syncthreads();
+        auto item = [&](int i) -> unsigned long long { return composite(cand[i].x, cand[i].y); };
+        const SelectThreshold thr = cta_radix_select(item, n_cand, k, sc);
+        n_sl = cta_compact(item, n_cand, thr, [&](int pos, int i, unsigned long long) { sl[pos] = cand[i].y; },
+                           scratch);
+      } else {
+        auto item = [&](int i) -> unsigned long long {
+          const uint2 v = __ldcg(gc + i);
+          return composite(v.x, v.y);
+        };
+        const SelectThreshold thr = cta_radix_select(item, n_cand, k, sc);
+        n_sl = cta_compact(item, n_cand, thr,
+                           [&](int pos, int, unsigned long long c) { sl[pos] = static_cast<int32_t>(~static_cast<uint32_t>(c)); },
+                           scratch);
+      }
+    } else {
+      // the sampled threshold was above the k-th best key: exact select over every key
+      for (int e = tid; e < p.a.subspaces * p.a.codewords; e += blockDim.x)
+        lut[e] = __ldcg(p.ws_lut + (size_t)prob * kMaxLut + e);
+      __syncthreads();
+      const uint8_t* codes = p.a.codes + h * p.a.codes_head_stride;
+      auto item = [&](int i) -> unsigned long long {
+        const uint32_t key = adc_key(p, codes, lut, t, i, len_t);
+        return key ? composite(key, static_cast<uint32_t>(i)) : 0ull;
+      };
+      const SelectThreshold thr = cta_radix_select(item, static_cast<int>(len_t), k, sc);
+      n_sl = cta_compact(item, static_cast<int>(len_t), thr, [&](int pos, int i, unsigned long long) { sl[pos] = i; },
+                         scratch);
+      if (p.a.stats && tid == 0) atomicAdd(p.a.stats + SVA_STAT_SELECT_FALLBACKS, 1ull);
+    }
+    if (tid == 0) misc[0] = n_sl;
+  }
+  cluster.sync();
+
+  // ---- phase 2: rescore, split across the cluster -----------------------------------------
+  const int32_t* sl0 = cluster.map_shared_rank(sl, 0);
+  uint32_t* rk0 = cluster.map_shared_rank(rk, 0);
+  const int n_sl = *cluster.map_shared_rank(misc, 0);
+  {
+    const int chunk = (n_sl + kCluster - 1) / kCluster;
+    const int j0 = min(n_sl, crank * chunk);
+    const int j1 = min(n_sl, j0 + chunk);
+    for (int j = j0 + tid; j < j1; j += blockDim.x) sl[j - j0] = sl0[j];
+    __syncthreads();
+    rescore_rows<8>(p, h, ql, sl, j1 - j0, rk);
+    for (int j = j0 + tid; j < j1; j += blockDim.x) rk0[j] = rk[j - j0];
+  }
+  cluster.sync();
+
+  // ---- phase 3 (CTA 0): budget select --------------------------------------------------
+  if (crank == 0) {
+    const int b = min(p.b_cap, n_sl);
+    auto item = [&](int j) -> unsigned long long { return composite(rk[j], static_cast<uint32_t>(sl[j])); };
+    const SelectThreshold thr = cta_radix_select(item, n_sl, b, sc);
+    const int n_fin = cta_compact(item, n_sl, thr, [&](int pos, int j, unsigned long long) { fin[pos] = sl[j]; },
+                                  scratch);
+    if (tid == 0) misc[1] = n_fin;
+  }
+  cluster.sync();
+
+  // ---- phase 4: logits, split -------------------------------------------------------------
+  const int32_t* fin0 = cluster.map_shared_rank(fin, 0);
+  float* lg0 = cluster.map_shared_rank(lg, 0);
+  const int n_fin = *cluster.map_shared_rank(misc + 1, 0);
+  const int fchunk = (n_fin + kCluster - 1) / kCluster;
+  const int f0 = min(n_fin, crank * fchunk);
+  const int f1 = min(n_fin, f0 + fchunk);
+  // rows of this CTA's slice: CTA 0 reads its own final list (f0 == 0), the others copy theirs
+  int32_t* myrows = fin;
+  {
+    if (crank != 0)
+      for (int j = f0 + tid; j < f1; j += blockDim.x) myrows[j - f0] = fin0[j];
+    __syncthreads();
+    float* mylg = reinterpret_cast<float*>(rk);
+    verify_logits<T>(p.a.keys, p.a.k_head_stride, p.a.k_row_stride, kvh, qf, D, myrows, f1 - f0,
+                     p.a.softmax_scale, p.a.logits_mode, mylg);
+    for (int j = f0 + tid; j < f1; j += blockDim.x) lg0[j] = mylg[j - f0];
+  }
+  cluster.sync();
+
+  // ---- phase 5: softmax over all logits (same order in every CTA), weights and partial sums -
+  {
+    float* all = (crank == 0) ? lg : reinterpret_cast<float*>(cand);
+    if (crank != 0)
+      for (int j = tid; j < n_fin; j += blockDim.x) all[j] = lg0[j];
+    __syncthreads();
+    float mx, denom;
+    softmax_stats(all, n_fin, scratch, acc, &mx, &denom);
+    float* w = reinterpret_cast<float*>(rk);
+    for (int j = f0 + tid; j < f1; j += blockDim.x) w[j - f0] = round_to<T>(expf(all[j] - mx) / denom);
+    __syncthreads();
+    double* sums = acc + (kThreads / 32) * 64;
+    accumulate_rows<T>(p.a.values, p.a.v_head_stride, p.a.v_row_stride, kvh, D, myrows, w, f1 - f0, acc, sums);
+    double* parts0 = cluster.map_shared_rank(parts, 0);
+    for (int d = tid; d < D; d += blockDim.x) parts0[crank * D + d] = sums[d];
+  }
+  cluster.sync();
+
+  // ---- phase 6 (CTA 0): merge, outputs, counters ------------------------------------------
+  if (crank == 0) {
+    T* out = reinterpret_cast<T*>(p.a.out) + h * p.a.out_head_stride + t * p.a.out_row_stride;
+    for (int d = tid; d < D; d += blockDim.x) {
+      double tot = 0.0;
+      for (int c = 0; c < kCluster; ++c) tot += parts[c * D + d];
+      out[d] = from_f32<T>(n_fin > 0 ? static_cast<float>(tot) : 0.f);
+    }
+    unsigned long long* tmp = reinterpret_cast<unsigned long long*>(cand);
+    if (p.a.shortlist_out) write_sorted(sl, n_sl, p.a.shortlist, p.a.shortlist_out + (size_t)prob * p.a.shortlist, tmp);
+    if (p.a.final_out) write_sorted(fin, n_fin, p.a.budget, p.a.final_out + (size_t)prob * p.a.budget, tmp);
+    if (p.a.stats && tid == 0) {
+      atomicAdd(p.a.stats + SVA_STAT_QUERIES, 1ull);
+      atomicAdd(p.a.stats + SVA_STAT_SUMMONED, static_cast<unsigned long long>(n_sl));
+      atomicAdd(p.a.stats + SVA_STAT_EXACT_SCORED, static_cast<unsigned long long>(n_fin));
+      atomicAdd(p.a.stats + SVA_STAT_VERIFIED, static_cast<unsigned long long>(n_fin));
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------------------
@@ -539,6 +653,7 @@ static bool pow2_float(double x) {
 
 struct DecodePlan {
   DecodeParams p;
+  FinishSmem fin_lay;
   size_t ws_bytes;
   size_t smem_bytes;
 };
@@ -581,80 +696,75 @@ static int plan_decode(const sva_decode_args* a, DecodePlan* plan) {
                     : 0;
   const int64_t P = static_cast<int64_t>(a->n_heads) * a->n_queries;
   p.grid_mode = a->key_len > kFusedMaxKeys ? 1 : 0;
-  p.nseg = static_cast<int>((a->key_len + kSegKeys - 1) / kSegKeys);
-  const int stage_bytes = 4 * a->head_dim * a->rank_dim;
-  int cache_bytes = p.grid_mode ? 8 * kEdgeSmem : std::max<int>(static_cast<int>(4 * a->key_len), stage_bytes);
-  // debug outputs reuse the cache region for a 64-bit sort of up to pow2(shortlist) entries
-  if (a->shortlist_out || a->final_out) {
-    int cap = 1;
-    while (cap < p.sl_cap) cap <<= 1;
-    cache_bytes = std::max(cache_bytes, 8 * cap);
-  }
-  p.lay = decode_smem_layout(a->head_dim, p.sl_cap, p.b_cap, cache_bytes);
-  plan->smem_bytes = static_cast<size_t>(p.lay.total);
-  if (plan->smem_bytes > static_cast<size_t>(kMaxDynSmem)) return set_error(SVA_ERR_SHAPE, "shared memory plan exceeds 227 KB");
+  p.nseg = static_cast<int>((a->key_len + kScanKeys - 1) / kScanKeys);
+  int dbg_cap = 1;
+  if (a->shortlist_out || a->final_out)
+    while (dbg_cap < p.sl_cap) dbg_cap <<= 1;
   size_t ws = 0;
-  if (p.grid_mode) {
+  if (!p.grid_mode) {
+    const int stage_bytes = 4 * a->head_dim * a->rank_dim;
+    int cache_bytes = std::max<int>(static_cast<int>(4 * a->key_len), stage_bytes);
+    cache_bytes = std::max(cache_bytes, 8 * dbg_cap);
+    p.lay = decode_smem_layout(a->head_dim, p.sl_cap, p.b_cap, cache_bytes);
+    plan->smem_bytes = static_cast<size_t>(p.lay.total);
+  } else {
+    const int cand_entries = std::max(kCandSmem, dbg_cap);
+    plan->fin_lay = finish_smem_layout(a->head_dim, p.sl_cap, p.b_cap, cand_entries);
+    plan->smem_bytes = static_cast<size_t>(plan->fin_lay.total);
     auto take = [&](size_t bytes) {
       size_t o = ws;
       ws = (ws + bytes + 255) & ~static_cast<size_t>(255);
       return o;
     };
-    const size_t o_ql = take(sizeof(float) * kMaxRank * P);
-    const size_t o_lut = take(sizeof(float) * kMaxLut * P);
-    const size_t o_hist = take(sizeof(uint32_t) * kBins * P);
-    const size_t o_ctrl = take(sizeof(uint32_t) * CTRL_WORDS * P);
-    const size_t o_part = take(sizeof(int32_t) * p.sl_cap * P);
-    const size_t o_edge = take(sizeof(uint2) * static_cast<size_t>(a->key_len) * P);
-    p.ws_qlow = reinterpret_cast<float*>(o_ql);
-    p.ws_lut = reinterpret_cast<float*>(o_lut);
-    p.ws_hist = reinterpret_cast<uint32_t*>(o_hist);
-    p.ws_ctrl = reinterpret_cast<uint32_t*>(o_ctrl);
-    p.ws_part = reinterpret_cast<int32_t*>(o_part);
-    p.ws_edge = reinterpret_cast<uint2*>(o_edge);
+    p.ws_qlow = reinterpret_cast<float*>(take(sizeof(float) * kMaxRank * P));
+    p.ws_lut = reinterpret_cast<float*>(take(sizeof(float) * kMaxLut * P));
+    p.ws_ctrl = reinterpret_cast<uint32_t*>(take(sizeof(uint32_t) * CTRL_WORDS * P));
+    p.ws_cand = reinterpret_cast<uint2*>(take(sizeof(uint2) * static_cast<size_t>(a->key_len) * P));
   }
+  if (plan->smem_bytes > static_cast<size_t>(kMaxDynSmem)) return set_error(SVA_ERR_SHAPE, "shared memory plan exceeds 227 KB");
   plan->ws_bytes = ws;
   return SVA_OK;
 }
 
 template <int S>
-static void launch_scan_kernels(const DecodeParams& p, int P, cudaStream_t stream) {
-  dim3 grid(p.nseg, P);
-  decode_hist_kernel<S><<<grid, kScanThreads, 0, stream>>>(p);
-  profile_mark(1, stream);
-  decode_collect_kernel<S><<<grid, kScanThreads, 0, stream>>>(p);
-  profile_mark(2, stream);
+static void launch_scan(const DecodeParams& p, int P, cudaStream_t stream) {
+  decode_scan_kernel<S><<<dim3(p.nseg, P), kScanThreads, 0, stream>>>(p);
 }
 
 template <typename T>
 static int launch_decode(DecodePlan& plan, void* ws, cudaStream_t stream) {
   DecodeParams& p = plan.p;
   const int P = p.a.n_heads * p.a.n_queries;
-  if (p.grid_mode) {
+  int rc;
+  if (!p.grid_mode) {
+    rc = ensure_smem_attr(reinterpret_cast<const void*>(decode_fused_kernel<T>), kMaxDynSmem);
+    if (rc != SVA_OK) return rc;
+    decode_fused_kernel<T><<<P, kThreads, plan.smem_bytes, stream>>>(p);
+    profile_mark(0, stream);
+  } else {
     char* base = static_cast<char*>(ws);
     p.ws_qlow = reinterpret_cast<float*>(base + reinterpret_cast<size_t>(p.ws_qlow));
     p.ws_lut = reinterpret_cast<float*>(base + reinterpret_cast<size_t>(p.ws_lut));
-    p.ws_hist = reinterpret_cast<uint32_t*>(base + reinterpret_cast<size_t>(p.ws_hist));
     p.ws_ctrl = reinterpret_cast<uint32_t*>(base + reinterpret_cast<size_t>(p.ws_ctrl));
-    p.ws_part = reinterpret_cast<int32_t*>(base + reinterpret_cast<size_t>(p.ws_part));
-    p.ws_edge = reinterpret_cast<uint2*>(base + reinterpret_cast<size_t>(p.ws_edge));
-    const int stage = 4 * p.a.head_dim * p.a.rank_dim;
-    int rc = ensure_smem_attr(reinterpret_cast<const void*>(decode_qlut_kernel<T>), kMaxDynSmem - 16 * 1024);
+    p.ws_cand = reinterpret_cast<uint2*>(base + reinterpret_cast<size_t>(p.ws_cand));
+    const int prep_smem = std::max(4 * p.a.head_dim * p.a.rank_dim, 4 * kSample);
+    rc = ensure_smem_attr(reinterpret_cast<const void*>(decode_prep_kernel<T>), prep_smem);
     if (rc != SVA_OK) return rc;
-    decode_qlut_kernel<T><<<P, 256, stage, stream>>>(p);
+    decode_prep_kernel<T><<<P, kThreads, prep_smem, stream>>>(p);
     profile_mark(0, stream);
     switch (p.vec_codes ? p.a.subspaces : 0) {
-      case 1: launch_scan_kernels<1>(p, P, stream); break;
-      case 2: launch_scan_kernels<2>(p, P, stream); break;
-      case 4: launch_scan_kernels<4>(p, P, stream); break;
-      case 8: launch_scan_kernels<8>(p, P, stream); break;
-      default: launch_scan_kernels<0>(p, P, stream); break;
+      case 1: launch_scan<1>(p, P, stream); break;
+      case 2: launch_scan<2>(p, P, stream); break;
+      case 4: launch_scan<4>(p, P, stream); break;
+      case 8: launch_scan<8>(p, P, stream); break;
+      default: launch_scan<0>(p, P, stream); break;
     }
+    profile_mark(1, stream);
+    rc = ensure_smem_attr(reinterpret_cast<const void*>(decode_finish_kernel<T>), static_cast<int>(plan.smem_bytes));
+    if (rc != SVA_OK) return rc;
+    decode_finish_kernel<T><<<P * kCluster, kThreads, plan.smem_bytes, stream>>>(p, plan.fin_lay);
+    profile_mark(2, stream);
   }
-  int rc = ensure_smem_attr(reinterpret_cast<const void*>(decode_problem_kernel<T>), kMaxDynSmem);
-  if (rc != SVA_OK) return rc;
-  decode_problem_kernel<T><<<P, kThreads, plan.smem_bytes, stream>>>(p);
-  profile_mark(p.grid_mode ? 3 : 0, stream);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
   return SVA_OK;

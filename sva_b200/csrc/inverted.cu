@@ -212,7 +212,7 @@ __global__ void __launch_bounds__(kInvScoreThreads) inv_score_kernel(const InvPa
       const int64_t slot = e - seg[lo];
       const size_t hs = (size_t)h * S + s;
       key = __ldg(a.post_ids + hs * a.post_ids_sub_stride + __ldg(a.post_offsets + hs * (C + 1) + c) + slot);
-      valid = key < a.allowed_len && key < L && key < a.postings_len;
+      valid = key < a.allowed_len && key < L && key < a.postings_len && (!a.allowed_mask || a.allowed_mask[key]);
       if (valid) {
         first = true;
         for (int s2 = 0; s2 < S; ++s2) {
@@ -225,7 +225,7 @@ __global__ void __launch_bounds__(kInvScoreThreads) inv_score_kernel(const InvPa
     } else if (e < e_total) {
       if (current) {
         key = L - 1;
-        valid = key >= 0 && key < a.allowed_len;
+        valid = key >= 0 && key < a.allowed_len && (!a.allowed_mask || a.allowed_mask[key]);
         if (valid) {
           int in = 0;
           if (key < a.postings_len)
@@ -235,7 +235,7 @@ __global__ void __launch_bounds__(kInvScoreThreads) inv_score_kernel(const InvPa
         }
       } else {
         key = tail_start + (e - e_post);
-        valid = key < a.allowed_len;
+        valid = key < a.allowed_len && (!a.allowed_mask || a.allowed_mask[key]);
         first = valid;
         m = 1;
       }
@@ -383,7 +383,7 @@ __host__ __device__ inline InvSmem inv_final_layout(int head_dim, int budget_pow
   s.tmp = o;     o = inv_align(o + 8 * kInvEdgeCap);
   s.fin = o;     o = inv_align(o + 4 * budget_pow2);
   s.lg = o;      o = inv_align(o + 4 * budget_pow2);
-  s.acc = o;     o = inv_align(o + 8 * ((kInvThreads / 32) * 64 + kInvThreads / 32 + 1));
+  s.acc = o;     o = inv_align(o + 8 * ((kInvThreads / 32) * 64 + kMaxHeadDim));
   s.total = o;
   return s;
 }

@@ -1,68 +1,82 @@
 // Exact verify over selected keys, shared by the scan and inverted decode kernels
 // (replaces sva/llama.py:304-317 and :532-553).
 //
-// logits: q . K[key] * softmax_scale, one half-warp per key row (16 lanes x 4 elements per
-//         64-wide chunk, tree order).  logits_mode 1 reproduces the reference scan path for
-//         bf16 / fp16 models: every product rounded to the value dtype, the sum rounded, the
-//         scaled logit rounded.  logits_mode 0 keeps fp32 logits (static path, benchmark).
+// logits : q . K[key] * softmax_scale, one half-warp per key row (16 lanes x 4 elements per
+//          64-wide chunk, tree order).  logits_mode 1 reproduces the reference scan path for
+//          bf16 / fp16 models: every product rounded to the value dtype, the sum rounded, the
+//          scaled logit rounded.  logits_mode 0 keeps fp32 logits (static path, benchmark).
 // softmax: fp32 max, fp64 denominator; weights rounded to the value dtype (the reference casts
-//         the fp32 softmax to the query dtype).
-// output: sum_j round(w_j * V[j]) accumulated in fp64 (exact for bf16 products, so the result
-//         does not depend on the order of the selected keys), rounded to the value dtype.
+//          the fp32 softmax to the query dtype).
+// output : sum_j round(w_j * V[j]) accumulated in fp64 (exact for bf16 products, so the result
+//          does not depend on the order of the selected keys or on how rows are split between
+//          CTAs), rounded to the value dtype.
+// Every function is block-cooperative and ends with a barrier.
 #pragma once
 
 #include "sva_common.cuh"
 
 namespace sva {
 
-// Shared-memory need: lg[n_fin] floats; acc[(nwarps * 64) + nwarps + 1] doubles; scratch[64] ints.
+constexpr int kVerifyUnroll = 8;
+
 template <typename T>
-__device__ void verify_rows(const void* keys, int64_t k_head_stride, int64_t k_row_stride, const void* values,
-                            int64_t v_head_stride, int64_t v_row_stride, int kvh, const float* qf, int D,
-                            const int32_t* fin, int n_fin, float softmax_scale, int logits_mode, float* lg,
-                            double* acc, int* scratch, T* out) {
+__device__ void verify_logits(const void* keys, int64_t k_head_stride, int64_t k_row_stride, int kvh, const float* qf,
+                              int D, const int32_t* rows, int n, float softmax_scale, int logits_mode, float* lg) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   const int half = lane >> 4, l16 = lane & 15;
   const T* kb = reinterpret_cast<const T*>(keys) + kvh * k_head_stride;
-  const T* vb = reinterpret_cast<const T*>(values) + kvh * v_head_stride;
-  constexpr int U = 4;
-  for (int base = warp * 2 * U; base < n_fin; base += nwarps * 2 * U) {
+  constexpr int U = kVerifyUnroll;
+  for (int base = warp * 2 * U; base < n; base += nwarps * 2 * U) {
+    float part[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) part[u] = 0.f;
+    for (int c0 = 0; c0 < D; c0 += 64) {
+      const int e = c0 + 4 * l16;
+      float4 k4[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int j = base + 2 * u + half;
+        k4[u] = (j < n && e < D) ? load4<T>(kb + (int64_t)rows[j] * k_row_stride, e, D) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      const float4 qv = (e < D) ? make_float4(qf[e], (e + 1 < D) ? qf[e + 1] : 0.f, (e + 2 < D) ? qf[e + 2] : 0.f,
+                                              (e + 3 < D) ? qf[e + 3] : 0.f)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (logits_mode == 1) {
+          float s = round_to<T>(__fmul_rn(k4[u].x, qv.x));
+          s = __fadd_rn(s, round_to<T>(__fmul_rn(k4[u].y, qv.y)));
+          s = __fadd_rn(s, round_to<T>(__fmul_rn(k4[u].z, qv.z)));
+          s = __fadd_rn(s, round_to<T>(__fmul_rn(k4[u].w, qv.w)));
+          part[u] = __fadd_rn(part[u], s);
+        } else {
+          part[u] = __fadd_rn(part[u], lane4(k4[u], qv));
+        }
+      }
+    }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int j = base + 2 * u + half;
-      const bool ok = j < n_fin;
-      const T* krow = ok ? kb + (int64_t)fin[j] * k_row_stride : nullptr;
-      float part = 0.f;
-      for (int c0 = 0; c0 < D; c0 += 64) {
-        const int e = c0 + 4 * l16;
-        if (!ok || e >= D) continue;
-        const float4 k4 = load4<T>(krow, e, D);
-        const float4 qv = make_float4(qf[e], (e + 1 < D) ? qf[e + 1] : 0.f, (e + 2 < D) ? qf[e + 2] : 0.f,
-                                      (e + 3 < D) ? qf[e + 3] : 0.f);
-        if (logits_mode == 1) {
-          float s = round_to<T>(__fmul_rn(k4.x, qv.x));
-          s = __fadd_rn(s, round_to<T>(__fmul_rn(k4.y, qv.y)));
-          s = __fadd_rn(s, round_to<T>(__fmul_rn(k4.z, qv.z)));
-          s = __fadd_rn(s, round_to<T>(__fmul_rn(k4.w, qv.w)));
-          part = __fadd_rn(part, s);
-        } else {
-          part = __fadd_rn(part, lane4(k4, qv));
-        }
-      }
-      float s = tree16(part);
+      float s = tree16(part[u]);
       if (logits_mode == 1) {
         s = round_to<T>(s);
         s = round_to<T>(__fmul_rn(s, softmax_scale));
       } else {
         s = __fmul_rn(s, softmax_scale);
       }
-      if (ok && l16 == 0) lg[j] = s;
+      if (j < n && l16 == 0) lg[j] = s;
     }
   }
   __syncthreads();
+}
 
+// Max (fp32) and fp64 denominator of softmax over lg[0, n); every thread gets both.
+// `red` needs (blockDim.x / 32 + 1) doubles, `scratch` 33 ints.
+__device__ inline void softmax_stats(const float* lg, int n, int* scratch, double* red, float* mx_out,
+                                     float* denom_out) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   float mx = -INFINITY;
-  for (int j = tid; j < n_fin; j += blockDim.x) mx = fmaxf(mx, lg[j]);
+  for (int j = tid; j < n; j += blockDim.x) mx = fmaxf(mx, lg[j]);
   mx = warp_max(mx);
   float* redf = reinterpret_cast<float*>(scratch);
   if (lane == 0) redf[warp] = mx;
@@ -75,45 +89,61 @@ __device__ void verify_rows(const void* keys, int64_t k_head_stride, int64_t k_r
   __syncthreads();
   mx = redf[32];
   double se = 0.0;
-  for (int j = tid; j < n_fin; j += blockDim.x) se += static_cast<double>(expf(lg[j] - mx));
+  for (int j = tid; j < n; j += blockDim.x) se += static_cast<double>(expf(lg[j] - mx));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) se += __shfl_xor_sync(0xFFFFFFFFu, se, o);
-  if (lane == 0) acc[warp] = se;
+  if (lane == 0) red[warp] = se;
   __syncthreads();
   if (tid == 0) {
     double tot = 0.0;
-    for (int w = 0; w < nwarps; ++w) tot += acc[w];
-    acc[nwarps] = tot;
+    for (int w = 0; w < nwarps; ++w) tot += red[w];
+    red[nwarps] = tot;
   }
   __syncthreads();
-  const float denom = static_cast<float>(acc[nwarps]);
+  *mx_out = mx;
+  *denom_out = static_cast<float>(red[nwarps]);
   __syncthreads();
-  for (int j = tid; j < n_fin; j += blockDim.x) lg[j] = round_to<T>(expf(lg[j] - mx) / denom);
-  __syncthreads();
+}
 
+// w[j] = round_T(exp(lg[j] - mx) / denom) for j in [0, n), in place.
+template <typename T>
+__device__ void softmax_weights(float* lg, int n, float mx, float denom) {
+  for (int j = threadIdx.x; j < n; j += blockDim.x) lg[j] = round_to<T>(expf(lg[j] - mx) / denom);
+  __syncthreads();
+}
+
+// out[d] = sum_j round_T(w[j] * V[rows[j]][d]) in fp64 for d < D (written by threads 0..63 per
+// 64-wide chunk).  `acc` needs (blockDim.x / 32) * 64 doubles.
+template <typename T>
+__device__ void accumulate_rows(const void* values, int64_t v_head_stride, int64_t v_row_stride, int kvh, int D,
+                                const int32_t* rows, const float* w, int n, double* acc, double* out) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  const int half = lane >> 4, l16 = lane & 15;
+  const T* vb = reinterpret_cast<const T*>(values) + kvh * v_head_stride;
+  constexpr int U = kVerifyUnroll;
   const int nchunks = (D + 63) / 64;
   for (int c = 0; c < nchunks; ++c) {
     const int e = c * 64 + 4 * l16;
     double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
-    for (int base = warp * 2 * U; base < n_fin; base += nwarps * 2 * U) {
+    for (int base = warp * 2 * U; base < n; base += nwarps * 2 * U) {
       float4 v[U];
-      float w[U];
+      float wu[U];
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int j = base + 2 * u + half;
         v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-        w[u] = 0.f;
-        if (j < n_fin && e < D) {
-          v[u] = load4<T>(vb + (int64_t)fin[j] * v_row_stride, e, D);
-          w[u] = lg[j];
+        wu[u] = 0.f;
+        if (j < n && e < D) {
+          v[u] = load4<T>(vb + (int64_t)rows[j] * v_row_stride, e, D);
+          wu[u] = w[j];
         }
       }
 #pragma unroll
       for (int u = 0; u < U; ++u) {
-        a0 += static_cast<double>(round_to<T>(__fmul_rn(w[u], v[u].x)));
-        a1 += static_cast<double>(round_to<T>(__fmul_rn(w[u], v[u].y)));
-        a2 += static_cast<double>(round_to<T>(__fmul_rn(w[u], v[u].z)));
-        a3 += static_cast<double>(round_to<T>(__fmul_rn(w[u], v[u].w)));
+        a0 += static_cast<double>(round_to<T>(__fmul_rn(wu[u], v[u].x)));
+        a1 += static_cast<double>(round_to<T>(__fmul_rn(wu[u], v[u].y)));
+        a2 += static_cast<double>(round_to<T>(__fmul_rn(wu[u], v[u].z)));
+        a3 += static_cast<double>(round_to<T>(__fmul_rn(wu[u], v[u].w)));
       }
     }
     a0 += __shfl_xor_sync(0xFFFFFFFFu, a0, 16);
@@ -131,10 +161,28 @@ __device__ void verify_rows(const void* keys, int64_t k_head_stride, int64_t k_r
     if (tid < 64 && c * 64 + tid < D) {
       double tot = 0.0;
       for (int w2 = 0; w2 < nwarps; ++w2) tot += acc[w2 * 64 + tid];
-      out[c * 64 + tid] = from_f32<T>(n_fin > 0 ? static_cast<float>(tot) : 0.f);
+      out[c * 64 + tid] = tot;
     }
     __syncthreads();
   }
+}
+
+// The whole verify inside one CTA.  Shared memory: lg[n_fin] floats; acc[(nwarps * 64) +
+// nwarps + 1] doubles; red[kMaxHeadDim] doubles for the output sums; scratch[64] ints.
+template <typename T>
+__device__ void verify_rows(const void* keys, int64_t k_head_stride, int64_t k_row_stride, const void* values,
+                            int64_t v_head_stride, int64_t v_row_stride, int kvh, const float* qf, int D,
+                            const int32_t* fin, int n_fin, float softmax_scale, int logits_mode, float* lg,
+                            double* acc, int* scratch, T* out) {
+  verify_logits<T>(keys, k_head_stride, k_row_stride, kvh, qf, D, fin, n_fin, softmax_scale, logits_mode, lg);
+  float mx, denom;
+  const int nwarps = blockDim.x >> 5;
+  softmax_stats(lg, n_fin, scratch, acc, &mx, &denom);
+  softmax_weights<T>(lg, n_fin, mx, denom);
+  double* sums = acc + nwarps * 64;  // D doubles after the per-warp partials
+  accumulate_rows<T>(values, v_head_stride, v_row_stride, kvh, D, fin, lg, n_fin, acc, sums);
+  for (int d = threadIdx.x; d < D; d += blockDim.x) out[d] = from_f32<T>(n_fin > 0 ? static_cast<float>(sums[d]) : 0.f);
+  __syncthreads();
 }
 
 }  // namespace sva

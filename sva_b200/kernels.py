@@ -231,7 +231,8 @@ def decode_inverted(q: torch.Tensor, q_proj: torch.Tensor, scale: torch.Tensor, 
                     codes: torch.Tensor, postings: Postings, k_low: torch.Tensor, keys: torch.Tensor,
                     values: torch.Tensor, budget: int, cells: int, min_budget: int, mid_budget: int,
                     low_margin: float = 0.35, high_margin: float = 0.70, dynamic: bool = False,
-                    refill_factor: int = 2, allowed_len: int | None = None, softmax_scale: float | None = None,
+                    refill_factor: int = 2, allowed_len: int | None = None, allowed_mask: torch.Tensor | None = None,
+                    softmax_scale: float | None = None,
                     out: torch.Tensor | None = None, want_selection: bool = False, stats: torch.Tensor | None = None):
     """Inverted-index decode of one token per head (reference sva/llama.py:427-576 / :330-425).
 
@@ -256,6 +257,7 @@ def decode_inverted(q: torch.Tensor, q_proj: torch.Tensor, scale: torch.Tensor, 
     a.key_len = key_len
     a.postings_len = postings.key_len
     a.allowed_len = key_len if allowed_len is None else int(allowed_len)
+    a.allowed_mask = _ptr(allowed_mask)
     a.query, a.q_head_stride = q.data_ptr(), q.stride(0)
     a.q_proj, a.scale, a.codebooks = q_proj.data_ptr(), scale.data_ptr(), codebooks.data_ptr()
     a.codes, a.codes_head_stride = codes.data_ptr(), codes.stride(0)
