@@ -342,7 +342,8 @@ def gpu_arm(args):
         one_query(st)
     torch.cuda.synchronize()
 
-    n_prof = 4
+    grid_schedule = local_keys > 32768
+    n_prof = 3 if grid_schedule else 1
     prof = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(n_prof + 1)]
     for e in prof:  # torch creates the CUDA event on its first record
         e.record()
@@ -403,16 +404,22 @@ def gpu_arm(args):
     us_query = 1000.0 * ms_step / qps
 
     # per-kernel timing (first query of every replay)
-    names = ["qlut", "summon_hist", "summon_collect", "rescore_verify"]
-    kmeans = [sum(k[j] for k in kern) / len(kern) for j in range(n_prof)]
     ab = algorithmic_bytes(args)
     local_frac = local_keys / args.keys
-    kernel_bytes = {
-        "qlut": (ab["codebooks"] + ab["q_proj"]),
-        "summon_hist": ab["codes"] * local_frac,
-        "summon_collect": ab["codes"] * local_frac,
-        "rescore_verify": ab["rescore"] + ab["verify"] + ab["codebooks"] + ab["q_proj"],
-    }
+    if grid_schedule:
+        names = ["prep", "scan", "finish"]
+        kernel_bytes = {
+            # prep reads the projections and codebooks (and a 4096-key sample of the codes)
+            "prep": ab["codebooks"] + ab["q_proj"],
+            # scan is the single pass over the codes
+            "scan": ab["codes"] * local_frac,
+            # finish gathers the shortlist's k_low rows and the budget's K and V rows
+            "finish": ab["rescore"] + ab["verify"],
+        }
+    else:
+        names = ["fused"]
+        kernel_bytes = {"fused": ab["total"] * local_frac}
+    kmeans = [sum(k[j] for k in kern) / len(kern) for j in range(n_prof)]
     dom = max(range(n_prof), key=lambda j: kmeans[j])
     peak, peak_kind = measured_peaks()
     achieved = kernel_bytes[names[dom]] / (kmeans[dom] * 1e-3) / 1e9
@@ -443,7 +450,7 @@ def gpu_arm(args):
                        "ms_per_set": round(build_ms / args.sets, 3)},
         "wall_s_timed": round(wall, 3),
     }
-    launches_per_query = 4 if local_keys > 32768 else 1
+    launches_per_query = 3 if grid_schedule else 1
     if world > 1:
         launches_per_query += shard.extra_launches
     line["gpu_launches"] = launches_per_query * qps * args.steps

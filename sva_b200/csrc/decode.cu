@@ -224,6 +224,26 @@ __device__ void rescore_rows(const DecodeParams& p, int h, const float* ql, cons
   __syncthreads();
 }
 
+// Block copy of n uint2 from global to shared memory with 8 loads in flight per thread; ends
+// with a barrier.
+__device__ inline void copy_batched(uint2* dst, const uint2* src, int n) {
+  constexpr int U = 8;
+  for (int base = 0; base < n; base += blockDim.x * U) {
+    uint2 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + threadIdx.x + u * blockDim.x;
+      if (i < n) v[u] = __ldcg(src + i);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + threadIdx.x + u * blockDim.x;
+      if (i < n) dst[i] = v[u];
+    }
+  }
+  __syncthreads();
+}
+
 // Ascending copies of the shortlist / final index sets for the debug outputs.
 __device__ void write_sorted(const int32_t* src, int n, int width, int32_t* dst, unsigned long long* tmp) {
   int cap = 1;
@@ -350,73 +370,140 @@ __device__ __forceinline__ void scan_segment(const DecodeParams& p, const uint8_
   }
 }
 
-// prep: q_low + LUT, and the sampled threshold T0.
+// prep: q_low + LUT, and the sampled threshold T0 (an ordered key; 1 = every allowed key).
+// The sample is kSampleRuns evenly spaced runs of kSampleRunKeys keys over the allowed range;
+// T0 is the lower edge of the 12-bit key bin holding the sample's r-th best key, with r chosen
+// so that about 3x the shortlist is expected at or above it.
 template <typename T>
 __global__ void __launch_bounds__(kThreads) decode_prep_kernel(const DecodeParams p) {
   extern __shared__ __align__(16) unsigned char dyn[];
   __shared__ float qf[kMaxHeadDim];
   __shared__ float ql[kMaxRank];
   __shared__ float lut[kMaxLut];
-  __shared__ SelectScratch sc;
   __shared__ int scratch[64];
+  __shared__ int wtot[kThreads / 32];
   __shared__ uint32_t t0_sh;
   float* stage = reinterpret_cast<float*>(dyn);
   const int prob = blockIdx.x;
   const int h = prob / p.a.n_queries, t = prob - h * p.a.n_queries;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   build_qlut<T>(p, h, t, qf, ql, lut, stage);
   const int SC = p.a.subspaces * p.a.codewords;
   float* gl = p.ws_lut + (size_t)prob * kMaxLut;
   for (int e = tid; e < SC; e += blockDim.x) gl[e] = lut[e];
   for (int r = tid; r < p.a.rank_dim; r += blockDim.x) p.ws_qlow[(size_t)prob * kMaxRank + r] = ql[r];
-  // sample: kSampleRuns evenly spaced runs of kSampleRunKeys keys over the allowed range
-  uint32_t* samp = reinterpret_cast<uint32_t*>(dyn);  // the stage is no longer needed
   const int64_t len_t = allowed_length(p, t);
   const uint8_t* codes = p.a.codes + h * p.a.codes_head_stride;
-  int nv = 0;
-  for (int e = tid; e < kSample; e += blockDim.x) {
-    const int run = e / kSampleRunKeys, off = e - run * kSampleRunKeys;
-    const int64_t i = (len_t * run) / kSampleRuns + off;
-    const uint32_t key = (i < len_t) ? adc_key(p, codes, lut, t, i, len_t) : 0u;
-    samp[e] = key;
-    nv += key != 0u;
+  // each thread scores kSample / kThreads keys; all code loads are issued before any is used
+  constexpr int kPer = kSample / kThreads;
+  uint32_t key[kPer];
+  {
+    uint8_t cb[kPer][kMaxSubspaces];
+    const int S = p.a.subspaces;
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      const int e = tid + u * kThreads;
+      const int run = e / kSampleRunKeys, off = e - run * kSampleRunKeys;
+      const int64_t i = (len_t * run) / kSampleRuns + off;
+      for (int s2 = 0; s2 < kMaxSubspaces; ++s2) cb[u][s2] = (i < len_t && s2 < S) ? __ldg(codes + i * S + s2) : 0;
+    }
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      const int e = tid + u * kThreads;
+      const int run = e / kSampleRunKeys, off = e - run * kSampleRunKeys;
+      const int64_t i = (len_t * run) / kSampleRuns + off;
+      key[u] = 0u;
+      if (key_allowed(p, t, i, len_t)) {
+        float sum = 0.f;
+        for (int s2 = 0; s2 < S; ++s2) sum = __fadd_rn(sum, lut[s2 * p.a.codewords + cb[u][s2]]);
+        key[u] = ordered_key(finish_score(sum, p));
+      }
+    }
   }
+  uint32_t* hist = reinterpret_cast<uint32_t*>(dyn);  // 4096 bins; the stage is no longer needed
+  for (int b = tid; b < 4096; b += blockDim.x) hist[b] = 0u;
+  __syncthreads();
+  int nv = 0;
+#pragma unroll
+  for (int u = 0; u < kPer; ++u)
+    if (key[u]) {
+      atomicAdd(&hist[key[u] >> 20], 1u);
+      ++nv;
+    }
   const int n_s = block_sum_int(nv, scratch);
   const int64_t k_est = imin64(p.sl_cap, len_t);
-  // about 3x the shortlist above the threshold, plus a margin for small samples
   const int64_t r = (3 * k_est * n_s + len_t - 1) / (len_t > 0 ? len_t : 1) + 8;
-  const bool sampled = n_s > 0 && r < n_s;
-  if (tid == 0) t0_sh = sampled ? 0xFFFFFFFFu : 1u;  // 1: every allowed key is a candidate
+  if (tid == 0) t0_sh = 1u;
   __syncthreads();
-  if (sampled) {
-    auto item = [&](int i) -> unsigned long long { return samp[i] ? composite(samp[i], static_cast<uint32_t>(i)) : 0ull; };
-    const SelectThreshold thr = cta_radix_select(item, kSample, static_cast<int>(r), &sc);
-    // T0 = smallest key among the r best samples
-    uint32_t mn = 0xFFFFFFFFu;
-    for (int e = tid; e < kSample; e += blockDim.x)
-      if (is_selected(thr, item(e))) mn = min(mn, samp[e]);
+  if (n_s > 0 && r < n_s) {
+    // thread j owns bins 4095-8j .. 4088-8j (descending); find the bin holding the r-th best
+    uint32_t mine[8];
+    int c = 0;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mn = min(mn, __shfl_xor_sync(0xFFFFFFFFu, mn, o));
-    if ((tid & 31) == 0) atomicMin(&t0_sh, mn);
+    for (int q = 0; q < 8; ++q) {
+      mine[q] = hist[4095 - (8 * tid + q)];
+      c += static_cast<int>(mine[q]);
+    }
+    int incl = warp_incl_scan(c);
+    if (lane == 31) wtot[warp] = incl;
+    __syncthreads();
+    for (int w = 0; w < warp; ++w) incl += wtot[w];
+    const int excl = incl - c;
+    if (excl < r && incl >= r) {
+      int run = excl;
+      for (int q = 0; q < 8; ++q) {
+        run += static_cast<int>(mine[q]);
+        if (run >= r) {
+          t0_sh = static_cast<uint32_t>(4095 - (8 * tid + q)) << 20;
+          break;
+        }
+      }
+    }
   }
   __syncthreads();
   if (tid == 0) {
     uint32_t* ctrl = p.ws_ctrl + (size_t)prob * CTRL_WORDS;
     ctrl[CTRL_NCAND] = 0u;
-    ctrl[CTRL_T0] = t0_sh;
+    ctrl[CTRL_T0] = t0_sh > 1u ? t0_sh : 1u;
   }
 }
 
-// scan: the single pass over the codes; keys >= T0 become candidates.
-template <int S>
+// scan: the single pass over the codes; keys >= T0 become candidates.  Specialised on the code
+// shape: S bytes per key and C codewords (C == 0: any).  For 4x64 the first two subspaces are
+// looked up in a pair table pair[c1][c0] = lut0[c0] + lut1[c1], the same fp32 sum as the
+// sequential accumulation.  Scores are compared with the threshold as floats; the ordered key
+// is computed only for the keys that are taken.
+template <int S, int C>
+__device__ __forceinline__ float adc_fast(const Codes4<S>& c, int j, const float* lut, const float* pair, int Crt) {
+  if constexpr (S == 4 && C == 64) {
+    const uint32_t w = (j == 0) ? c.a.x : (j == 1) ? c.a.y : (j == 2) ? c.a.z : c.a.w;
+    const float s01 = pair[(w & 0x3Fu) | ((w >> 2) & 0xFC0u)];
+    const float s2 = lut[2 * 64 + ((w >> 16) & 0x3Fu)];
+    const float s3 = lut[3 * 64 + (w >> 24)];
+    return __fadd_rn(__fadd_rn(s01, s2), s3);
+  } else {
+    const int cw = C > 0 ? C : Crt;
+    float sum = lut[code_at<S>(c, j, 0)];
+#pragma unroll
+    for (int s2 = 1; s2 < S; ++s2) sum = __fadd_rn(sum, lut[s2 * cw + code_at<S>(c, j, s2)]);
+    return sum;
+  }
+}
+
+template <int S, int C>
 __global__ void __launch_bounds__(kScanThreads, 4) decode_scan_kernel(const DecodeParams p) {
   __shared__ float lut[kMaxLut];
+  __shared__ float pair[(S == 4 && C == 64) ? 4096 : 1];
   const int prob = blockIdx.y, seg = blockIdx.x;
   const int h = prob / p.a.n_queries, t = prob - h * p.a.n_queries;
   uint32_t* ctrl = p.ws_ctrl + (size_t)prob * CTRL_WORDS;
   const uint32_t t0 = __ldcg(ctrl + CTRL_T0);
   const int SC = p.a.subspaces * p.a.codewords;
-  for (int e = threadIdx.x; e < SC; e += blockDim.x) lut[e] = __ldcg(p.ws_lut + (size_t)prob * kMaxLut + e);
+  const float* glut = p.ws_lut + (size_t)prob * kMaxLut;
+  for (int e = threadIdx.x; e < SC; e += blockDim.x) lut[e] = __ldcg(glut + e);
+  if constexpr (S == 4 && C == 64) {
+    for (int e = threadIdx.x; e < 4096; e += blockDim.x) pair[e] = __fadd_rn(__ldcg(glut + (e & 63)), __ldcg(glut + 64 + (e >> 6)));
+  }
   __syncthreads();
   const int64_t len_t = allowed_length(p, t);
   const int64_t i0 = (int64_t)seg * kScanKeys;
@@ -426,8 +513,7 @@ __global__ void __launch_bounds__(kScanThreads, 4) decode_scan_kernel(const Deco
   uint2* cand = p.ws_cand + (size_t)prob * p.a.key_len;
   const int lane = threadIdx.x & 31;
   const unsigned lt = (1u << lane) - 1u;
-  scan_segment<S>(p, codes, lut, t, len_t, i0, i1, [&](int64_t i, uint32_t key) {
-    const bool take = key != 0u && key >= t0;
+  auto append = [&](bool take, uint32_t key, int64_t i) {
     const unsigned b = __ballot_sync(0xFFFFFFFFu, take);
     if (b == 0u) return;
     uint32_t base = 0;
@@ -437,6 +523,48 @@ __global__ void __launch_bounds__(kScanThreads, 4) decode_scan_kernel(const Deco
       const uint32_t pos = base + __popc(b & lt);
       if (static_cast<int64_t>(pos) < p.a.key_len) cand[pos] = make_uint2(key, static_cast<uint32_t>(i));
     }
+  };
+  const bool fast = (S > 0) && p.a.allowed_mask == nullptr && ((i1 - i0) & 3) == 0;
+  if constexpr (S > 0) {
+    if (fast) {
+      const float t0f = (t0 <= 1u) ? -INFINITY : key_to_float(t0);
+      const float scale = p.inv_sqrt_r;
+      const bool pow2 = p.sqrt_r_pow2 != 0;
+      const int ngroups = static_cast<int>((i1 - i0) >> 2);
+      const uint8_t* cbase = codes + i0 * S;
+      for (int gb = (threadIdx.x & ~31); gb < ngroups; gb += blockDim.x * kGroupsInFlight) {
+        Codes4<S> c[kGroupsInFlight];
+#pragma unroll
+        for (int u = 0; u < kGroupsInFlight; ++u) {
+          const int g = gb + lane + u * blockDim.x;
+          if (g < ngroups) c[u] = load_codes4<S>(cbase, 4 * g);
+        }
+#pragma unroll
+        for (int u = 0; u < kGroupsInFlight; ++u) {
+          const int g = gb + lane + u * blockDim.x;
+          float sc4[4];
+          bool any = false;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float sum = adc_fast<S, C>(c[u], j, lut, pair, p.a.codewords);
+            sc4[j] = pow2 ? __fmul_rn(sum, scale) : __fdiv_rn(sum, p.sqrt_r);
+            any |= (g < ngroups) && (sc4[j] >= t0f);
+          }
+          if (__any_sync(0xFFFFFFFFu, any)) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const bool take = (g < ngroups) && (sc4[j] >= t0f);
+              append(take, ordered_key(sc4[j]), i0 + 4 * g + j);
+            }
+          }
+        }
+      }
+      return;
+    }
+  }
+  // masked or ragged segments: generic per-key path
+  scan_segment<S>(p, codes, lut, t, len_t, i0, i1, [&](int64_t i, uint32_t key) {
+    append(key != 0u && key >= t0, key, i);
   });
 }
 
@@ -522,8 +650,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
     int n_sl = 0;
     if (n_cand >= k) {
       if (n_cand <= kCandSmem) {
-        for (int i = tid; i < n_cand; i += blockDim.x) cand[i] = __ldcg(gc + i);
-        __syncthreads();
+        copy_batched(cand, gc, n_cand);
         auto item = [&](int i) -> unsigned long long { return composite(cand[i].x, cand[i].y); };
         const SelectThreshold thr = cta_radix_select(item, n_cand, k, sc);
         n_sl = cta_compact(item, n_cand, thr, [&](int pos, int i, unsigned long long) { sl[pos] = cand[i].y; },
@@ -726,9 +853,9 @@ static int plan_decode(const sva_decode_args* a, DecodePlan* plan) {
   return SVA_OK;
 }
 
-template <int S>
+template <int S, int C>
 static void launch_scan(const DecodeParams& p, int P, cudaStream_t stream) {
-  decode_scan_kernel<S><<<dim3(p.nseg, P), kScanThreads, 0, stream>>>(p);
+  decode_scan_kernel<S, C><<<dim3(p.nseg, P), kScanThreads, 0, stream>>>(p);
 }
 
 template <typename T>
@@ -747,17 +874,21 @@ static int launch_decode(DecodePlan& plan, void* ws, cudaStream_t stream) {
     p.ws_lut = reinterpret_cast<float*>(base + reinterpret_cast<size_t>(p.ws_lut));
     p.ws_ctrl = reinterpret_cast<uint32_t*>(base + reinterpret_cast<size_t>(p.ws_ctrl));
     p.ws_cand = reinterpret_cast<uint2*>(base + reinterpret_cast<size_t>(p.ws_cand));
-    const int prep_smem = std::max(4 * p.a.head_dim * p.a.rank_dim, 4 * kSample);
+    const int prep_smem = std::max(4 * p.a.head_dim * p.a.rank_dim, 4 * 4096);
     rc = ensure_smem_attr(reinterpret_cast<const void*>(decode_prep_kernel<T>), prep_smem);
     if (rc != SVA_OK) return rc;
     decode_prep_kernel<T><<<P, kThreads, prep_smem, stream>>>(p);
     profile_mark(0, stream);
+    const int C = p.a.codewords;
     switch (p.vec_codes ? p.a.subspaces : 0) {
-      case 1: launch_scan<1>(p, P, stream); break;
-      case 2: launch_scan<2>(p, P, stream); break;
-      case 4: launch_scan<4>(p, P, stream); break;
-      case 8: launch_scan<8>(p, P, stream); break;
-      default: launch_scan<0>(p, P, stream); break;
+      case 1: launch_scan<1, 0>(p, P, stream); break;
+      case 2: launch_scan<2, 0>(p, P, stream); break;
+      case 4:
+        if (C == 64) launch_scan<4, 64>(p, P, stream);
+        else launch_scan<4, 0>(p, P, stream);
+        break;
+      case 8: launch_scan<8, 0>(p, P, stream); break;
+      default: launch_scan<0, 0>(p, P, stream); break;
     }
     profile_mark(1, stream);
     rc = ensure_smem_attr(reinterpret_cast<const void*>(decode_finish_kernel<T>), static_cast<int>(plan.smem_bytes));

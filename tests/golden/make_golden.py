@@ -173,10 +173,13 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=None, help="path of the reference checkout (contains sva/)")
     ap.add_argument("--out", default=str(HERE / "golden_v1.npz"))
+    ap.add_argument("--models", action="store_true", help="write the model-level fixtures instead")
     args = ap.parse_args()
     if args.reference:
         sys.path.insert(0, args.reference)
     torch.set_num_threads(8)
+    if args.models:
+        return
     res = {}
     res.update(scan_case(config1(), "cfg1"))
     res.update(scan_case(config2(key_len=1 << 16, subspaces=1, codewords=256), "cfg2s_1x256"))
@@ -192,3 +195,40 @@ def main() -> None:
 
 if __name__ == "__main__":
     main()
+
+
+def canonical_topk(self, k, dim=-1, largest=True, sorted=True):
+    """torch.topk with the canonical tie rule (score desc, index asc): a stable descending sort."""
+    assert largest, "the reference only takes largest-k"
+    vals, idx = torch.sort(self, dim=dim, descending=True, stable=True)
+    return torch.return_types.topk((vals.narrow(dim, 0, k), idx.narrow(dim, 0, k)))
+
+
+def model_cases(out_path: str) -> None:
+    """Model-level fixtures: the reference's patch_llama_attention on seeded random Llama models,
+    with torch.Tensor.topk replaced by canonical_topk for the duration of each run."""
+    from sva import SVAArtifactBundle, SVALayerArtifacts, patch_llama_attention
+    from tests.golden import model_cases as mc
+
+    res = {}
+    original = torch.Tensor.topk
+    try:
+        torch.Tensor.topk = canonical_topk
+        for name in mc.CASES:
+            model, bundle, steps, case = mc.build(name, SVAArtifactBundle, SVALayerArtifacts)
+            res[f"{name}_model_checksum"] = np.asarray(sum(float(p.double().sum()) for p in model.parameters()))
+            outs, summary, state = mc.run(model, patch_llama_attention, bundle, steps, case)
+            for i, o in enumerate(outs):
+                res[f"{name}_logits_{i}"] = o.numpy()
+            for k, v in summary.items():
+                res[f"{name}_summary_{k}"] = np.asarray(v)
+            for k, v in state.items():
+                res[f"{name}_state_{k}"] = np.asarray(v)
+    finally:
+        torch.Tensor.topk = original
+    np.savez_compressed(out_path, **res)
+    print("wrote", out_path, len(res), "arrays")
+
+
+if __name__ == "__main__" and "--models" in sys.argv:
+    model_cases(str(HERE / "golden_models_v1.npz"))
