@@ -361,9 +361,11 @@ def gpu_arm(args):
                 if i == 0:
                     prof[0].record()
                     lib.sva_profile_events(handles, n_prof)
-                one_query(st)
-                if i == 0:
-                    lib.sva_profile_events(None, 0)
+                try:
+                    one_query(st)
+                finally:
+                    if i == 0:
+                        lib.sva_profile_events(None, 0)
     torch.cuda.synchronize()
 
     for _ in range(args.warmup):

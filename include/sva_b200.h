@@ -62,6 +62,11 @@ const char* sva_last_error(void);
  * external events, so the hook also works inside CUDA-graph capture.  Pass n = 0 to clear. */
 int sva_profile_events(void* const* events, int32_t n);
 
+/* Phase-timestamp hook (no reference counterpart; measurement only).  When set on the calling
+ * thread, the million-key schedule of sva_decode writes %globaltimer nanoseconds at its phase
+ * boundaries into device_buffer[problem * 16 + slot] (slots 0..9).  Pass NULL to clear. */
+int sva_debug_timestamps(void* device_buffer);
+
 /* ---------------------------------------------------------------------------------------
  * Write path: key catalog.
  * k_low[h][l][:] = K[h / (H/Hkv)][l][:] . k_proj[h]        (fp32, sequential order over D)

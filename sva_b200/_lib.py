@@ -39,6 +39,7 @@ EXPORTED = (
     "sva_version",
     "sva_last_error",
     "sva_profile_events",
+    "sva_debug_timestamps",
     "sva_catalog_encode",
     "sva_assign_centroids",
     "sva_pq_scores",
@@ -175,6 +176,7 @@ def load() -> ctypes.CDLL:
         lib.sva_last_error.restype = ctypes.c_char_p
         sigs = {
             "sva_profile_events": ([c_vp, c_i32], ctypes.c_int),
+            "sva_debug_timestamps": ([c_vp], ctypes.c_int),
             "sva_catalog_encode": ([c_vp, c_i32, c_i64, c_i64, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_i32, c_i32,
                                     c_i64, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp], ctypes.c_int),
             "sva_assign_centroids": ([c_vp, c_i64, c_i32, c_i64, c_vp, c_i32, c_vp, c_vp], ctypes.c_int),

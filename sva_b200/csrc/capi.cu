@@ -50,11 +50,27 @@ static thread_local void* const* g_prof_events = nullptr;
 static thread_local int g_prof_n = 0;
 
 void profile_mark(int i, cudaStream_t stream) {
-  if (g_prof_events && i < g_prof_n && g_prof_events[i])
-    cudaEventRecordWithFlags(static_cast<cudaEvent_t>(g_prof_events[i]), stream, cudaEventRecordExternal);
+  if (!g_prof_events || i >= g_prof_n || !g_prof_events[i]) return;
+  // External event records are only valid while the stream is being captured into a graph.
+  cudaStreamCaptureStatus status = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &status) != cudaSuccess) status = cudaStreamCaptureStatusNone;
+  const cudaEvent_t ev = static_cast<cudaEvent_t>(g_prof_events[i]);
+  const cudaError_t e = (status == cudaStreamCaptureStatusActive)
+                            ? cudaEventRecordWithFlags(ev, stream, cudaEventRecordExternal)
+                            : cudaEventRecord(ev, stream);
+  if (e != cudaSuccess) cudaGetLastError();  // timing is best effort; never fail the launch
 }
 
+static thread_local void* g_debug_ts = nullptr;
+
+void* debug_timestamps() { return g_debug_ts; }
+
 }  // namespace sva
+
+extern "C" int sva_debug_timestamps(void* device_buffer) {
+  sva::g_debug_ts = device_buffer;
+  return SVA_OK;
+}
 
 extern "C" int sva_profile_events(void* const* events, int32_t n) {
   sva::g_prof_events = (n > 0) ? events : nullptr;

@@ -9,8 +9,9 @@
 //
 // * grid   (longer caches), three launches:
 //     prep    : one CTA per problem builds q_low and the LUT into the workspace, scores a
-//               sample of 4096 keys (32 evenly spaced runs of 128) and takes the sample's r-th
-//               best key as a threshold T0 chosen so that about 3x the shortlist lies above it;
+//               sample of 16384 keys (64 evenly spaced runs of 256) and takes the lower edge of
+//               the key bin of the sample's r-th best key as a threshold T0 chosen so that about
+//               2x the shortlist lies above it;
 //     scan    : one CTA per segment of kScanKeys keys, the single full pass over the codes:
 //               every allowed key with key >= T0 is appended to the problem's candidate list;
 //     finish  : a cluster of kCluster CTAs per problem.  CTA 0 selects the exact shortlist from
@@ -42,8 +43,8 @@ constexpr int kFusedMaxKeys = 32768;
 constexpr int kCandSmem = 12288;         // candidates selected in shared memory
 constexpr int kScanThreads = 256;
 constexpr int kGroupsInFlight = 4;
-constexpr int kSampleRuns = 32;
-constexpr int kSampleRunKeys = 128;
+constexpr int kSampleRuns = 64;
+constexpr int kSampleRunKeys = 256;
 constexpr int kSample = kSampleRuns * kSampleRunKeys;
 constexpr int kCluster = 8;
 
@@ -90,7 +91,19 @@ struct DecodeParams {
   float* ws_lut;
   uint32_t* ws_ctrl;
   uint2* ws_cand;  // [P][key_len] (key32, index)
+  unsigned long long* dbg_ts;  // optional phase timestamps (measurement only)
 };
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Records a phase timestamp for problem `prob` (slot < 16) when the timestamp hook is set.
+__device__ __forceinline__ void stamp(const DecodeParams& p, int prob, int slot) {
+  if (p.dbg_ts) p.dbg_ts[(size_t)prob * 16 + slot] = global_ns();
+}
 
 // ---------------------------------------------------------------------------------------
 // small device helpers
@@ -370,10 +383,55 @@ __device__ __forceinline__ void scan_segment(const DecodeParams& p, const uint8_
   }
 }
 
+// Keys of this thread's share of the sample: groups g = tid + u * kThreads of four consecutive
+// keys; group g lies in run g / (kSampleRunKeys / 4).
+template <int S>
+__device__ __forceinline__ void sample_keys(const DecodeParams& p, const uint8_t* codes, const float* lut, int t,
+                                            int64_t len_t, uint32_t* key) {
+  constexpr int kPer = kSample / kThreads;
+  constexpr int kGroups = kPer / 4;
+  constexpr int kRunGroups = kSampleRunKeys / 4;
+  int64_t gstart[kGroups];
+#pragma unroll
+  for (int u = 0; u < kGroups; ++u) {
+    const int g = threadIdx.x + u * kThreads;
+    const int run = g / kRunGroups, off = (g - run * kRunGroups) * 4;
+    gstart[u] = ((len_t * run) / kSampleRuns & ~static_cast<int64_t>(3)) + off;
+  }
+  if constexpr (S > 0) {
+    Codes4<S> c[kGroups];
+#pragma unroll
+    for (int u = 0; u < kGroups; ++u)
+      if (gstart[u] + 3 < len_t) c[u] = load_codes4<S>(codes, gstart[u]);
+#pragma unroll
+    for (int u = 0; u < kGroups; ++u) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t i = gstart[u] + j;
+        uint32_t k = 0u;
+        if (gstart[u] + 3 < len_t) {
+          k = key_allowed(p, t, i, len_t) ? adc_key4<S>(p, c[u], j, lut) : 0u;
+        } else if (i < len_t) {
+          k = adc_key(p, codes, lut, t, i, len_t);
+        }
+        key[4 * u + j] = k;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int u = 0; u < kGroups; ++u)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t i = gstart[u] + j;
+        key[4 * u + j] = (i < len_t) ? adc_key(p, codes, lut, t, i, len_t) : 0u;
+      }
+  }
+}
+
 // prep: q_low + LUT, and the sampled threshold T0 (an ordered key; 1 = every allowed key).
 // The sample is kSampleRuns evenly spaced runs of kSampleRunKeys keys over the allowed range;
 // T0 is the lower edge of the 12-bit key bin holding the sample's r-th best key, with r chosen
-// so that about 3x the shortlist is expected at or above it.
+// so that about 2x the shortlist is expected at or above it.
 template <typename T>
 __global__ void __launch_bounds__(kThreads) decode_prep_kernel(const DecodeParams p) {
   extern __shared__ __align__(16) unsigned char dyn[];
@@ -387,38 +445,25 @@ __global__ void __launch_bounds__(kThreads) decode_prep_kernel(const DecodeParam
   const int prob = blockIdx.x;
   const int h = prob / p.a.n_queries, t = prob - h * p.a.n_queries;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) stamp(p, prob, 0);
   build_qlut<T>(p, h, t, qf, ql, lut, stage);
+  if (tid == 0) stamp(p, prob, 9);
   const int SC = p.a.subspaces * p.a.codewords;
   float* gl = p.ws_lut + (size_t)prob * kMaxLut;
   for (int e = tid; e < SC; e += blockDim.x) gl[e] = lut[e];
   for (int r = tid; r < p.a.rank_dim; r += blockDim.x) p.ws_qlow[(size_t)prob * kMaxRank + r] = ql[r];
   const int64_t len_t = allowed_length(p, t);
   const uint8_t* codes = p.a.codes + h * p.a.codes_head_stride;
-  // each thread scores kSample / kThreads keys; all code loads are issued before any is used
+  // each thread scores kSample / kThreads keys (groups of four, one vector load each, all loads
+  // issued before any is used); runs start on multiples of four keys
   constexpr int kPer = kSample / kThreads;
   uint32_t key[kPer];
-  {
-    uint8_t cb[kPer][kMaxSubspaces];
-    const int S = p.a.subspaces;
-#pragma unroll
-    for (int u = 0; u < kPer; ++u) {
-      const int e = tid + u * kThreads;
-      const int run = e / kSampleRunKeys, off = e - run * kSampleRunKeys;
-      const int64_t i = (len_t * run) / kSampleRuns + off;
-      for (int s2 = 0; s2 < kMaxSubspaces; ++s2) cb[u][s2] = (i < len_t && s2 < S) ? __ldg(codes + i * S + s2) : 0;
-    }
-#pragma unroll
-    for (int u = 0; u < kPer; ++u) {
-      const int e = tid + u * kThreads;
-      const int run = e / kSampleRunKeys, off = e - run * kSampleRunKeys;
-      const int64_t i = (len_t * run) / kSampleRuns + off;
-      key[u] = 0u;
-      if (key_allowed(p, t, i, len_t)) {
-        float sum = 0.f;
-        for (int s2 = 0; s2 < S; ++s2) sum = __fadd_rn(sum, lut[s2 * p.a.codewords + cb[u][s2]]);
-        key[u] = ordered_key(finish_score(sum, p));
-      }
-    }
+  switch (p.vec_codes ? p.a.subspaces : 0) {
+    case 1: sample_keys<1>(p, codes, lut, t, len_t, key); break;
+    case 2: sample_keys<2>(p, codes, lut, t, len_t, key); break;
+    case 4: sample_keys<4>(p, codes, lut, t, len_t, key); break;
+    case 8: sample_keys<8>(p, codes, lut, t, len_t, key); break;
+    default: sample_keys<0>(p, codes, lut, t, len_t, key); break;
   }
   uint32_t* hist = reinterpret_cast<uint32_t*>(dyn);  // 4096 bins; the stage is no longer needed
   for (int b = tid; b < 4096; b += blockDim.x) hist[b] = 0u;
@@ -432,7 +477,7 @@ __global__ void __launch_bounds__(kThreads) decode_prep_kernel(const DecodeParam
     }
   const int n_s = block_sum_int(nv, scratch);
   const int64_t k_est = imin64(p.sl_cap, len_t);
-  const int64_t r = (3 * k_est * n_s + len_t - 1) / (len_t > 0 ? len_t : 1) + 8;
+  const int64_t r = (2 * k_est * n_s + len_t - 1) / (len_t > 0 ? len_t : 1) + 8;
   if (tid == 0) t0_sh = 1u;
   __syncthreads();
   if (n_s > 0 && r < n_s) {
@@ -465,6 +510,7 @@ __global__ void __launch_bounds__(kThreads) decode_prep_kernel(const DecodeParam
     uint32_t* ctrl = p.ws_ctrl + (size_t)prob * CTRL_WORDS;
     ctrl[CTRL_NCAND] = 0u;
     ctrl[CTRL_T0] = t0_sh > 1u ? t0_sh : 1u;
+    stamp(p, prob, 1);
   }
 }
 
@@ -501,10 +547,11 @@ __global__ void __launch_bounds__(kScanThreads, 4) decode_scan_kernel(const Deco
   const int SC = p.a.subspaces * p.a.codewords;
   const float* glut = p.ws_lut + (size_t)prob * kMaxLut;
   for (int e = threadIdx.x; e < SC; e += blockDim.x) lut[e] = __ldcg(glut + e);
-  if constexpr (S == 4 && C == 64) {
-    for (int e = threadIdx.x; e < 4096; e += blockDim.x) pair[e] = __fadd_rn(__ldcg(glut + (e & 63)), __ldcg(glut + 64 + (e >> 6)));
-  }
   __syncthreads();
+  if constexpr (S == 4 && C == 64) {
+    for (int e = threadIdx.x; e < 4096; e += blockDim.x) pair[e] = __fadd_rn(lut[e & 63], lut[64 + (e >> 6)]);
+    __syncthreads();
+  }
   const int64_t len_t = allowed_length(p, t);
   const int64_t i0 = (int64_t)seg * kScanKeys;
   const int64_t i1 = min(len_t, i0 + kScanKeys);
@@ -630,6 +677,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
   __syncthreads();
 
   // ---- phase 1 (CTA 0): the exact shortlist ------------------------------------------------
+  if (crank == 0 && tid == 0) stamp(p, prob, 2);
   if (crank == 0) {
     const uint32_t* ctrl = p.ws_ctrl + (size_t)prob * CTRL_WORDS;
     const uint32_t t0 = __ldcg(ctrl + CTRL_T0);
@@ -682,6 +730,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
     }
     if (tid == 0) misc[0] = n_sl;
   }
+  if (crank == 0 && tid == 0) stamp(p, prob, 3);
   cluster.sync();
 
   // ---- phase 2: rescore, split across the cluster -----------------------------------------
@@ -698,6 +747,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
     for (int j = j0 + tid; j < j1; j += blockDim.x) rk0[j] = rk[j - j0];
   }
   cluster.sync();
+  if (crank == 0 && tid == 0) stamp(p, prob, 4);
 
   // ---- phase 3 (CTA 0): budget select --------------------------------------------------
   if (crank == 0) {
@@ -708,6 +758,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
                                   scratch);
     if (tid == 0) misc[1] = n_fin;
   }
+  if (crank == 0 && tid == 0) stamp(p, prob, 5);
   cluster.sync();
 
   // ---- phase 4: logits, split -------------------------------------------------------------
@@ -729,6 +780,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
     for (int j = f0 + tid; j < f1; j += blockDim.x) lg0[j] = mylg[j - f0];
   }
   cluster.sync();
+  if (crank == 0 && tid == 0) stamp(p, prob, 6);
 
   // ---- phase 5: softmax over all logits (same order in every CTA), weights and partial sums -
   {
@@ -747,6 +799,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
     for (int d = tid; d < D; d += blockDim.x) parts0[crank * D + d] = sums[d];
   }
   cluster.sync();
+  if (crank == 0 && tid == 0) stamp(p, prob, 7);
 
   // ---- phase 6 (CTA 0): merge, outputs, counters ------------------------------------------
   if (crank == 0) {
@@ -765,6 +818,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
       atomicAdd(p.a.stats + SVA_STAT_EXACT_SCORED, static_cast<unsigned long long>(n_fin));
       atomicAdd(p.a.stats + SVA_STAT_VERIFIED, static_cast<unsigned long long>(n_fin));
     }
+    if (tid == 0) stamp(p, prob, 8);
   }
 }
 
@@ -874,6 +928,7 @@ static int launch_decode(DecodePlan& plan, void* ws, cudaStream_t stream) {
     p.ws_lut = reinterpret_cast<float*>(base + reinterpret_cast<size_t>(p.ws_lut));
     p.ws_ctrl = reinterpret_cast<uint32_t*>(base + reinterpret_cast<size_t>(p.ws_ctrl));
     p.ws_cand = reinterpret_cast<uint2*>(base + reinterpret_cast<size_t>(p.ws_cand));
+    p.dbg_ts = static_cast<unsigned long long*>(debug_timestamps());
     const int prep_smem = std::max(4 * p.a.head_dim * p.a.rank_dim, 4 * 4096);
     rc = ensure_smem_attr(reinterpret_cast<const void*>(decode_prep_kernel<T>), prep_smem);
     if (rc != SVA_OK) return rc;

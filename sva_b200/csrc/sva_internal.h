@@ -20,6 +20,9 @@ int set_error(int code, const char* msg);
 // Raises a kernel's dynamic shared-memory limit once per (kernel, device).
 int ensure_smem_attr(const void* kernel, int bytes);
 
+// Device buffer for phase timestamps set by sva_debug_timestamps (measurement only), or NULL.
+void* debug_timestamps();
+
 // Records the calling thread's i-th profiling event (sva_profile_events) on `stream`, if set.
 void profile_mark(int i, cudaStream_t stream);
 

@@ -183,14 +183,18 @@ class SVALlamaAttention(nn.Module):
             min_budget = min(self.serving.adaptive_min_budget or max_budget, max_budget, k_len)
             mid_budget = min(self.serving.adaptive_mid_budget or max(min_budget, max_budget // 2), max_budget, k_len)
             prof_events = ev.kernel_events(4) if ev else None
-            out = kernels.decode_inverted(
-                query[0, :, 0, :], self.sva_q_proj, self.sva_scale, self.sva_coarse_codebooks, self._codes_buf,
-                self._postings, k_low, keys, values, max_budget, self.serving.inverted_cells_per_subspace, min_budget,
-                mid_budget, low_margin=self.serving.adaptive_low_margin, high_margin=self.serving.adaptive_high_margin,
-                dynamic=(mode == "inverted"), allowed_mask=None if allowed_mask is None else allowed_mask[0],
-                softmax_scale=self.scaling, stats=counters)
+            try:
+                out = kernels.decode_inverted(
+                    query[0, :, 0, :], self.sva_q_proj, self.sva_scale, self.sva_coarse_codebooks, self._codes_buf,
+                    self._postings, k_low, keys, values, max_budget, self.serving.inverted_cells_per_subspace,
+                    min_budget, mid_budget, low_margin=self.serving.adaptive_low_margin,
+                    high_margin=self.serving.adaptive_high_margin, dynamic=(mode == "inverted"),
+                    allowed_mask=None if allowed_mask is None else allowed_mask[0], softmax_scale=self.scaling,
+                    stats=counters)
+            finally:
+                if ev:
+                    ev.release_kernel_events()
             if ev:
-                ev.release_kernel_events()
                 ev.mark("total")
                 self._record_profile(ev, prof_events)
             return out[None, :, None, :]
