@@ -47,6 +47,7 @@ constexpr int kSampleRuns = 64;
 constexpr int kSampleRunKeys = 256;
 constexpr int kSample = kSampleRuns * kSampleRunKeys;
 constexpr int kCluster = 8;
+constexpr int kScanLocalCands = 2048;
 
 enum { CTRL_NCAND = 0, CTRL_T0, CTRL_WORDS = 4 };
 
@@ -468,14 +469,18 @@ __global__ void __launch_bounds__(kThreads) decode_prep_kernel(const DecodeParam
   uint32_t* hist = reinterpret_cast<uint32_t*>(dyn);  // 4096 bins; the stage is no longer needed
   for (int b = tid; b < 4096; b += blockDim.x) hist[b] = 0u;
   __syncthreads();
+  if (tid == 0) stamp(p, prob, 10);
   int nv = 0;
 #pragma unroll
-  for (int u = 0; u < kPer; ++u)
-    if (key[u]) {
-      atomicAdd(&hist[key[u] >> 20], 1u);
-      ++nv;
-    }
+  for (int u = 0; u < kPer; ++u) {
+    // one shared atomic per distinct bin of the warp (sample keys crowd a few bins)
+    const uint32_t bin = key[u] ? (key[u] >> 20) : 0xFFFFFFFFu;
+    const unsigned same = __match_any_sync(0xFFFFFFFFu, bin);
+    if (key[u] && (same & ((1u << lane) - 1u)) == 0u) atomicAdd(&hist[bin], static_cast<uint32_t>(__popc(same)));
+    nv += key[u] != 0u;
+  }
   const int n_s = block_sum_int(nv, scratch);
+  if (tid == 0) stamp(p, prob, 11);
   const int64_t k_est = imin64(p.sl_cap, len_t);
   const int64_t r = (2 * k_est * n_s + len_t - 1) / (len_t > 0 ? len_t : 1) + 8;
   if (tid == 0) t0_sh = 1u;
@@ -540,6 +545,9 @@ template <int S, int C>
 __global__ void __launch_bounds__(kScanThreads, 4) decode_scan_kernel(const DecodeParams p) {
   __shared__ float lut[kMaxLut];
   __shared__ float pair[(S == 4 && C == 64) ? 4096 : 1];
+  __shared__ uint2 local[kScanLocalCands];  // this CTA's candidates, flushed with one atomic
+  __shared__ uint32_t n_local;
+  __shared__ uint32_t flush_base;
   const int prob = blockIdx.y, seg = blockIdx.x;
   const int h = prob / p.a.n_queries, t = prob - h * p.a.n_queries;
   uint32_t* ctrl = p.ws_ctrl + (size_t)prob * CTRL_WORDS;
@@ -547,6 +555,7 @@ __global__ void __launch_bounds__(kScanThreads, 4) decode_scan_kernel(const Deco
   const int SC = p.a.subspaces * p.a.codewords;
   const float* glut = p.ws_lut + (size_t)prob * kMaxLut;
   for (int e = threadIdx.x; e < SC; e += blockDim.x) lut[e] = __ldcg(glut + e);
+  if (threadIdx.x == 0) n_local = 0u;
   __syncthreads();
   if constexpr (S == 4 && C == 64) {
     for (int e = threadIdx.x; e < 4096; e += blockDim.x) pair[e] = __fadd_rn(lut[e & 63], lut[64 + (e >> 6)]);
@@ -560,18 +569,26 @@ __global__ void __launch_bounds__(kScanThreads, 4) decode_scan_kernel(const Deco
   uint2* cand = p.ws_cand + (size_t)prob * p.a.key_len;
   const int lane = threadIdx.x & 31;
   const unsigned lt = (1u << lane) - 1u;
+  // Candidates go to shared memory (one shared atomic per warp and step); when that buffer is
+  // full they go straight to the global list.
   auto append = [&](bool take, uint32_t key, int64_t i) {
     const unsigned b = __ballot_sync(0xFFFFFFFFu, take);
     if (b == 0u) return;
     uint32_t base = 0;
-    if (lane == 0) base = atomicAdd(ctrl + CTRL_NCAND, static_cast<uint32_t>(__popc(b)));
+    if (lane == 0) base = atomicAdd(&n_local, static_cast<uint32_t>(__popc(b)));
     base = __shfl_sync(0xFFFFFFFFu, base, 0);
     if (take) {
       const uint32_t pos = base + __popc(b & lt);
-      if (static_cast<int64_t>(pos) < p.a.key_len) cand[pos] = make_uint2(key, static_cast<uint32_t>(i));
+      if (pos < static_cast<uint32_t>(kScanLocalCands)) {
+        local[pos] = make_uint2(key, static_cast<uint32_t>(i));
+      } else {
+        const uint32_t g = atomicAdd(ctrl + CTRL_NCAND, 1u);
+        if (static_cast<int64_t>(g) < p.a.key_len) cand[g] = make_uint2(key, static_cast<uint32_t>(i));
+      }
     }
   };
   const bool fast = (S > 0) && p.a.allowed_mask == nullptr && ((i1 - i0) & 3) == 0;
+  bool done = false;
   if constexpr (S > 0) {
     if (fast) {
       const float t0f = (t0 <= 1u) ? -INFINITY : key_to_float(t0);
@@ -606,13 +623,25 @@ __global__ void __launch_bounds__(kScanThreads, 4) decode_scan_kernel(const Deco
           }
         }
       }
-      return;
+      done = true;
     }
   }
-  // masked or ragged segments: generic per-key path
-  scan_segment<S>(p, codes, lut, t, len_t, i0, i1, [&](int64_t i, uint32_t key) {
-    append(key != 0u && key >= t0, key, i);
-  });
+  if (!done) {
+    // masked or ragged segments: generic per-key path
+    scan_segment<S>(p, codes, lut, t, len_t, i0, i1, [&](int64_t i, uint32_t key) {
+      append(key != 0u && key >= t0, key, i);
+    });
+  }
+  __syncthreads();
+  const uint32_t nl = min(n_local, static_cast<uint32_t>(kScanLocalCands));
+  if (threadIdx.x == 0 && nl > 0) flush_base = atomicAdd(ctrl + CTRL_NCAND, nl);
+  __syncthreads();
+  if (nl > 0) {
+    for (uint32_t e = threadIdx.x; e < nl; e += blockDim.x) {
+      const uint32_t g = flush_base + e;
+      if (static_cast<int64_t>(g) < p.a.key_len) cand[g] = local[e];
+    }
+  }
 }
 
 struct FinishSmem {
@@ -699,6 +728,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
     if (n_cand >= k) {
       if (n_cand <= kCandSmem) {
         copy_batched(cand, gc, n_cand);
+        if (tid == 0) stamp(p, prob, 12);
         auto item = [&](int i) -> unsigned long long { return composite(cand[i].x, cand[i].y); };
         const SelectThreshold thr = cta_radix_select(item, n_cand, k, sc);
         n_sl = cta_compact(item, n_cand, thr, [&](int pos, int i, unsigned long long) { sl[pos] = cand[i].y; },
