@@ -4,20 +4,24 @@
 // an ordered score key (sva::ordered_key); c == 0 marks an item that is not a candidate.  The
 // selection order is c descending, i.e. score descending, then key index ascending -- the rule
 // the CPU oracle applies to every torch.topk of the reference (sva/llama.py:278, :295, :100,
-// :113).  A caller whose items share their top bits may pass a left-shifted composite that
-// keeps only the varying bits, as long as the order is preserved and real items stay non-zero.
+// :113).
 //
-// The select is an MSB-first radix select with 8-bit digits starting at bit `top_bit`.  Each
-// level makes one pass over the items (a functor call per item, so items may live in shared
-// memory or be re-read from global memory), builds a 256-bin histogram of the digit among the
-// items that still match the prefix, and fixes one digit.  It stops as soon as the boundary
-// digit holds exactly the number of items still needed.  An item is selected iff c != 0 and
-// (c & mask) >= prefix.
+// The select first finds the range [min, max] of the non-zero items, then runs an MSB-first
+// radix select on (c - min) with 11-bit digits starting at the highest bit of (max - min): each
+// level divides the current window into 2048 equal bins, counts the items of the window per bin
+// (a functor call per item, so items may live in shared memory or be re-read from global
+// memory) and keeps the bin holding the k-th item.  Starting at the range's own top bit keeps
+// items that share their high bits (every candidate above a threshold does) from piling into
+// one bin.  It stops as soon as the boundary bin holds exactly the number of items still
+// needed.  The result is a plain threshold: an item is selected iff c != 0 and c >= prefix.
 #pragma once
 
 #include "sva_common.cuh"
 
 namespace sva {
+
+constexpr int kSelectBins = 2048;
+constexpr int kSelectDigit = 11;
 
 struct SelectThreshold {
   unsigned long long prefix;
@@ -32,70 +36,116 @@ __device__ __forceinline__ bool is_selected(const SelectThreshold& t, unsigned l
   return c != 0ull && (c & t.mask) >= t.prefix;
 }
 
-// Shared scratch for cta_radix_select: 256-bin histogram plus a few broadcast slots.
+// Shared scratch for cta_radix_select: the bin counts plus a few broadcast slots.
 struct SelectScratch {
-  uint32_t hist[256];
-  int warp_tot[9];
+  uint32_t hist[kSelectBins];
+  unsigned long long lo_part[32];
+  unsigned long long hi_part[32];
+  int warp_tot[32];
+  unsigned long long base;
+  unsigned long long top;
   int digit;
   int above;
   int count;
 };
 
-// Requires blockDim.x >= 256 and a multiple of 32.  `k` must not exceed the number of non-zero
-// items.  All threads of the block must call it.  Digits are bits [top_bit-7, top_bit],
-// [top_bit-15, top_bit-8], ... (top_bit in 7..63, the last digit may be narrower).
+// Requires blockDim.x in {256, 512, 1024}.  `k` should not exceed the number of non-zero items
+// (if it does, every non-zero item is selected).  All threads of the block must call it.
 template <class ItemFn>
-__device__ SelectThreshold cta_radix_select(const ItemFn& item, int n, int k, SelectScratch* sc, int top_bit = 63) {
+__device__ SelectThreshold cta_radix_select(const ItemFn& item, int n, int k, SelectScratch* sc) {
   SelectThreshold thr;
-  thr.prefix = 0ull;
-  thr.mask = 0ull;
+  thr.mask = ~0ull;
   if (k <= 0) {
-    thr.prefix = ~0ull;  // (c & 0) >= ~0 is false for every item
+    thr.prefix = ~0ull;
+    thr.mask = 0ull;  // (c & 0) >= ~0 is false for every item
     return thr;
   }
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  unsigned long long mn = ~0ull, mx = 0ull;
+  for (int i = tid; i < n; i += blockDim.x) {
+    const unsigned long long c = item(i);
+    if (c != 0ull) {
+      mn = c < mn ? c : mn;
+      mx = c > mx ? c : mx;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long a = __shfl_xor_sync(0xFFFFFFFFu, mn, o);
+    const unsigned long long b = __shfl_xor_sync(0xFFFFFFFFu, mx, o);
+    mn = a < mn ? a : mn;
+    mx = b > mx ? b : mx;
+  }
+  if (lane == 0) {
+    sc->lo_part[warp] = mn;
+    sc->hi_part[warp] = mx;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    unsigned long long a = ~0ull, b = 0ull;
+    for (int w = 0; w < nwarps; ++w) {
+      a = sc->lo_part[w] < a ? sc->lo_part[w] : a;
+      b = sc->hi_part[w] > b ? sc->hi_part[w] : b;
+    }
+    sc->base = a;
+    sc->top = b;
+  }
+  __syncthreads();
+  unsigned long long base = sc->base;
+  const unsigned long long top = sc->top;
+  __syncthreads();
+  if (top == 0ull || top == base) {  // no items, or all non-zero items equal
+    thr.prefix = base;
+    return thr;
+  }
+  int hi = 63 - __clzll(static_cast<long long>(top - base));
   int remaining = k;
-  const int tid = threadIdx.x;
-  const int lane = tid & 31;
-  for (int hi = top_bit; hi >= 0; hi -= 8) {
-    const int lo = hi >= 7 ? hi - 7 : 0;
-    const int width = hi - lo + 1;
-    const unsigned long long dmask = ((1ull << width) - 1ull) << lo;
-    for (int b = tid; b < 256; b += blockDim.x) sc->hist[b] = 0u;
+  const int per = kSelectBins / blockDim.x;  // bins per thread in the scan
+  for (;;) {
+    const int lo = hi >= kSelectDigit - 1 ? hi - (kSelectDigit - 1) : 0;
+    for (int b = tid; b < kSelectBins; b += blockDim.x) sc->hist[b] = 0u;
+    if (tid == 0) sc->count = -1;
     __syncthreads();
     for (int i = tid; i < n; i += blockDim.x) {
       const unsigned long long c = item(i);
-      if (c == 0ull || (c & thr.mask) != thr.prefix) continue;
-      atomicAdd(&sc->hist[(c >> lo) & ((1ull << width) - 1ull)], 1u);
+      if (c == 0ull || c < base) continue;
+      const unsigned long long d = c - base;
+      if (hi < 63 && (d >> (hi + 1)) != 0ull) continue;  // above the window [base, base + 2^(hi+1))
+      atomicAdd(&sc->hist[d >> lo], 1u);
     }
     __syncthreads();
-    // Descending suffix scan over the digits with warps 0..7 (thread t owns digit 255-t): the
-    // owner of the first digit whose running count reaches `remaining` is the boundary.
-    int v = 0, incl = 0;
-    if (tid < 256) {
-      v = static_cast<int>(sc->hist[255 - tid]);
-      incl = warp_incl_scan(v);
-      if (lane == 31) sc->warp_tot[tid >> 5] = incl;
-    }
+    // Descending scan: thread t owns bins kSelectBins-1-per*t ... kSelectBins-per*(t+1).
+    int cnt = 0;
+    for (int q = 0; q < per; ++q) cnt += static_cast<int>(sc->hist[kSelectBins - 1 - (per * tid + q)]);
+    int incl = warp_incl_scan(cnt);
+    if (lane == 31) sc->warp_tot[warp] = incl;
     __syncthreads();
-    if (tid < 256) {
-      int base = 0;
-      for (int w = 0; w < (tid >> 5); ++w) base += sc->warp_tot[w];
-      incl += base;
-      if (incl >= remaining && incl - v < remaining) {
-        sc->digit = 255 - tid;
-        sc->above = incl - v;
-        sc->count = v;
+    for (int w = 0; w < warp; ++w) incl += sc->warp_tot[w];
+    const int excl = incl - cnt;
+    if (excl < remaining && incl >= remaining) {
+      int run = excl;
+      for (int q = 0; q < per; ++q) {
+        const int b = kSelectBins - 1 - (per * tid + q);
+        const int v = static_cast<int>(sc->hist[b]);
+        if (run + v >= remaining) {
+          sc->digit = b;
+          sc->above = run;
+          sc->count = v;
+          break;
+        }
+        run += v;
       }
     }
     __syncthreads();
-    const unsigned long long d = static_cast<unsigned long long>(sc->digit);
+    const int count = sc->count;
+    if (count < 0) break;  // fewer items than k: keep the window's base, select all
+    base += static_cast<unsigned long long>(sc->digit) << lo;
     remaining -= sc->above;
-    const int cnt = sc->count;
-    thr.prefix |= d << lo;
-    thr.mask |= dmask;
     __syncthreads();
-    if (cnt == remaining) break;
+    if (count == remaining || lo == 0) break;
+    hi = lo - 1;
   }
+  thr.prefix = base;
   return thr;
 }
 

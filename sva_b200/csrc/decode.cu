@@ -38,7 +38,7 @@ namespace sva {
 namespace cg = cooperative_groups;
 
 constexpr int kThreads = 512;
-constexpr int kScanKeys = 8192;          // keys per scan CTA
+constexpr int kScanKeys = 16384;         // keys per scan CTA
 constexpr int kFusedMaxKeys = 32768;
 constexpr int kCandSmem = 12288;         // candidates selected in shared memory
 constexpr int kScanThreads = 256;
@@ -46,8 +46,10 @@ constexpr int kGroupsInFlight = 4;
 constexpr int kSampleRuns = 64;
 constexpr int kSampleRunKeys = 256;
 constexpr int kSample = kSampleRuns * kSampleRunKeys;
+constexpr int kPrepSmemLimit = 192 * 1024;  // dynamic shared memory of the prep kernel
 constexpr int kCluster = 8;
-constexpr int kScanLocalCands = 2048;
+constexpr int kScanLocalCands = 1024;
+constexpr int kRepEntries = 256;  // largest S * C of the bank-replicated scan LUT
 
 enum { CTRL_NCAND = 0, CTRL_T0, CTRL_WORDS = 4 };
 
@@ -87,6 +89,7 @@ struct DecodeParams {
   int grid_mode;
   int nseg;
   int vec_codes;  // codes aligned for 4-key vector loads
+  int prep_rep;   // the prep kernel's sample lookups use a bank-replicated LUT
   DecodeSmem lay;
   float* ws_qlow;
   float* ws_lut;
@@ -112,8 +115,11 @@ __device__ __forceinline__ void stamp(const DecodeParams& p, int prob, int slot)
 
 __host__ __device__ __forceinline__ int64_t imin64(int64_t x, int64_t y) { return x < y ? x : y; }
 
+// Out of line: the division's instruction sequence is not repeated at every unrolled call site.
+__device__ __noinline__ float div_rn_outlined(float a, float b) { return __fdiv_rn(a, b); }
+
 __device__ __forceinline__ float finish_score(float sum, const DecodeParams& p) {
-  return p.sqrt_r_pow2 ? __fmul_rn(sum, p.inv_sqrt_r) : __fdiv_rn(sum, p.sqrt_r);
+  return p.sqrt_r_pow2 ? __fmul_rn(sum, p.inv_sqrt_r) : div_rn_outlined(sum, p.sqrt_r);
 }
 
 __device__ __forceinline__ int64_t allowed_length(const DecodeParams& p, int t) {
@@ -163,6 +169,25 @@ __device__ __forceinline__ Codes4<S> load_codes4(const uint8_t* base, int64_t i)
   return r;
 }
 
+// The same from shared memory (plain loads; the read-only path cannot address shared memory).
+template <int S>
+__device__ __forceinline__ Codes4<S> load_codes4_shared(const uint8_t* base, int i) {
+  Codes4<S> r;
+  if (S == 1) {
+    r.a.x = *reinterpret_cast<const uint32_t*>(base + i);
+  } else if (S == 2) {
+    const uint2 w = *reinterpret_cast<const uint2*>(base + 2 * i);
+    r.a.x = w.x;
+    r.a.y = w.y;
+  } else if (S == 4) {
+    r.a = *reinterpret_cast<const uint4*>(base + 4 * i);
+  } else {
+    r.a = *reinterpret_cast<const uint4*>(base + 8 * i);
+    r.b = *reinterpret_cast<const uint4*>(base + 8 * i + 16);
+  }
+  return r;
+}
+
 // Code of key j (0..3) in subspace s.
 template <int S>
 __device__ __forceinline__ uint32_t code_at(const Codes4<S>& c, int j, int s) {
@@ -188,6 +213,16 @@ __device__ __forceinline__ uint32_t adc_key4(const DecodeParams& p, const Codes4
 #pragma unroll
   for (int s = 0; s < S; ++s) sum = __fadd_rn(sum, lut[s * C + code_at<S>(c, j, s)]);
   return ordered_key(finish_score(sum, p));
+}
+
+// Plain-layout ADC sum of key j (C == 0: the runtime codeword count Crt).
+template <int S, int C>
+__device__ __forceinline__ float adc_plain(const Codes4<S>& c, int j, const float* lut, int Crt) {
+  const int cw = C > 0 ? C : Crt;
+  float sum = lut[code_at<S>(c, j, 0)];
+#pragma unroll
+  for (int s2 = 1; s2 < S; ++s2) sum = __fadd_rn(sum, lut[s2 * cw + code_at<S>(c, j, s2)]);
+  return sum;
 }
 
 template <typename T>
@@ -384,263 +419,280 @@ __device__ __forceinline__ void scan_segment(const DecodeParams& p, const uint8_
   }
 }
 
-// Keys of this thread's share of the sample: groups g = tid + u * kThreads of four consecutive
-// keys; group g lies in run g / (kSampleRunKeys / 4).
-template <int S>
-__device__ __forceinline__ void sample_keys(const DecodeParams& p, const uint8_t* codes, const float* lut, int t,
-                                            int64_t len_t, uint32_t* key) {
-  constexpr int kPer = kSample / kThreads;
-  constexpr int kGroups = kPer / 4;
+// Start key of this thread's u-th sample group: groups g = tid + u * kThreads of four consecutive
+// keys; group g lies in run g / (kSampleRunKeys / 4); runs start on multiples of four keys.
+__device__ __forceinline__ int64_t sample_group_start(int64_t len_t, int u) {
   constexpr int kRunGroups = kSampleRunKeys / 4;
-  int64_t gstart[kGroups];
-#pragma unroll
-  for (int u = 0; u < kGroups; ++u) {
-    const int g = threadIdx.x + u * kThreads;
-    const int run = g / kRunGroups, off = (g - run * kRunGroups) * 4;
-    gstart[u] = ((len_t * run) / kSampleRuns & ~static_cast<int64_t>(3)) + off;
-  }
-  if constexpr (S > 0) {
-    Codes4<S> c[kGroups];
-#pragma unroll
-    for (int u = 0; u < kGroups; ++u)
-      if (gstart[u] + 3 < len_t) c[u] = load_codes4<S>(codes, gstart[u]);
-#pragma unroll
-    for (int u = 0; u < kGroups; ++u) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int64_t i = gstart[u] + j;
-        uint32_t k = 0u;
-        if (gstart[u] + 3 < len_t) {
-          k = key_allowed(p, t, i, len_t) ? adc_key4<S>(p, c[u], j, lut) : 0u;
-        } else if (i < len_t) {
-          k = adc_key(p, codes, lut, t, i, len_t);
-        }
-        key[4 * u + j] = k;
-      }
-    }
+  const int g = threadIdx.x + u * kThreads;
+  const int run = g / kRunGroups, off = (g - run * kRunGroups) * 4;
+  return ((len_t * run) / kSampleRuns & ~static_cast<int64_t>(3)) + off;
+}
+
+// Asynchronous global -> shared copy of one 4-key code group (4 * S bytes, aligned to that).
+template <int S>
+__device__ __forceinline__ void copy_group_async(uint8_t* dst, const uint8_t* src) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+  if constexpr (S == 1) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(d), "l"(src) : "memory");
+  } else if constexpr (S == 2) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(d), "l"(src) : "memory");
+  } else if constexpr (S == 4) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(src) : "memory");
   } else {
-#pragma unroll
-    for (int u = 0; u < kGroups; ++u)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int64_t i = gstart[u] + j;
-        key[4 * u + j] = (i < len_t) ? adc_key(p, codes, lut, t, i, len_t) : 0u;
-      }
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(src) : "memory");
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d + 16), "l"(src + 16) : "memory");
   }
+}
+
+// Dynamic shared memory of the prep kernel: the LUT stage (later the sample's keys), then,
+// for the vector-code variants, the sampled codes (kSample keys x S bytes), then, when
+// S * C <= kRepEntries, the bank-replicated LUT.
+__host__ __device__ inline int prep_stage_bytes(int head_dim, int rank_dim) {
+  return 4 * head_dim * rank_dim > 4 * kSample ? 4 * head_dim * rank_dim : 4 * kSample;
+}
+
+// ADC sum of key j from a bank-replicated LUT with a runtime codeword count (codes clamped to
+// the table, so a corrupt code cannot read outside it).
+template <int S>
+__device__ __forceinline__ float adc_rep_rt(const Codes4<S>& c, int j, const float* lut_lane, int C) {
+  float sum = lut_lane[min(code_at<S>(c, j, 0), static_cast<uint32_t>(C - 1)) * 32];
+#pragma unroll
+  for (int s = 1; s < S; ++s)
+    sum = __fadd_rn(sum, lut_lane[(s * C + min(code_at<S>(c, j, s), static_cast<uint32_t>(C - 1))) * 32]);
+  return sum;
+}
+
+// Keeps the four largest values seen, t[0] >= t[1] >= t[2] >= t[3].
+__device__ __forceinline__ void top4_insert(uint32_t (&t)[4], uint32_t x) {
+#pragma unroll
+  for (int q = 0; q < 3; ++q) {
+    const uint32_t hi = max(t[q], x);
+    x = min(t[q], x);
+    t[q] = hi;
+  }
+  t[3] = max(t[3], x);
 }
 
 // prep: q_low + LUT, and the sampled threshold T0 (an ordered key; 1 = every allowed key).
 // The sample is kSampleRuns evenly spaced runs of kSampleRunKeys keys over the allowed range;
-// T0 is the lower edge of the 12-bit key bin holding the sample's r-th best key, with r chosen
-// so that about 2x the shortlist is expected at or above it.
-template <typename T>
+// its codes are copied to shared memory asynchronously while the query LUT is built.  T0 is
+// the r-th best key of the sample, r chosen so that about 2x the shortlist plus a margin is
+// expected at or above it.  When r <= 4 * kThreads the select runs over the four best keys of
+// every thread's share, whose r-th best can only be lower than the sample's (a safe, slightly
+// larger candidate set); otherwise over the whole sample.
+template <typename T, int S>
 __global__ void __launch_bounds__(kThreads) decode_prep_kernel(const DecodeParams p) {
   extern __shared__ __align__(16) unsigned char dyn[];
   __shared__ float qf[kMaxHeadDim];
   __shared__ float ql[kMaxRank];
   __shared__ float lut[kMaxLut];
   __shared__ int scratch[64];
-  __shared__ int wtot[kThreads / 32];
-  __shared__ uint32_t t0_sh;
+  __shared__ SelectScratch sel;
+  __shared__ __align__(16) uint32_t tops[4 * kThreads];
   float* stage = reinterpret_cast<float*>(dyn);
+  const int stage_bytes = prep_stage_bytes(p.a.head_dim, p.a.rank_dim);
+  uint8_t* sample = dyn + stage_bytes;
+  float* lut_rep = reinterpret_cast<float*>(dyn + stage_bytes + (S > 0 ? kSample * S : 0));
   const int prob = blockIdx.x;
   const int h = prob / p.a.n_queries, t = prob - h * p.a.n_queries;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (tid == 0) stamp(p, prob, 0);
+  const int64_t len_t = allowed_length(p, t);
+  const uint8_t* codes = p.a.codes + h * p.a.codes_head_stride;
+  constexpr int kGroups = kSample / kThreads / 4;
+  if constexpr (S > 0) {
+#pragma unroll
+    for (int u = 0; u < kGroups; ++u) {
+      const int64_t g0 = sample_group_start(len_t, u);
+      if (g0 + 3 < len_t) copy_group_async<S>(sample + (tid + u * kThreads) * 4 * S, codes + g0 * S);
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+  }
   build_qlut<T>(p, h, t, qf, ql, lut, stage);
   if (tid == 0) stamp(p, prob, 9);
-  const int SC = p.a.subspaces * p.a.codewords;
+  const int C = p.a.codewords;
+  const int SC = p.a.subspaces * C;
   float* gl = p.ws_lut + (size_t)prob * kMaxLut;
   for (int e = tid; e < SC; e += blockDim.x) gl[e] = lut[e];
   for (int r = tid; r < p.a.rank_dim; r += blockDim.x) p.ws_qlow[(size_t)prob * kMaxRank + r] = ql[r];
-  const int64_t len_t = allowed_length(p, t);
-  const uint8_t* codes = p.a.codes + h * p.a.codes_head_stride;
-  // each thread scores kSample / kThreads keys (groups of four, one vector load each, all loads
-  // issued before any is used); runs start on multiples of four keys
-  constexpr int kPer = kSample / kThreads;
-  uint32_t key[kPer];
-  switch (p.vec_codes ? p.a.subspaces : 0) {
-    case 1: sample_keys<1>(p, codes, lut, t, len_t, key); break;
-    case 2: sample_keys<2>(p, codes, lut, t, len_t, key); break;
-    case 4: sample_keys<4>(p, codes, lut, t, len_t, key); break;
-    case 8: sample_keys<8>(p, codes, lut, t, len_t, key); break;
-    default: sample_keys<0>(p, codes, lut, t, len_t, key); break;
-  }
-  uint32_t* hist = reinterpret_cast<uint32_t*>(dyn);  // 4096 bins; the stage is no longer needed
-  for (int b = tid; b < 4096; b += blockDim.x) hist[b] = 0u;
-  __syncthreads();
-  if (tid == 0) stamp(p, prob, 10);
-  int nv = 0;
-#pragma unroll
-  for (int u = 0; u < kPer; ++u) {
-    // one shared atomic per distinct bin of the warp (sample keys crowd a few bins)
-    const uint32_t bin = key[u] ? (key[u] >> 20) : 0xFFFFFFFFu;
-    const unsigned same = __match_any_sync(0xFFFFFFFFu, bin);
-    if (key[u] && (same & ((1u << lane) - 1u)) == 0u) atomicAdd(&hist[bin], static_cast<uint32_t>(__popc(same)));
-    nv += key[u] != 0u;
-  }
-  const int n_s = block_sum_int(nv, scratch);
-  if (tid == 0) stamp(p, prob, 11);
-  const int64_t k_est = imin64(p.sl_cap, len_t);
-  const int64_t r = (2 * k_est * n_s + len_t - 1) / (len_t > 0 ? len_t : 1) + 8;
-  if (tid == 0) t0_sh = 1u;
-  __syncthreads();
-  if (n_s > 0 && r < n_s) {
-    // thread j owns bins 4095-8j .. 4088-8j (descending); find the bin holding the r-th best
-    uint32_t mine[8];
-    int c = 0;
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      mine[q] = hist[4095 - (8 * tid + q)];
-      c += static_cast<int>(mine[q]);
-    }
-    int incl = warp_incl_scan(c);
-    if (lane == 31) wtot[warp] = incl;
-    __syncthreads();
-    for (int w = 0; w < warp; ++w) incl += wtot[w];
-    const int excl = incl - c;
-    if (excl < r && incl >= r) {
-      int run = excl;
-      for (int q = 0; q < 8; ++q) {
-        run += static_cast<int>(mine[q]);
-        if (run >= r) {
-          t0_sh = static_cast<uint32_t>(4095 - (8 * tid + q)) << 20;
-          break;
-        }
+  const bool rep = S > 0 && p.prep_rep;
+  if (rep) {
+    for (int e0 = warp * 32; e0 < SC; e0 += blockDim.x) {
+      const float v = (e0 + lane < SC) ? lut[e0 + lane] : 0.f;
+#pragma unroll 8
+      for (int k = 0; k < 32; ++k) {
+        const float x = __shfl_sync(0xFFFFFFFFu, v, k);
+        if (e0 + k < SC) lut_rep[(e0 + k) * 32 + lane] = x;
       }
     }
   }
+  uint32_t* skeys = reinterpret_cast<uint32_t*>(dyn);  // kSample keys; the stage is no longer needed
+  if constexpr (S > 0) asm volatile("cp.async.wait_all;\n" ::: "memory");
   __syncthreads();
+  int nv = 0;
+  uint32_t top[4] = {0u, 0u, 0u, 0u};
+  const float* rep_lane = lut_rep + lane;
+#pragma unroll 1
+  for (int u = 0; u < kGroups; ++u) {
+    const int g = tid + u * kThreads;
+    const int64_t g0 = sample_group_start(len_t, u);
+    uint32_t k4[4];
+    if (S > 0 && g0 + 3 < len_t) {
+      const Codes4<(S > 0 ? S : 1)> c = load_codes4_shared<(S > 0 ? S : 1)>(sample, g * 4);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float sum = rep ? adc_rep_rt<(S > 0 ? S : 1)>(c, j, rep_lane, C)
+                              : adc_plain<(S > 0 ? S : 1), 0>(c, j, lut, C);
+        k4[j] = key_allowed(p, t, g0 + j, len_t) ? ordered_key(finish_score(sum, p)) : 0u;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) k4[j] = adc_key(p, codes, lut, t, g0 + j, len_t);
+    }
+    *reinterpret_cast<uint4*>(skeys + 4 * g) = make_uint4(k4[0], k4[1], k4[2], k4[3]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      top4_insert(top, k4[j]);
+      nv += k4[j] != 0u;
+    }
+  }
+  *reinterpret_cast<uint4*>(tops + 4 * tid) = make_uint4(top[0], top[1], top[2], top[3]);
+  if (tid == 0) stamp(p, prob, 10);
+  const int n_s = block_sum_int(nv, scratch);  // ends with a barrier: skeys and tops are complete
+  if (tid == 0) stamp(p, prob, 11);
+  const int64_t k_est = imin64(p.sl_cap, len_t);
+  const int64_t r = (2 * k_est * n_s + len_t - 1) / (len_t > 0 ? len_t : 1) + 8;
+  uint32_t t0 = 1u;
+  if (n_s > 0 && r < n_s) {
+    const bool small = r <= 4 * kThreads;
+    const uint32_t* items = small ? tops : skeys;
+    auto item = [&](int i) -> unsigned long long { return static_cast<unsigned long long>(items[i]); };
+    const SelectThreshold thr = cta_radix_select(item, small ? 4 * kThreads : kSample, static_cast<int>(r), &sel);
+    t0 = static_cast<uint32_t>(thr.prefix);
+  }
   if (tid == 0) {
     uint32_t* ctrl = p.ws_ctrl + (size_t)prob * CTRL_WORDS;
     ctrl[CTRL_NCAND] = 0u;
-    ctrl[CTRL_T0] = t0_sh > 1u ? t0_sh : 1u;
+    ctrl[CTRL_T0] = t0 > 1u ? t0 : 1u;
     stamp(p, prob, 1);
   }
 }
 
-// scan: the single pass over the codes; keys >= T0 become candidates.  Specialised on the code
-// shape: S bytes per key and C codewords (C == 0: any).  For 4x64 the first two subspaces are
-// looked up in a pair table pair[c1][c0] = lut0[c0] + lut1[c1], the same fp32 sum as the
-// sequential accumulation.  Scores are compared with the threshold as floats; the ordered key
-// is computed only for the keys that are taken.
+// LUT lookup of key j in the bank-replicated table: entry e lives at lut[e * 32 + lane], so
+// the 32 lanes of a warp read 32 different banks whatever their codes are.  C is a power of
+// two; codes are masked to it (a valid catalog never holds a code >= C).
 template <int S, int C>
-__device__ __forceinline__ float adc_fast(const Codes4<S>& c, int j, const float* lut, const float* pair, int Crt) {
-  if constexpr (S == 4 && C == 64) {
-    const uint32_t w = (j == 0) ? c.a.x : (j == 1) ? c.a.y : (j == 2) ? c.a.z : c.a.w;
-    const float s01 = pair[(w & 0x3Fu) | ((w >> 2) & 0xFC0u)];
-    const float s2 = lut[2 * 64 + ((w >> 16) & 0x3Fu)];
-    const float s3 = lut[3 * 64 + (w >> 24)];
-    return __fadd_rn(__fadd_rn(s01, s2), s3);
-  } else {
-    const int cw = C > 0 ? C : Crt;
-    float sum = lut[code_at<S>(c, j, 0)];
+__device__ __forceinline__ float adc_rep(const Codes4<S>& c, int j, const float* lut_lane) {
+  float sum = lut_lane[(code_at<S>(c, j, 0) & (C - 1)) * 32];
 #pragma unroll
-    for (int s2 = 1; s2 < S; ++s2) sum = __fadd_rn(sum, lut[s2 * cw + code_at<S>(c, j, s2)]);
-    return sum;
-  }
+  for (int s = 1; s < S; ++s) sum = __fadd_rn(sum, lut_lane[(s * C + (code_at<S>(c, j, s) & (C - 1))) * 32]);
+  return sum;
 }
 
-template <int S, int C>
+// scan: the single pass over the codes; keys >= T0 become candidates.  One CTA scans
+// kScanKeys keys of one problem.  For the common codebook shapes (S * C <= 256, C a power of
+// two) the LUT is replicated 32 times across the banks, so the random lookups are free of bank
+// conflicts; the score of every key is the canonical sequential fp32 sum.  Candidates are rare
+// (about 2x the shortlist among all keys), so each one takes a shared atomic of its own and the
+// CTA publishes its list with one global atomic.
+template <int S, int C, bool POW2>
 __global__ void __launch_bounds__(kScanThreads, 4) decode_scan_kernel(const DecodeParams p) {
-  __shared__ float lut[kMaxLut];
-  __shared__ float pair[(S == 4 && C == 64) ? 4096 : 1];
+  constexpr bool kRep = (S > 0) && (C > 0) && (S * C <= kRepEntries);
+  constexpr int kInFlight = S == 8 ? 2 : kGroupsInFlight;  // 4-key groups loaded ahead per thread
+  __shared__ float lut[kRep ? kRepEntries * 32 : kMaxLut];
   __shared__ uint2 local[kScanLocalCands];  // this CTA's candidates, flushed with one atomic
   __shared__ uint32_t n_local;
   __shared__ uint32_t flush_base;
   const int prob = blockIdx.y, seg = blockIdx.x;
   const int h = prob / p.a.n_queries, t = prob - h * p.a.n_queries;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   uint32_t* ctrl = p.ws_ctrl + (size_t)prob * CTRL_WORDS;
   const uint32_t t0 = __ldcg(ctrl + CTRL_T0);
   const int SC = p.a.subspaces * p.a.codewords;
   const float* glut = p.ws_lut + (size_t)prob * kMaxLut;
-  for (int e = threadIdx.x; e < SC; e += blockDim.x) lut[e] = __ldcg(glut + e);
-  if (threadIdx.x == 0) n_local = 0u;
-  __syncthreads();
-  if constexpr (S == 4 && C == 64) {
-    for (int e = threadIdx.x; e < 4096; e += blockDim.x) pair[e] = __fadd_rn(lut[e & 63], lut[64 + (e >> 6)]);
-    __syncthreads();
-  }
   const int64_t len_t = allowed_length(p, t);
   const int64_t i0 = (int64_t)seg * kScanKeys;
   const int64_t i1 = min(len_t, i0 + kScanKeys);
-  if (i0 >= i1) return;
-  const uint8_t* codes = p.a.codes + h * p.a.codes_head_stride;
-  uint2* cand = p.ws_cand + (size_t)prob * p.a.key_len;
-  const int lane = threadIdx.x & 31;
-  const unsigned lt = (1u << lane) - 1u;
-  // Candidates go to shared memory (one shared atomic per warp and step); when that buffer is
-  // full they go straight to the global list.
-  auto append = [&](bool take, uint32_t key, int64_t i) {
-    const unsigned b = __ballot_sync(0xFFFFFFFFu, take);
-    if (b == 0u) return;
-    uint32_t base = 0;
-    if (lane == 0) base = atomicAdd(&n_local, static_cast<uint32_t>(__popc(b)));
-    base = __shfl_sync(0xFFFFFFFFu, base, 0);
-    if (take) {
-      const uint32_t pos = base + __popc(b & lt);
-      if (pos < static_cast<uint32_t>(kScanLocalCands)) {
-        local[pos] = make_uint2(key, static_cast<uint32_t>(i));
-      } else {
-        const uint32_t g = atomicAdd(ctrl + CTRL_NCAND, 1u);
-        if (static_cast<int64_t>(g) < p.a.key_len) cand[g] = make_uint2(key, static_cast<uint32_t>(i));
+  if (i0 >= i1) return;  // uniform over the block
+  const bool fast = (S > 0) && p.a.allowed_mask == nullptr && ((i1 - i0) & 3) == 0;
+  if (kRep && fast) {
+    // warp w fills entries w*32 .. w*32+31 (+ multiples of blockDim.x); lane l writes copy l
+    for (int e0 = warp * 32; e0 < SC; e0 += blockDim.x) {
+      const float v = (e0 + lane < SC) ? __ldcg(glut + e0 + lane) : 0.f;
+#pragma unroll 8
+      for (int k = 0; k < 32; ++k) {
+        const float x = __shfl_sync(0xFFFFFFFFu, v, k);
+        if (e0 + k < SC) lut[(e0 + k) * 32 + lane] = x;
       }
     }
+  } else {
+    for (int e = tid; e < SC; e += blockDim.x) lut[e] = __ldcg(glut + e);
+  }
+  if (tid == 0) n_local = 0u;
+  __syncthreads();
+  const uint8_t* codes = p.a.codes + h * p.a.codes_head_stride;
+  uint2* cand = p.ws_cand + (size_t)prob * p.a.key_len;
+  auto take = [&](uint32_t key, int64_t i) {
+    const uint32_t pos = atomicAdd(&n_local, 1u);
+    if (pos < static_cast<uint32_t>(kScanLocalCands)) {
+      local[pos] = make_uint2(key, static_cast<uint32_t>(i));
+    } else {
+      const uint32_t g = atomicAdd(ctrl + CTRL_NCAND, 1u);
+      if (static_cast<int64_t>(g) < p.a.key_len) cand[g] = make_uint2(key, static_cast<uint32_t>(i));
+    }
   };
-  const bool fast = (S > 0) && p.a.allowed_mask == nullptr && ((i1 - i0) & 3) == 0;
-  bool done = false;
   if constexpr (S > 0) {
     if (fast) {
       const float t0f = (t0 <= 1u) ? -INFINITY : key_to_float(t0);
       const float scale = p.inv_sqrt_r;
-      const bool pow2 = p.sqrt_r_pow2 != 0;
       const int ngroups = static_cast<int>((i1 - i0) >> 2);
       const uint8_t* cbase = codes + i0 * S;
-      for (int gb = (threadIdx.x & ~31); gb < ngroups; gb += blockDim.x * kGroupsInFlight) {
-        Codes4<S> c[kGroupsInFlight];
+      const float* lut_lane = lut + lane;
+      auto score = [&](const Codes4<S>& c, int j) -> float {
+        float sum;
+        if constexpr (kRep) sum = adc_rep<S, C>(c, j, lut_lane);
+        else sum = adc_plain<S, C>(c, j, lut, p.a.codewords);
+        if constexpr (POW2) return __fmul_rn(sum, scale);
+        else return __fdiv_rn(sum, p.sqrt_r);
+      };
+      const int tile = kScanThreads * kInFlight;
+      const int nfull = ngroups - ngroups % tile;
+      for (int gb = tid; gb < nfull; gb += tile) {
+        Codes4<S> c[kInFlight];
 #pragma unroll
-        for (int u = 0; u < kGroupsInFlight; ++u) {
-          const int g = gb + lane + u * blockDim.x;
-          if (g < ngroups) c[u] = load_codes4<S>(cbase, 4 * g);
-        }
+        for (int u = 0; u < kInFlight; ++u) c[u] = load_codes4<S>(cbase, 4 * (gb + u * kScanThreads));
 #pragma unroll
-        for (int u = 0; u < kGroupsInFlight; ++u) {
-          const int g = gb + lane + u * blockDim.x;
-          float sc4[4];
-          bool any = false;
+        for (int u = 0; u < kInFlight; ++u) {
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const float sum = adc_fast<S, C>(c[u], j, lut, pair, p.a.codewords);
-            sc4[j] = pow2 ? __fmul_rn(sum, scale) : __fdiv_rn(sum, p.sqrt_r);
-            any |= (g < ngroups) && (sc4[j] >= t0f);
-          }
-          if (__any_sync(0xFFFFFFFFu, any)) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const bool take = (g < ngroups) && (sc4[j] >= t0f);
-              append(take, ordered_key(sc4[j]), i0 + 4 * g + j);
-            }
+            const float sc = score(c[u], j);
+            if (sc >= t0f) take(ordered_key(sc), i0 + 4 * (gb + u * kScanThreads) + j);
           }
         }
       }
-      done = true;
+      for (int g = nfull + tid; g < ngroups; g += kScanThreads) {
+        const Codes4<S> c = load_codes4<S>(cbase, 4 * g);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float sc = score(c, j);
+          if (sc >= t0f) take(ordered_key(sc), i0 + 4 * g + j);
+        }
+      }
     }
   }
-  if (!done) {
-    // masked or ragged segments: generic per-key path
+  if (!fast) {
+    // masked or ragged segments: generic per-key path over the plain LUT layout
     scan_segment<S>(p, codes, lut, t, len_t, i0, i1, [&](int64_t i, uint32_t key) {
-      append(key != 0u && key >= t0, key, i);
+      if (key != 0u && key >= t0) take(key, i);
     });
   }
   __syncthreads();
   const uint32_t nl = min(n_local, static_cast<uint32_t>(kScanLocalCands));
-  if (threadIdx.x == 0 && nl > 0) flush_base = atomicAdd(ctrl + CTRL_NCAND, nl);
+  if (tid == 0 && nl > 0) flush_base = atomicAdd(ctrl + CTRL_NCAND, nl);
   __syncthreads();
-  if (nl > 0) {
-    for (uint32_t e = threadIdx.x; e < nl; e += blockDim.x) {
-      const uint32_t g = flush_base + e;
-      if (static_cast<int64_t>(g) < p.a.key_len) cand[g] = local[e];
-    }
+  for (uint32_t e = tid; e < nl; e += blockDim.x) {
+    const uint32_t g = flush_base + e;
+    if (static_cast<int64_t>(g) < p.a.key_len) cand[g] = local[e];
   }
 }
 
@@ -939,7 +991,16 @@ static int plan_decode(const sva_decode_args* a, DecodePlan* plan) {
 
 template <int S, int C>
 static void launch_scan(const DecodeParams& p, int P, cudaStream_t stream) {
-  decode_scan_kernel<S, C><<<dim3(p.nseg, P), kScanThreads, 0, stream>>>(p);
+  if (p.sqrt_r_pow2) decode_scan_kernel<S, C, true><<<dim3(p.nseg, P), kScanThreads, 0, stream>>>(p);
+  else decode_scan_kernel<S, C, false><<<dim3(p.nseg, P), kScanThreads, 0, stream>>>(p);
+}
+
+template <typename T, int S>
+static int launch_prep(const DecodeParams& p, int P, int smem, cudaStream_t stream) {
+  int rc = ensure_smem_attr(reinterpret_cast<const void*>(decode_prep_kernel<T, S>), smem);
+  if (rc != SVA_OK) return rc;
+  decode_prep_kernel<T, S><<<P, kThreads, smem, stream>>>(p);
+  return SVA_OK;
 }
 
 template <typename T>
@@ -959,20 +1020,40 @@ static int launch_decode(DecodePlan& plan, void* ws, cudaStream_t stream) {
     p.ws_ctrl = reinterpret_cast<uint32_t*>(base + reinterpret_cast<size_t>(p.ws_ctrl));
     p.ws_cand = reinterpret_cast<uint2*>(base + reinterpret_cast<size_t>(p.ws_cand));
     p.dbg_ts = static_cast<unsigned long long*>(debug_timestamps());
-    const int prep_smem = std::max(4 * p.a.head_dim * p.a.rank_dim, 4 * 4096);
-    rc = ensure_smem_attr(reinterpret_cast<const void*>(decode_prep_kernel<T>), prep_smem);
+    const int prep_base = prep_stage_bytes(p.a.head_dim, p.a.rank_dim);
+    const bool prep_vec = p.vec_codes && prep_base + kSample * p.a.subspaces <= kPrepSmemLimit;
+    int prep_smem = prep_base + (prep_vec ? kSample * p.a.subspaces : 0);
+    const int rep_bytes = p.a.subspaces * p.a.codewords * 32 * 4;
+    p.prep_rep = (prep_vec && p.a.subspaces * p.a.codewords <= kRepEntries &&
+                  prep_smem + rep_bytes <= kPrepSmemLimit) ? 1 : 0;
+    if (p.prep_rep) prep_smem += rep_bytes;
+    switch (prep_vec ? p.a.subspaces : 0) {
+      case 1: rc = launch_prep<T, 1>(p, P, prep_smem, stream); break;
+      case 2: rc = launch_prep<T, 2>(p, P, prep_smem, stream); break;
+      case 4: rc = launch_prep<T, 4>(p, P, prep_smem, stream); break;
+      case 8: rc = launch_prep<T, 8>(p, P, prep_smem, stream); break;
+      default: rc = launch_prep<T, 0>(p, P, prep_smem, stream); break;
+    }
     if (rc != SVA_OK) return rc;
-    decode_prep_kernel<T><<<P, kThreads, prep_smem, stream>>>(p);
     profile_mark(0, stream);
     const int C = p.a.codewords;
     switch (p.vec_codes ? p.a.subspaces : 0) {
-      case 1: launch_scan<1, 0>(p, P, stream); break;
-      case 2: launch_scan<2, 0>(p, P, stream); break;
+      case 1:
+        if (C == 256) launch_scan<1, 256>(p, P, stream);
+        else launch_scan<1, 0>(p, P, stream);
+        break;
+      case 2:
+        if (C == 128) launch_scan<2, 128>(p, P, stream);
+        else launch_scan<2, 0>(p, P, stream);
+        break;
       case 4:
         if (C == 64) launch_scan<4, 64>(p, P, stream);
         else launch_scan<4, 0>(p, P, stream);
         break;
-      case 8: launch_scan<8, 0>(p, P, stream); break;
+      case 8:
+        if (C == 32) launch_scan<8, 32>(p, P, stream);
+        else launch_scan<8, 0>(p, P, stream);
+        break;
       default: launch_scan<0, 0>(p, P, stream); break;
     }
     profile_mark(1, stream);
