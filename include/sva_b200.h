@@ -162,6 +162,29 @@ int sva_postings_build(const uint8_t* codes, int64_t codes_head_stride, int32_t 
                        void* stream);
 
 /* ---------------------------------------------------------------------------------------
+ * No-alloc variant of sva_postings_build.  No reference counterpart: the reference builds its
+ * posting lists with torch ops that allocate as they go (sva/llama.py:626-657).
+ *
+ * For callers that cannot allocate device memory on the call path: a host runtime bound to
+ * this library through a C foreign-function interface, which has no device allocator of its
+ * own, or a server that fixes its device memory when it starts.  The chunk histograms live in
+ * a buffer inside the library, SVA_POSTINGS_NOALLOC_SCRATCH_BYTES per device, so the call takes
+ * no workspace; the outputs are the caller's, exactly as for sva_postings_build.
+ * Limit: sva_postings_workspace_size(n_heads, subspaces, codewords, key_len), that is
+ * 4 * H * S * C * ceil(L / 4096) bytes, must not exceed the buffer, else SVA_ERR_WORKSPACE
+ * (9 heads of 4x64 codes: up to 3.7M keys; 1 head of 1x256 codes: up to 33M keys).
+ * Calls on one device share the buffer: two calls that may overlap in time (on different
+ * streams, or from host threads without ordering between them) race and corrupt each other's
+ * lists, so issue them on one stream.  The first call on each device looks up the buffer's
+ * address, which may load the library's device module: make it before any stream capture.
+ * Nothing is claimed about CUDA graph capture of this entry point.
+ * ------------------------------------------------------------------------------------- */
+#define SVA_POSTINGS_NOALLOC_SCRATCH_BYTES (8u << 20)
+int sva_postings_build_noalloc(const uint8_t* codes, int64_t codes_head_stride, int32_t n_heads, int32_t subspaces,
+                               int32_t codewords, int64_t key_len, int32_t* counts, int32_t* offsets, int32_t* ids,
+                               int64_t ids_sub_stride, int32_t* max_bucket, void* stream);
+
+/* ---------------------------------------------------------------------------------------
  * Inverted-index summon -> rank rescore -> verify for one query token per head.
  * static  (dynamic == 0), replaces sva/llama.py:427-576: candidates are the posting lists of the
  *         top `cells` codewords per subspace (code score desc, codeword asc) plus the tail keys

@@ -33,6 +33,7 @@ STAT_VERIFIED = 4
 STAT_CELL_VISITS = 5
 STAT_SELECT_FALLBACKS = 6
 STAT_COUNT = 8
+POSTINGS_NOALLOC_SCRATCH_BYTES = 8 << 20  # SVA_POSTINGS_NOALLOC_SCRATCH_BYTES
 
 # Every symbol include/sva_b200.h declares (checked by the CPU test suite).
 EXPORTED = (
@@ -47,6 +48,7 @@ EXPORTED = (
     "sva_decode",
     "sva_postings_workspace_size",
     "sva_postings_build",
+    "sva_postings_build_noalloc",
     "sva_inverted_workspace_size",
     "sva_decode_inverted",
     "sva_top_unique",
@@ -186,6 +188,8 @@ def load() -> ctypes.CDLL:
             "sva_postings_workspace_size": ([c_i32, c_i32, c_i32, c_i64], c_sz),
             "sva_postings_build": ([c_vp, c_i64, c_i32, c_i32, c_i32, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp,
                                     c_sz, c_vp], ctypes.c_int),
+            "sva_postings_build_noalloc": ([c_vp, c_i64, c_i32, c_i32, c_i32, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp,
+                                            c_vp], ctypes.c_int),
             "sva_inverted_workspace_size": ([ctypes.POINTER(InvertedArgs)], c_sz),
             "sva_decode_inverted": ([ctypes.POINTER(InvertedArgs), c_vp, c_sz, c_vp], ctypes.c_int),
             "sva_top_unique": ([c_vp, c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp,

@@ -11,6 +11,8 @@
 //   2. per (h, s): counts, offsets, and the base of every (chunk, c) run (in place)
 //   3. per chunk: stable scatter; within a round of 256 keys the rank of a key among same-code
 //      keys comes from a warp match plus per-warp counters, so ids keep key order.
+#include <mutex>
+
 #include "sva_common.cuh"
 #include "sva_internal.h"
 
@@ -170,4 +172,44 @@ extern "C" int sva_postings_build(const uint8_t* codes, int64_t codes_head_strid
   e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
   return SVA_OK;
+}
+
+// ---- no-alloc variant ---------------------------------------------------------------------
+// The chunk histograms come from a fixed buffer inside the library (one per device, created
+// with the module) instead of a caller-provided workspace.  Nothing in it has to start at zero:
+// the histogram pass writes every entry the later passes read, and the call zeroes *max_bucket.
+
+static __device__ __align__(256) unsigned char g_postings_scratch[SVA_POSTINGS_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kTrackedDevices = 64;
+std::mutex g_postings_scratch_mu;
+void* g_postings_scratch_addr[kTrackedDevices] = {};
+}  // namespace
+
+extern "C" int sva_postings_build_noalloc(const uint8_t* codes, int64_t codes_head_stride, int32_t n_heads,
+                                          int32_t subspaces, int32_t codewords, int64_t key_len, int32_t* counts,
+                                          int32_t* offsets, int32_t* ids, int64_t ids_sub_stride, int32_t* max_bucket,
+                                          void* stream) {
+  const size_t need = sva_postings_workspace_size(n_heads, subspaces, codewords, key_len);
+  if (need > static_cast<size_t>(SVA_POSTINGS_NOALLOC_SCRATCH_BYTES))
+    return set_error(SVA_ERR_WORKSPACE, "postings need more than the static scratch of sva_postings_build_noalloc");
+  void* scratch = nullptr;
+  if (need > 0) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
+    if (dev < 0 || dev >= kTrackedDevices) return set_error(SVA_ERR_CUDA, "device ordinal out of range");
+    std::lock_guard<std::mutex> lock(g_postings_scratch_mu);
+    if (!g_postings_scratch_addr[dev]) {
+      void* addr = nullptr;
+      e = cudaGetSymbolAddress(&addr, g_postings_scratch);  // resolved on the current device
+      if (e != cudaSuccess || addr == nullptr)
+        return set_error(SVA_ERR_CUDA, e != cudaSuccess ? cudaGetErrorString(e) : "null scratch address");
+      g_postings_scratch_addr[dev] = addr;
+    }
+    scratch = g_postings_scratch_addr[dev];
+  }
+  return sva_postings_build(codes, codes_head_stride, n_heads, subspaces, codewords, key_len, counts, offsets, ids,
+                            ids_sub_stride, max_bucket, scratch, need, stream);
 }
