@@ -342,7 +342,7 @@ def gpu_arm(args):
         one_query(st)
     torch.cuda.synchronize()
 
-    grid_schedule = local_keys > 32768
+    grid_schedule = local_keys > 32768 or world > 1  # shards always run prep + scan + top
     n_prof = 3 if grid_schedule else 1
     prof = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(n_prof + 1)]
     for e in prof:  # torch creates the CUDA event on its first record
@@ -409,20 +409,26 @@ def gpu_arm(args):
     ab = algorithmic_bytes(args)
     local_frac = local_keys / args.keys
     if grid_schedule:
-        names = ["prep", "scan", "finish"]
+        # third launch: finish on one GPU (rescore + verify); on shards the local top select
+        # (its rescore / verify stages follow the all-gathers and are not separately timed)
+        names = ["prep", "scan", "finish" if world == 1 else "top"]
         kernel_bytes = {
-            # prep reads the projections and codebooks (and a 4096-key sample of the codes)
+            # prep reads the projections and codebooks (and a 16384-key sample of the codes)
             "prep": ab["codebooks"] + ab["q_proj"],
             # scan is the single pass over the codes
             "scan": ab["codes"] * local_frac,
             # finish gathers the shortlist's k_low rows and the budget's K and V rows
             "finish": ab["rescore"] + ab["verify"],
+            # top reads the scan's candidates (about 2x the shortlist, 8 bytes each)
+            "top": 2 * args.shortlist * 8 * args.heads,
         }
     else:
         names = ["fused"]
         kernel_bytes = {"fused": ab["total"] * local_frac}
     kmeans = [sum(k[j] for k in kern) / len(kern) for j in range(n_prof)]
     dom = max(range(n_prof), key=lambda j: kmeans[j])
+    if world > 1:
+        dom = names.index("scan")  # the kernel whose work the shards divide
     peak, peak_kind = measured_peaks()
     achieved = kernel_bytes[names[dom]] / (kmeans[dom] * 1e-3) / 1e9
     workload_key = f"{args.pq}_{args.heads}h_{args.keys}"
@@ -454,7 +460,7 @@ def gpu_arm(args):
     }
     launches_per_query = 3 if grid_schedule else 1
     if world > 1:
-        launches_per_query += shard.extra_launches
+        launches_per_query = 3 + shard.extra_launches
     line["gpu_launches"] = launches_per_query * qps * args.steps
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         times, threads = run_cpu_decoder(args, 1000, 1, args.cpu_seconds)
@@ -512,7 +518,8 @@ def e2e_measure(args, sets, one_query, device, group):
     obytes = sets[0]["out"].numel() * sets[0]["out"].element_size()
     return {"value": round(1000.0 * ms / n, 3), "unit": UNIT, "h2d_bytes_per_step": qbytes,
             "d2h_bytes_per_step": obytes, "queries": n,
-            "path": "sva_b200.kernels.decode (eager ctypes call per query) with pinned host q/out"}
+            "path": ("sva_b200.kernels.decode" if group is None else "sva_b200.sharded.ShardedDecoder.decode")
+                    + " (eager ctypes calls per query) with pinned host q/out"}
 
 
 def main():

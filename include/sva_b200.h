@@ -150,6 +150,37 @@ size_t sva_decode_workspace_size(const sva_decode_args* args);
 int sva_decode(const sva_decode_args* args, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------------------
+ * Key-range shards: the scan decode of one token per head with the catalog split by key range
+ * across ranks, one process per GPU.  Replaces the single-device sva/llama.py:171-328 when the
+ * cache does not live on one GPU (the reference itself is single-device).
+ *
+ * Rank r's args describe its own keys, global indices [key_offset, key_offset + key_len), with
+ * n_queries == 1, no allowed_len / allowed_mask and no shortlist_out / final_out; shortlist
+ * <= 8192.  The same args go to every stage of one decode.  The host all-gathers each stage's
+ * output over the W ranks, in rank order, before the next stage ([W][...] below):
+ *   sva_shard_summon : top_out [H][shortlist] u64 composites (coarse key << 32 | ~global index)
+ *                      of the exact local shortlist, zero padded.  Uses the workspace.
+ *   sva_shard_rescore: from gathered_top [W][H][shortlist], the global shortlist; this rank's
+ *                      members rescored and their verify logits computed -> records_out
+ *                      [H][shortlist][4] u32 (rank composite lo, hi, logit bits, 0), zero
+ *                      padded.  Takes the workspace sva_shard_summon filled, unchanged.
+ *   sva_shard_verify : from gathered_records [W][H][shortlist][4], the global budget set and
+ *                      softmax; partial_out [H][head_dim] f64 = this rank's share of the output.
+ *   sva_shard_combine: from gathered_partials [W][H][head_dim], writes args->out.
+ * Shortlist and final sets equal sva_decode's over the concatenated keys; the output equals it
+ * up to the order of exact fp64 sums.  Stats (queries, summoned, verified) are counted on rank 0.
+ * ------------------------------------------------------------------------------------- */
+size_t sva_shard_workspace_size(const sva_decode_args* args);
+int sva_shard_summon(const sva_decode_args* args, int64_t key_offset, uint64_t* top_out, void* workspace,
+                     size_t workspace_bytes, void* stream);
+int sva_shard_rescore(const sva_decode_args* args, int64_t key_offset, int32_t world, int32_t rank,
+                      const uint64_t* gathered_top, uint32_t* records_out, void* workspace, size_t workspace_bytes,
+                      void* stream);
+int sva_shard_verify(const sva_decode_args* args, int64_t key_offset, int32_t world, int32_t rank,
+                     const uint32_t* gathered_records, double* partial_out, void* stream);
+int sva_shard_combine(const sva_decode_args* args, int32_t world, const double* gathered_partials, void* stream);
+
+/* ---------------------------------------------------------------------------------------
  * Posting lists of the static inverted index.  Replaces sva/llama.py:626-657.
  * For every (head, subspace): counts [H][S][C], offsets [H][S][C+1] (CSR) and ids
  * [H][S][ids_sub_stride] holding the keys [0, key_len) grouped by code, ascending inside a cell.

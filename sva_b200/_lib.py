@@ -46,6 +46,11 @@ EXPORTED = (
     "sva_pq_scores",
     "sva_decode_workspace_size",
     "sva_decode",
+    "sva_shard_workspace_size",
+    "sva_shard_summon",
+    "sva_shard_rescore",
+    "sva_shard_verify",
+    "sva_shard_combine",
     "sva_postings_workspace_size",
     "sva_postings_build",
     "sva_postings_build_noalloc",
@@ -185,6 +190,12 @@ def load() -> ctypes.CDLL:
             "sva_pq_scores": ([c_vp, c_i32, c_i32, c_i32, c_vp, c_i32, c_i32, c_vp, c_i64, c_vp, c_vp], ctypes.c_int),
             "sva_decode_workspace_size": ([ctypes.POINTER(DecodeArgs)], c_sz),
             "sva_decode": ([ctypes.POINTER(DecodeArgs), c_vp, c_sz, c_vp], ctypes.c_int),
+            "sva_shard_workspace_size": ([ctypes.POINTER(DecodeArgs)], c_sz),
+            "sva_shard_summon": ([ctypes.POINTER(DecodeArgs), c_i64, c_vp, c_vp, c_sz, c_vp], ctypes.c_int),
+            "sva_shard_rescore": ([ctypes.POINTER(DecodeArgs), c_i64, c_i32, c_i32, c_vp, c_vp, c_vp, c_sz, c_vp],
+                                  ctypes.c_int),
+            "sva_shard_verify": ([ctypes.POINTER(DecodeArgs), c_i64, c_i32, c_i32, c_vp, c_vp, c_vp], ctypes.c_int),
+            "sva_shard_combine": ([ctypes.POINTER(DecodeArgs), c_i32, c_vp, c_vp], ctypes.c_int),
             "sva_postings_workspace_size": ([c_i32, c_i32, c_i32, c_i64], c_sz),
             "sva_postings_build": ([c_vp, c_i64, c_i32, c_i32, c_i32, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp,
                                     c_sz, c_vp], ctypes.c_int),

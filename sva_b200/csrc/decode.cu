@@ -696,6 +696,75 @@ __global__ void __launch_bounds__(kScanThreads, 4) decode_scan_kernel(const Deco
   }
 }
 
+// The exact shortlist of problem `prob` from the scan's candidates (CTA-cooperative):
+// k = min(shortlist, allowed keys) keys by (coarse key desc, key index asc).  The candidates are
+// selected in shared memory when they fit (`cand`, kCandSmem entries), else streamed from L2; if
+// fewer than k keys reached the threshold the select runs exactly over every allowed key (using
+// `lut`) and a fallback is counted.  emit(pos, key32, idx) is called once per selected key with
+// consecutive positions; returns the number selected.
+template <class Emit>
+__device__ int select_shortlist(const DecodeParams& p, int prob, int h, int t, int64_t len_t, uint2* cand, float* lut,
+                                SelectScratch* sc, int* scratch, const Emit& emit) {
+  const int tid = threadIdx.x;
+  const int64_t L = p.a.key_len;
+  const uint32_t* ctrl = p.ws_ctrl + (size_t)prob * CTRL_WORDS;
+  const uint32_t t0 = __ldcg(ctrl + CTRL_T0);
+  const int64_t n_cand64 = __ldcg(ctrl + CTRL_NCAND);
+  const int n_cand = static_cast<int>(n_cand64 < L ? n_cand64 : L);
+  int64_t n_allowed = n_cand;
+  if (t0 > 1u && n_cand < p.sl_cap) {
+    if (!p.a.allowed_mask) {
+      n_allowed = len_t;
+    } else {
+      int c = 0;
+      for (int64_t i = tid; i < len_t; i += blockDim.x) c += p.a.allowed_mask[t * p.a.mask_row_stride + i] != 0;
+      n_allowed = block_sum_int(c, scratch);
+    }
+  }
+  const int k = static_cast<int>(imin64(p.sl_cap, n_allowed));
+  const uint2* gc = p.ws_cand + (size_t)prob * L;
+  int n_sl = 0;
+  if (n_cand >= k) {
+    if (n_cand <= kCandSmem) {
+      copy_batched(cand, gc, n_cand);
+      if (tid == 0) stamp(p, prob, 12);
+      auto item = [&](int i) -> unsigned long long { return composite(cand[i].x, cand[i].y); };
+      const SelectThreshold thr = cta_radix_select(item, n_cand, k, sc);
+      n_sl = cta_compact(item, n_cand, thr, [&](int pos, int i, unsigned long long) { emit(pos, cand[i].x, cand[i].y); },
+                         scratch);
+    } else {
+      auto item = [&](int i) -> unsigned long long {
+        const uint2 v = __ldcg(gc + i);
+        return composite(v.x, v.y);
+      };
+      const SelectThreshold thr = cta_radix_select(item, n_cand, k, sc);
+      n_sl = cta_compact(item, n_cand, thr,
+                         [&](int pos, int, unsigned long long c) {
+                           emit(pos, static_cast<uint32_t>(c >> 32), ~static_cast<uint32_t>(c));
+                         },
+                         scratch);
+    }
+  } else {
+    // the sampled threshold was above the k-th best key: exact select over every key
+    for (int e = tid; e < p.a.subspaces * p.a.codewords; e += blockDim.x)
+      lut[e] = __ldcg(p.ws_lut + (size_t)prob * kMaxLut + e);
+    __syncthreads();
+    const uint8_t* codes = p.a.codes + h * p.a.codes_head_stride;
+    auto item = [&](int i) -> unsigned long long {
+      const uint32_t key = adc_key(p, codes, lut, t, i, len_t);
+      return key ? composite(key, static_cast<uint32_t>(i)) : 0ull;
+    };
+    const SelectThreshold thr = cta_radix_select(item, static_cast<int>(len_t), k, sc);
+    n_sl = cta_compact(item, static_cast<int>(len_t), thr,
+                       [&](int pos, int i, unsigned long long c) {
+                         emit(pos, static_cast<uint32_t>(c >> 32), static_cast<uint32_t>(i));
+                       },
+                       scratch);
+    if (p.a.stats && tid == 0) atomicAdd(p.a.stats + SVA_STAT_SELECT_FALLBACKS, 1ull);
+  }
+  return n_sl;
+}
+
 struct FinishSmem {
   int qf, ql, lut, sc, scratch, misc, sl, rk, fin, lg, acc, parts, cand, total;
 };
@@ -760,56 +829,8 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
   // ---- phase 1 (CTA 0): the exact shortlist ------------------------------------------------
   if (crank == 0 && tid == 0) stamp(p, prob, 2);
   if (crank == 0) {
-    const uint32_t* ctrl = p.ws_ctrl + (size_t)prob * CTRL_WORDS;
-    const uint32_t t0 = __ldcg(ctrl + CTRL_T0);
-    const int64_t n_cand64 = __ldcg(ctrl + CTRL_NCAND);
-    const int n_cand = static_cast<int>(n_cand64 < L ? n_cand64 : L);
-    int64_t n_allowed = n_cand;
-    if (t0 > 1u && n_cand < p.sl_cap) {
-      if (!p.a.allowed_mask) {
-        n_allowed = len_t;
-      } else {
-        int c = 0;
-        for (int64_t i = tid; i < len_t; i += blockDim.x) c += p.a.allowed_mask[t * p.a.mask_row_stride + i] != 0;
-        n_allowed = block_sum_int(c, scratch);
-      }
-    }
-    const int k = static_cast<int>(imin64(p.sl_cap, n_allowed));
-    const uint2* gc = p.ws_cand + (size_t)prob * L;
-    int n_sl = 0;
-    if (n_cand >= k) {
-      if (n_cand <= kCandSmem) {
-        copy_batched(cand, gc, n_cand);
-        if (tid == 0) stamp(p, prob, 12);
-        auto item = [&](int i) -> unsigned long long { return composite(cand[i].x, cand[i].y); };
-        const SelectThreshold thr = cta_radix_select(item, n_cand, k, sc);
-        n_sl = cta_compact(item, n_cand, thr, [&](int pos, int i, unsigned long long) { sl[pos] = cand[i].y; },
-                           scratch);
-      } else {
-        auto item = [&](int i) -> unsigned long long {
-          const uint2 v = __ldcg(gc + i);
-          return composite(v.x, v.y);
-        };
-        const SelectThreshold thr = cta_radix_select(item, n_cand, k, sc);
-        n_sl = cta_compact(item, n_cand, thr,
-                           [&](int pos, int, unsigned long long c) { sl[pos] = static_cast<int32_t>(~static_cast<uint32_t>(c)); },
-                           scratch);
-      }
-    } else {
-      // the sampled threshold was above the k-th best key: exact select over every key
-      for (int e = tid; e < p.a.subspaces * p.a.codewords; e += blockDim.x)
-        lut[e] = __ldcg(p.ws_lut + (size_t)prob * kMaxLut + e);
-      __syncthreads();
-      const uint8_t* codes = p.a.codes + h * p.a.codes_head_stride;
-      auto item = [&](int i) -> unsigned long long {
-        const uint32_t key = adc_key(p, codes, lut, t, i, len_t);
-        return key ? composite(key, static_cast<uint32_t>(i)) : 0ull;
-      };
-      const SelectThreshold thr = cta_radix_select(item, static_cast<int>(len_t), k, sc);
-      n_sl = cta_compact(item, static_cast<int>(len_t), thr, [&](int pos, int i, unsigned long long) { sl[pos] = i; },
-                         scratch);
-      if (p.a.stats && tid == 0) atomicAdd(p.a.stats + SVA_STAT_SELECT_FALLBACKS, 1ull);
-    }
+    const int n_sl = select_shortlist(p, prob, h, t, len_t, cand, lut, sc, scratch,
+                                      [&](int pos, uint32_t, uint32_t idx) { sl[pos] = static_cast<int32_t>(idx); });
     if (tid == 0) misc[0] = n_sl;
   }
   if (crank == 0 && tid == 0) stamp(p, prob, 3);
@@ -921,7 +942,7 @@ struct DecodePlan {
   size_t smem_bytes;
 };
 
-static int plan_decode(const sva_decode_args* a, DecodePlan* plan) {
+static int plan_decode(const sva_decode_args* a, DecodePlan* plan, bool force_grid = false) {
   if (!a) return set_error(SVA_ERR_SHAPE, "null args");
   if (a->n_heads <= 0 || a->n_kv_heads <= 0 || a->n_heads % a->n_kv_heads != 0)
     return set_error(SVA_ERR_SHAPE, "n_heads must be a positive multiple of n_kv_heads");
@@ -958,7 +979,7 @@ static int plan_decode(const sva_decode_args* a, DecodePlan* plan) {
                     ? 1
                     : 0;
   const int64_t P = static_cast<int64_t>(a->n_heads) * a->n_queries;
-  p.grid_mode = a->key_len > kFusedMaxKeys ? 1 : 0;
+  p.grid_mode = (force_grid || a->key_len > kFusedMaxKeys) ? 1 : 0;
   p.nseg = static_cast<int>((a->key_len + kScanKeys - 1) / kScanKeys);
   int dbg_cap = 1;
   if (a->shortlist_out || a->final_out)
@@ -1003,6 +1024,60 @@ static int launch_prep(const DecodeParams& p, int P, int smem, cudaStream_t stre
   return SVA_OK;
 }
 
+// Points the planned workspace offsets at `ws`.
+static void bind_workspace(DecodeParams& p, void* ws) {
+  char* base = static_cast<char*>(ws);
+  p.ws_qlow = reinterpret_cast<float*>(base + reinterpret_cast<size_t>(p.ws_qlow));
+  p.ws_lut = reinterpret_cast<float*>(base + reinterpret_cast<size_t>(p.ws_lut));
+  p.ws_ctrl = reinterpret_cast<uint32_t*>(base + reinterpret_cast<size_t>(p.ws_ctrl));
+  p.ws_cand = reinterpret_cast<uint2*>(base + reinterpret_cast<size_t>(p.ws_cand));
+}
+
+// The grid schedule's prep and scan launches (q_low, LUT, threshold, candidates).
+template <typename T>
+static int launch_prep_scan(DecodeParams& p, cudaStream_t stream) {
+  const int P = p.a.n_heads * p.a.n_queries;
+  int rc;
+  const int prep_base = prep_stage_bytes(p.a.head_dim, p.a.rank_dim);
+  const bool prep_vec = p.vec_codes && prep_base + kSample * p.a.subspaces <= kPrepSmemLimit;
+  int prep_smem = prep_base + (prep_vec ? kSample * p.a.subspaces : 0);
+  const int rep_bytes = p.a.subspaces * p.a.codewords * 32 * 4;
+  p.prep_rep = (prep_vec && p.a.subspaces * p.a.codewords <= kRepEntries &&
+                prep_smem + rep_bytes <= kPrepSmemLimit) ? 1 : 0;
+  if (p.prep_rep) prep_smem += rep_bytes;
+  switch (prep_vec ? p.a.subspaces : 0) {
+    case 1: rc = launch_prep<T, 1>(p, P, prep_smem, stream); break;
+    case 2: rc = launch_prep<T, 2>(p, P, prep_smem, stream); break;
+    case 4: rc = launch_prep<T, 4>(p, P, prep_smem, stream); break;
+    case 8: rc = launch_prep<T, 8>(p, P, prep_smem, stream); break;
+    default: rc = launch_prep<T, 0>(p, P, prep_smem, stream); break;
+  }
+  if (rc != SVA_OK) return rc;
+  profile_mark(0, stream);
+  const int C = p.a.codewords;
+  switch (p.vec_codes ? p.a.subspaces : 0) {
+    case 1:
+      if (C == 256) launch_scan<1, 256>(p, P, stream);
+      else launch_scan<1, 0>(p, P, stream);
+      break;
+    case 2:
+      if (C == 128) launch_scan<2, 128>(p, P, stream);
+      else launch_scan<2, 0>(p, P, stream);
+      break;
+    case 4:
+      if (C == 64) launch_scan<4, 64>(p, P, stream);
+      else launch_scan<4, 0>(p, P, stream);
+      break;
+    case 8:
+      if (C == 32) launch_scan<8, 32>(p, P, stream);
+      else launch_scan<8, 0>(p, P, stream);
+      break;
+    default: launch_scan<0, 0>(p, P, stream); break;
+  }
+  profile_mark(1, stream);
+  return SVA_OK;
+}
+
 template <typename T>
 static int launch_decode(DecodePlan& plan, void* ws, cudaStream_t stream) {
   DecodeParams& p = plan.p;
@@ -1014,49 +1089,10 @@ static int launch_decode(DecodePlan& plan, void* ws, cudaStream_t stream) {
     decode_fused_kernel<T><<<P, kThreads, plan.smem_bytes, stream>>>(p);
     profile_mark(0, stream);
   } else {
-    char* base = static_cast<char*>(ws);
-    p.ws_qlow = reinterpret_cast<float*>(base + reinterpret_cast<size_t>(p.ws_qlow));
-    p.ws_lut = reinterpret_cast<float*>(base + reinterpret_cast<size_t>(p.ws_lut));
-    p.ws_ctrl = reinterpret_cast<uint32_t*>(base + reinterpret_cast<size_t>(p.ws_ctrl));
-    p.ws_cand = reinterpret_cast<uint2*>(base + reinterpret_cast<size_t>(p.ws_cand));
+    bind_workspace(p, ws);
     p.dbg_ts = static_cast<unsigned long long*>(debug_timestamps());
-    const int prep_base = prep_stage_bytes(p.a.head_dim, p.a.rank_dim);
-    const bool prep_vec = p.vec_codes && prep_base + kSample * p.a.subspaces <= kPrepSmemLimit;
-    int prep_smem = prep_base + (prep_vec ? kSample * p.a.subspaces : 0);
-    const int rep_bytes = p.a.subspaces * p.a.codewords * 32 * 4;
-    p.prep_rep = (prep_vec && p.a.subspaces * p.a.codewords <= kRepEntries &&
-                  prep_smem + rep_bytes <= kPrepSmemLimit) ? 1 : 0;
-    if (p.prep_rep) prep_smem += rep_bytes;
-    switch (prep_vec ? p.a.subspaces : 0) {
-      case 1: rc = launch_prep<T, 1>(p, P, prep_smem, stream); break;
-      case 2: rc = launch_prep<T, 2>(p, P, prep_smem, stream); break;
-      case 4: rc = launch_prep<T, 4>(p, P, prep_smem, stream); break;
-      case 8: rc = launch_prep<T, 8>(p, P, prep_smem, stream); break;
-      default: rc = launch_prep<T, 0>(p, P, prep_smem, stream); break;
-    }
+    rc = launch_prep_scan<T>(p, stream);
     if (rc != SVA_OK) return rc;
-    profile_mark(0, stream);
-    const int C = p.a.codewords;
-    switch (p.vec_codes ? p.a.subspaces : 0) {
-      case 1:
-        if (C == 256) launch_scan<1, 256>(p, P, stream);
-        else launch_scan<1, 0>(p, P, stream);
-        break;
-      case 2:
-        if (C == 128) launch_scan<2, 128>(p, P, stream);
-        else launch_scan<2, 0>(p, P, stream);
-        break;
-      case 4:
-        if (C == 64) launch_scan<4, 64>(p, P, stream);
-        else launch_scan<4, 0>(p, P, stream);
-        break;
-      case 8:
-        if (C == 32) launch_scan<8, 32>(p, P, stream);
-        else launch_scan<8, 0>(p, P, stream);
-        break;
-      default: launch_scan<0, 0>(p, P, stream); break;
-    }
-    profile_mark(1, stream);
     rc = ensure_smem_attr(reinterpret_cast<const void*>(decode_finish_kernel<T>), static_cast<int>(plan.smem_bytes));
     if (rc != SVA_OK) return rc;
     decode_finish_kernel<T><<<P * kCluster, kThreads, plan.smem_bytes, stream>>>(p, plan.fin_lay);
@@ -1088,3 +1124,5 @@ extern "C" int sva_decode(const sva_decode_args* args, void* workspace, size_t w
     default: return sva::launch_decode<__half>(plan, workspace, s);
   }
 }
+
+#include "decode_shard.cuh"

@@ -116,18 +116,13 @@ def pq_scores(q_low: torch.Tensor, codebooks: torch.Tensor, codes_u8: torch.Tens
     return out
 
 
-def decode(q: torch.Tensor, q_proj: torch.Tensor, scale: torch.Tensor, codebooks: torch.Tensor, codes: torch.Tensor,
-           k_low: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, shortlist: int, budget: int,
-           softmax_scale: float | None = None, logits_mode: int = 0, allowed_len: torch.Tensor | None = None,
-           allowed_mask: torch.Tensor | None = None, lut_override: torch.Tensor | None = None,
-           out: torch.Tensor | None = None, want_shortlist: bool = False, want_final: bool = False,
-           stats: torch.Tensor | None = None):
-    """Scan summon -> rescore -> verify for H heads x T tokens (see include/sva_b200.h).
-
-    q [H, T, D]; codes [H, L, S] uint8 (rows contiguous); k_low [H, L, R] fp32 (rows
-    contiguous); keys/values [Hkv, L, D].  Returns out [H, T, D] (and the shortlist / final
-    index tensors when requested, [H, T, shortlist] / [H, T, budget] int32, ascending, -1 padded).
-    """
+def decode_args(q: torch.Tensor, q_proj: torch.Tensor, scale: torch.Tensor, codebooks: torch.Tensor,
+                codes: torch.Tensor, k_low: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, shortlist: int,
+                budget: int, softmax_scale: float | None = None, logits_mode: int = 0,
+                allowed_len: torch.Tensor | None = None, allowed_mask: torch.Tensor | None = None,
+                lut_override: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                stats: torch.Tensor | None = None) -> tuple[_lib.DecodeArgs, torch.Tensor]:
+    """Validated sva_decode_args for the tensors of a decode call, and the output tensor."""
     for name, t in (("q", q), ("codes", codes), ("k_low", k_low), ("keys", keys), ("values", values)):
         _cuda(t, name)
     dev = q.device
@@ -166,6 +161,26 @@ def decode(q: torch.Tensor, q_proj: torch.Tensor, scale: torch.Tensor, codebooks
     a.allowed_mask = _ptr(allowed_mask)
     a.mask_row_stride = 0 if allowed_mask is None else allowed_mask.stride(0)
     a.out, a.out_head_stride, a.out_row_stride = out.data_ptr(), out.stride(0), out.stride(1)
+    a.stats = _ptr(stats)
+    return a, out
+
+
+def decode(q: torch.Tensor, q_proj: torch.Tensor, scale: torch.Tensor, codebooks: torch.Tensor, codes: torch.Tensor,
+           k_low: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, shortlist: int, budget: int,
+           softmax_scale: float | None = None, logits_mode: int = 0, allowed_len: torch.Tensor | None = None,
+           allowed_mask: torch.Tensor | None = None, lut_override: torch.Tensor | None = None,
+           out: torch.Tensor | None = None, want_shortlist: bool = False, want_final: bool = False,
+           stats: torch.Tensor | None = None):
+    """Scan summon -> rescore -> verify for H heads x T tokens (see include/sva_b200.h).
+
+    q [H, T, D]; codes [H, L, S] uint8 (rows contiguous); k_low [H, L, R] fp32 (rows
+    contiguous); keys/values [Hkv, L, D].  Returns out [H, T, D] (and the shortlist / final
+    index tensors when requested, [H, T, shortlist] / [H, T, budget] int32, ascending, -1 padded).
+    """
+    a, out = decode_args(q, q_proj, scale, codebooks, codes, k_low, keys, values, shortlist, budget, softmax_scale,
+                         logits_mode, allowed_len, allowed_mask, lut_override, out, stats)
+    dev = q.device
+    n_heads, n_q, _ = q.shape
     sl_out = fin_out = None
     if want_shortlist:
         sl_out = torch.empty(n_heads, n_q, int(shortlist), dtype=torch.int32, device=dev)
@@ -173,7 +188,6 @@ def decode(q: torch.Tensor, q_proj: torch.Tensor, scale: torch.Tensor, codebooks
     if want_final:
         fin_out = torch.empty(n_heads, n_q, int(budget), dtype=torch.int32, device=dev)
         a.final_out = fin_out.data_ptr()
-    a.stats = _ptr(stats)
     lib = _lib.load()
     ws_bytes = int(lib.sva_decode_workspace_size(ctypes.byref(a)))
     ws = _decode_ws.get(dev, ws_bytes)
