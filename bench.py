@@ -12,8 +12,8 @@ query touches ~44 MB; four sets ~176 MB > the 126 MB L2), i.e. every query runs 
 L2.  Inputs are resident in HBM before timing; the catalog is built by the CUDA write path.
 
 Multi-GPU (``torchrun --nproc-per-node N``): the catalog is sharded by key range; every rank
-summons and partially verifies its range and the per-rank candidates are merged exactly after
-one NCCL all-gather (sva_b200.sharded).  ``value`` is the max over ranks.
+summons, rescores and partially verifies its range, and the exact global result comes from three
+NCCL all-gathers between the stages (sva_b200.sharded).  ``value`` is the max over ranks.
 
 ``--impl reference`` times the CPU restatement of the reference path (oracle/cpu_baseline.py,
 the reference itself is PyTorch code that cannot be shipped to the GPU host) on the same
