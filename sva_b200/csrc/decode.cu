@@ -879,7 +879,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
     __syncthreads();
     float* mylg = reinterpret_cast<float*>(rk);
     verify_logits<T>(p.a.keys, p.a.k_head_stride, p.a.k_row_stride, kvh, qf, D, myrows, f1 - f0,
-                     p.a.softmax_scale, p.a.logits_mode, mylg);
+                     p.a.softmax_scale, p.a.logits_mode, mylg, p.a.values, p.a.v_head_stride, p.a.v_row_stride);
     for (int j = f0 + tid; j < f1; j += blockDim.x) lg0[j] = mylg[j - f0];
   }
   cluster.sync();

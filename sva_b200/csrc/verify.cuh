@@ -19,12 +19,16 @@ namespace sva {
 
 constexpr int kVerifyUnroll = 8;
 
+// `values` (optional): the V rows of the same keys are prefetched into L2 while the K rows load,
+// so that the weighted sum that follows reads them from L2.
 template <typename T>
 __device__ void verify_logits(const void* keys, int64_t k_head_stride, int64_t k_row_stride, int kvh, const float* qf,
-                              int D, const int32_t* rows, int n, float softmax_scale, int logits_mode, float* lg) {
+                              int D, const int32_t* rows, int n, float softmax_scale, int logits_mode, float* lg,
+                              const void* values = nullptr, int64_t v_head_stride = 0, int64_t v_row_stride = 0) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   const int half = lane >> 4, l16 = lane & 15;
   const T* kb = reinterpret_cast<const T*>(keys) + kvh * k_head_stride;
+  const T* vb = values ? reinterpret_cast<const T*>(values) + kvh * v_head_stride : nullptr;
   constexpr int U = kVerifyUnroll;
   for (int base = warp * 2 * U; base < n; base += nwarps * 2 * U) {
     float part[U];
@@ -37,6 +41,15 @@ __device__ void verify_logits(const void* keys, int64_t k_head_stride, int64_t k
       for (int u = 0; u < U; ++u) {
         const int j = base + 2 * u + half;
         k4[u] = (j < n && e < D) ? load4<T>(kb + (int64_t)rows[j] * k_row_stride, e, D) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      if (vb) {
+        // one prefetch per 128-byte line of each row's chunk: lanes l16 = 0, 8 of every half-warp
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int j = base + 2 * u + half;
+          if (j < n && e < D && ((e * static_cast<int>(sizeof(T))) & 127) == 0)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(vb + (int64_t)rows[j] * v_row_stride + e));
+        }
       }
       const float4 qv = (e < D) ? make_float4(qf[e], (e + 1 < D) ? qf[e + 1] : 0.f, (e + 2 < D) ? qf[e + 2] : 0.f,
                                               (e + 3 < D) ? qf[e + 3] : 0.f)
