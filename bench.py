@@ -288,16 +288,47 @@ def build_sets(args, device, rank: int, world: int):
         q_proj, k_proj, cb = q_proj.to(device), k_proj.to(device), cb.to(device)
         k_low = torch.empty(heads, hi - lo, r, dtype=torch.float32, device=device)
         codes = torch.empty(heads, hi - lo, s, dtype=torch.uint8, device=device)
+        tc = kernels.tensor_core_write_ok(kk, k_proj)
+        status = torch.zeros(1, dtype=torch.int32, device=device)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        kernels.catalog_encode(kk, k_proj, cb, 0, hi - lo, k_low, codes)
+        kernels.catalog_encode(kk, k_proj, cb, 0, hi - lo, k_low, codes, tensor_cores=tc, status=status)
         e1.record()
         torch.cuda.synchronize()
+        if int(status.item()) != 0:
+            raise RuntimeError("tensor-core write path timed out")
         build_ms += e0.elapsed_time(e1)
+        if si == 0:
+            # the exact CUDA-core write path, timed once for comparison (into scratch buffers)
+            k2, c2 = torch.empty_like(k_low), torch.empty_like(codes)
+            e0.record()
+            kernels.catalog_encode(kk, k_proj, cb, 0, hi - lo, k2, c2, tensor_cores=False)
+            e1.record()
+            torch.cuda.synchronize()
+            exact_ms = e0.elapsed_time(e1)
+            del k2, c2
         scale = torch.ones(heads, dtype=torch.float32, device=device)
         sets.append(dict(q=q, q_proj=q_proj, scale=scale, cb=cb, codes=codes, k_low=k_low, keys=kk, values=vv,
                          out=torch.empty(heads, 1, d, dtype=torch.bfloat16, device=device), offset=lo))
-    return sets, build_ms, (hi - lo)
+    write = {"tensor_cores": bool(tc), "ms_per_set": build_ms / args.sets, "exact_ms_per_set": exact_ms}
+    return sets, write, (hi - lo)
+
+
+def write_path_summary(args, write: dict, local_keys: int, peak: float) -> dict:
+    """The catalog write of one set (all heads): keys/s, projection TFLOP/s and the fraction of
+    the measured HBM peak its algorithmic bytes reach (K read as bf16, k_low fp32 written, codes)."""
+    s, _ = pq_shape(args.pq)
+    keys = args.heads * local_keys
+    flops = 2.0 * keys * 64 * 64
+    nbytes = keys * (64 * 2 + 64 * 4 + s)
+    out = {"path": "tcgen05 projection + CUDA-core assignment" if write["tensor_cores"] else "exact CUDA-core"}
+    for name, ms in (("", write["ms_per_set"]), ("exact_", write["exact_ms_per_set"])):
+        out[name + "ms_per_set"] = round(ms, 3)
+        out[name + "keys_per_s"] = round(keys / (ms * 1e-3), 1)
+        out[name + "projection_tflops"] = round(flops / (ms * 1e-3) / 1e12, 3)
+        out[name + "hbm_frac"] = round(nbytes / (ms * 1e-3) / 1e9 / peak, 4)
+    out["algorithmic_bytes_per_set"] = int(nbytes)
+    return out
 
 
 def gpu_arm(args):
@@ -321,7 +352,7 @@ def gpu_arm(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
         group = dist.group.WORLD
     lib = _lib.load()
-    sets, build_ms, local_keys = build_sets(args, device, rank, world)
+    sets, write, local_keys = build_sets(args, device, rank, world)
 
     if world == 1:
         def one_query(st):
@@ -454,8 +485,7 @@ def gpu_arm(args):
         "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16 K/V, 64 planted keys/head, catalog built on GPU)",
         "config": workload_config(args, world),
         "gpu_launches": None, "roofline": roofline, "step_roofline": step_roofline, "clocks": clocks, "e2e": e2e,
-        "write_path": {"keys_per_s": round(args.sets * args.heads * local_keys / (build_ms * 1e-3), 1),
-                       "ms_per_set": round(build_ms / args.sets, 3)},
+        "write_path": write_path_summary(args, write, local_keys, peak),
         "wall_s_timed": round(wall, 3),
     }
     launches_per_query = 3 if grid_schedule else 1

@@ -83,6 +83,19 @@ int sva_catalog_encode(const void* keys, int32_t key_dtype, int64_t key_head_str
                        int64_t start, int64_t count, float* k_low, int64_t k_low_head_stride, uint8_t* codes,
                        int64_t codes_head_stride, void* stream);
 
+/* The same on the tensor cores: k_low = K . Kproj by tcgen05 MMA (bf16 operands, fp32
+ * accumulator in tensor memory), then the same nearest-codeword assignment on the fp32 rows.
+ * K must be bf16 with 16-byte aligned rows; Kproj is rounded to bf16, which is exact for bf16
+ * artifacts; head_dim a multiple of 16 up to 128, rank_dim a multiple of 16 up to 64.  k_low
+ * differs from sva_catalog_encode's only in the fp32 summation order (a few ulp), so codes can
+ * differ only where two codewords are that close.  *status (device int, may be NULL) is set to
+ * SVA_ERR_TIMEOUT if a tile's tensor-core wait ran out.  Replaces sva/llama.py:578-624. */
+int sva_catalog_encode_tc(const void* keys, int32_t key_dtype, int64_t key_head_stride, int64_t key_row_stride,
+                          int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t rank_dim,
+                          const float* k_proj, const float* codebooks, int32_t subspaces, int32_t codewords,
+                          int64_t start, int64_t count, float* k_low, int64_t k_low_head_stride, uint8_t* codes,
+                          int64_t codes_head_stride, int32_t* status, void* stream);
+
 /* Nearest centroid of each row of x [n][dim] (row stride x_row_stride) among centroids
  * [C][dim]; labels as int64.  Replaces sva/ops.py:10-21. */
 int sva_assign_centroids(const float* x, int64_t n, int32_t dim, int64_t x_row_stride, const float* centroids,

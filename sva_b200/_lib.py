@@ -42,6 +42,7 @@ EXPORTED = (
     "sva_profile_events",
     "sva_debug_timestamps",
     "sva_catalog_encode",
+    "sva_catalog_encode_tc",
     "sva_assign_centroids",
     "sva_pq_scores",
     "sva_decode_workspace_size",
@@ -186,6 +187,8 @@ def load() -> ctypes.CDLL:
             "sva_debug_timestamps": ([c_vp], ctypes.c_int),
             "sva_catalog_encode": ([c_vp, c_i32, c_i64, c_i64, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_i32, c_i32,
                                     c_i64, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp], ctypes.c_int),
+            "sva_catalog_encode_tc": ([c_vp, c_i32, c_i64, c_i64, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_i32,
+                                       c_i32, c_i64, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_vp], ctypes.c_int),
             "sva_assign_centroids": ([c_vp, c_i64, c_i32, c_i64, c_vp, c_i32, c_vp, c_vp], ctypes.c_int),
             "sva_pq_scores": ([c_vp, c_i32, c_i32, c_i32, c_vp, c_i32, c_i32, c_vp, c_i64, c_vp, c_vp], ctypes.c_int),
             "sva_decode_workspace_size": ([ctypes.POINTER(DecodeArgs)], c_sz),

@@ -1,6 +1,7 @@
 // Library-wide C ABI helpers: version, thread-local last error, kernel attribute cache.
 #include <mutex>
 #include <string>
+#include <unordered_map>
 #include <unordered_set>
 
 #include "sva_internal.h"
@@ -15,8 +16,9 @@ int set_error(int code, const char* msg) {
 }
 
 int ensure_smem_attr(const void* kernel, int bytes) {
+  // (kernel, device) -> the limit set so far; a call asking for more raises it again
   static std::mutex mu;
-  static std::unordered_set<unsigned long long> done;
+  static std::unordered_map<unsigned long long, int> done;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) {
@@ -26,23 +28,27 @@ int ensure_smem_attr(const void* kernel, int bytes) {
   const unsigned long long key = (reinterpret_cast<unsigned long long>(kernel) << 6) ^ static_cast<unsigned long long>(dev);
   {
     std::lock_guard<std::mutex> lock(mu);
-    if (done.count(key)) return SVA_OK;
+    auto it = done.find(key);
+    if (it != done.end() && it->second >= bytes) return SVA_OK;
   }
   // The dynamic limit may not exceed the opt-in maximum minus the kernel's static shared memory.
   cudaFuncAttributes fa;
   int optin = 0;
+  int set = bytes;
   e = cudaFuncGetAttributes(&fa, kernel);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   if (e == cudaSuccess) {
     const int room = optin - static_cast<int>(fa.sharedSizeBytes);
-    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes < room ? bytes : room);
+    set = bytes < room ? bytes : room;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, set);
   }
   if (e != cudaSuccess) {
     cudaGetLastError();  // do not leave the error for the next runtime call
     return set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
   }
   std::lock_guard<std::mutex> lock(mu);
-  done.insert(key);
+  int& v = done[key];
+  if (set > v) v = set;
   return SVA_OK;
 }
 

@@ -58,12 +58,28 @@ class Workspace:
 _decode_ws = Workspace()
 
 
+def tensor_core_write_ok(keys: torch.Tensor, k_proj: torch.Tensor) -> bool:
+    """Whether the tcgen05 write path applies: bf16 keys with 16-byte aligned rows, head_dim a
+    multiple of 16 up to 128, rank a multiple of 16 up to 64, and a key projection whose values
+    are bf16 numbers (so rounding it to bf16 changes nothing)."""
+    head_dim, rank = int(keys.shape[-1]), int(k_proj.shape[-1])
+    if keys.dtype != torch.bfloat16 or head_dim % 16 or head_dim > 128 or rank % 16 or rank > 64:
+        return False
+    if keys.data_ptr() % 16 or (keys.stride(-2) * 2) % 16 or (keys.stride(0) * 2) % 16:
+        return False
+    return bool(torch.equal(k_proj, k_proj.to(torch.bfloat16).to(k_proj.dtype)))
+
+
 def catalog_encode(keys: torch.Tensor, k_proj: torch.Tensor, codebooks: torch.Tensor, start: int, count: int,
-                   k_low: torch.Tensor | None, codes: torch.Tensor | None, n_heads: int | None = None) -> None:
+                   k_low: torch.Tensor | None, codes: torch.Tensor | None, n_heads: int | None = None,
+                   tensor_cores: bool = False, status: torch.Tensor | None = None) -> None:
     """Write k_low / codes rows [start, start+count) of every query head.
 
     keys [Hkv, L, D] (rows contiguous), k_proj [H, D, R] fp32, codebooks [H, S, C, R/S] fp32,
-    k_low [H, cap, R] fp32 (contiguous rows), codes [H, cap, S] uint8.
+    k_low [H, cap, R] fp32 (contiguous rows), codes [H, cap, S] uint8.  ``tensor_cores`` selects
+    the tcgen05 projection (sva_catalog_encode_tc; see ``tensor_core_write_ok``) instead of the
+    exact sequential-order CUDA-core projection; ``status`` (int32 device scalar) receives its
+    timeout flag.
     """
     _cuda(keys, "keys")
     if keys.stride(-1) != 1:
@@ -80,11 +96,13 @@ def catalog_encode(keys: torch.Tensor, k_proj: torch.Tensor, codebooks: torch.Te
             if not (t.stride(-1) == 1 and t.stride(-2) == t.shape[-1]):
                 raise ValueError(f"{name} rows must be contiguous")
     lib = _lib.load()
-    rc = lib.sva_catalog_encode(
-        keys.data_ptr(), dtype_code(keys.dtype), keys.stride(0), keys.stride(1), n_heads, n_kv, head_dim, rank,
-        k_proj.data_ptr(), codebooks.data_ptr(), subspaces, codewords, int(start), int(count), _ptr(k_low),
-        0 if k_low is None else k_low.stride(0), _ptr(codes), 0 if codes is None else codes.stride(0),
-        _stream(keys.device))
+    common = (keys.data_ptr(), dtype_code(keys.dtype), keys.stride(0), keys.stride(1), n_heads, n_kv, head_dim, rank,
+              k_proj.data_ptr(), codebooks.data_ptr(), subspaces, codewords, int(start), int(count), _ptr(k_low),
+              0 if k_low is None else k_low.stride(0), _ptr(codes), 0 if codes is None else codes.stride(0))
+    if tensor_cores:
+        rc = lib.sva_catalog_encode_tc(*common, _ptr(status), _stream(keys.device))
+    else:
+        rc = lib.sva_catalog_encode(*common, _stream(keys.device))
     _lib.check(rc)
 
 

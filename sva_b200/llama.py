@@ -49,6 +49,10 @@ class SVALlamaServingConfig:
     adaptive_high_margin: float = 0.70
     profile_components: bool = False
     static_tail_rebuild_interval: int = 64
+    # Not in the reference: "auto" projects keys on the tensor cores (tcgen05) when the keys are
+    # bf16 and the key projection holds bf16 values, else exactly on CUDA cores; "exact" always
+    # uses the CUDA-core projection in the canonical fp32 order.
+    write_path: str = "auto"
 
 
 class SVALlamaAttention(nn.Module):
@@ -91,6 +95,8 @@ class SVALlamaAttention(nn.Module):
         self._cached_postings_key_len = 0
         self._cached_key_len = 0
         self._cached_signature: tuple | None = None
+        self._tc_write_key: tuple | None = None
+        self._tc_write = False
 
     @property
     def _cached_k_low(self) -> torch.Tensor | None:
@@ -242,6 +248,18 @@ class SVALlamaAttention(nn.Module):
         self._postings = kernels.postings_build(self._codes_buf, int(self.sva_coarse_codebooks.shape[2]), key_len=key_len)
         self._cached_postings_key_len = key_len
 
+    def _tensor_core_write(self, keys: torch.Tensor) -> bool:
+        """Whether new keys go through the tcgen05 projection (serving option ``write_path``)."""
+        if self.serving.write_path == "exact":
+            return False
+        if self.serving.write_path != "auto":
+            raise ValueError(f"Unknown write_path {self.serving.write_path!r}; expected 'auto' or 'exact'.")
+        key = (keys.device, keys.dtype, keys.data_ptr() % 16, keys.stride(-2), keys.stride(0))
+        if self._tc_write_key != key:
+            self._tc_write_key = key
+            self._tc_write = kernels.tensor_core_write_ok(keys, self.sva_k_proj.to(keys.device))
+        return self._tc_write
+
     def _key_catalog(self, keys: torch.Tensor, q_len: int) -> None:
         """Keep the device catalog in step with the cache (reference sva/llama.py:578-624).
 
@@ -258,7 +276,7 @@ class SVALlamaAttention(nn.Module):
         start = self._cached_key_len if can_append else 0
         self._ensure_capacity(n_heads, k_len, keys.device)
         kernels.catalog_encode(keys, self.sva_k_proj, self.sva_coarse_codebooks, start, k_len - start, self._k_low_buf,
-                               self._codes_buf, n_heads=n_heads)
+                               self._codes_buf, n_heads=n_heads, tensor_cores=self._tensor_core_write(keys))
         if can_append:
             if mode == "inverted":
                 self._codes_len = k_len
@@ -350,7 +368,7 @@ class SVALlamaPatcher:
                  adaptive_min_budget: int | None = None, adaptive_mid_budget: int | None = None,
                  adaptive_low_margin: float = 0.35, adaptive_high_margin: float = 0.70,
                  profile_components: bool = False, static_tail_rebuild_interval: int = 64,
-                 layers: list[int] | None = None) -> None:
+                 layers: list[int] | None = None, write_path: str = "auto") -> None:
         self.model = model
         self.bundle = bundle
         self.stats = SVAStats()
@@ -370,6 +388,7 @@ class SVALlamaPatcher:
             adaptive_high_margin=adaptive_high_margin,
             profile_components=profile_components,
             static_tail_rebuild_interval=static_tail_rebuild_interval,
+            write_path=write_path,
         )
 
     def patch(self) -> "SVALlamaPatcher":
@@ -446,8 +465,14 @@ def patch_llama_attention(model: nn.Module, artifact_dir_or_bundle: str | Path |
                           inverted_cells_per_subspace: int = 8, adaptive_min_budget: int | None = None,
                           adaptive_mid_budget: int | None = None, adaptive_low_margin: float = 0.35,
                           adaptive_high_margin: float = 0.70, profile_components: bool = False,
-                          static_tail_rebuild_interval: int = 64, layers: list[int] | None = None) -> SVALlamaPatcher:
-    """Patch a Llama-family model with SVA attention and return a reversible handle (reference sva/llama.py:808-848)."""
+                          static_tail_rebuild_interval: int = 64, layers: list[int] | None = None,
+                          write_path: str = "auto") -> SVALlamaPatcher:
+    """Patch a Llama-family model with SVA attention and return a reversible handle (reference sva/llama.py:808-848).
+
+    ``write_path`` (not in the reference) selects the key projection: "auto" (tcgen05 tensor cores
+    when the keys are bf16 and the projection holds bf16 values) or "exact" (CUDA cores, canonical
+    fp32 order).
+    """
     bundle = (artifact_dir_or_bundle if isinstance(artifact_dir_or_bundle, SVAArtifactBundle)
               else load_sva_artifact_bundle(artifact_dir_or_bundle))
     return SVALlamaPatcher(
@@ -456,5 +481,5 @@ def patch_llama_attention(model: nn.Module, artifact_dir_or_bundle: str | Path |
         inverted_cells_per_subspace=inverted_cells_per_subspace, adaptive_min_budget=adaptive_min_budget,
         adaptive_mid_budget=adaptive_mid_budget, adaptive_low_margin=adaptive_low_margin,
         adaptive_high_margin=adaptive_high_margin, profile_components=profile_components,
-        static_tail_rebuild_interval=static_tail_rebuild_interval, layers=layers,
+        static_tail_rebuild_interval=static_tail_rebuild_interval, layers=layers, write_path=write_path,
     ).patch()
