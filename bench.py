@@ -58,6 +58,8 @@ def parse_args():
     ap.add_argument("--e2e-queries", type=int, default=64)
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--throughput-heads", type=int, default=64,
+                    help="heads per launch of the throughput-mode measurement (0: skip)")
     ap.add_argument("--seed", type=int, default=0)
     return ap.parse_args()
 
@@ -314,6 +316,56 @@ def build_sets(args, device, rank: int, world: int):
     return sets, write, (hi - lo)
 
 
+def throughput_measure(args, device, peak: float) -> dict:
+    """Throughput mode (one GPU): many independent (head, query) problems per launch, here
+    ``--throughput-heads`` heads of 2^20 keys decoded by one call, so that the per-problem latency
+    chains overlap and the scan streams at bandwidth.  One catalog of that many heads (its codes
+    alone exceed L2); a CUDA graph of 8 calls; device-timed over 5 replays after 3 warm-ups."""
+    import copy
+
+    import torch
+
+    from sva_b200 import kernels
+
+    targs = copy.copy(args)
+    targs.heads, targs.sets = args.throughput_heads, 1
+    sets, _, _ = build_sets(targs, device, 0, 1)
+    st = sets[0]
+
+    def call():
+        kernels.decode(st["q"], st["q_proj"], st["scale"], st["cb"], st["codes"], st["k_low"], st["keys"],
+                       st["values"], args.shortlist, args.budget, softmax_scale=0.125, logits_mode=1, out=st["out"])
+
+    call()
+    torch.cuda.synchronize()
+    calls = 8
+    graph = torch.cuda.CUDAGraph()
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(graph, stream=stream):
+            for _ in range(calls):
+                call()
+    torch.cuda.synchronize()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 5
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = 1000.0 * e0.elapsed_time(e1) / (reps * calls)
+    nbytes = algorithmic_bytes(targs)["total"]
+    gbs = nbytes / (us * 1e-6) / 1e9
+    del graph, sets, st
+    torch.cuda.empty_cache()
+    return {"heads_per_launch": targs.heads, "us_per_launch": round(us, 2), "us_per_head": round(us / targs.heads, 3),
+            "algorithmic_bytes_per_launch": int(nbytes), "achieved_gbs": round(gbs, 1), "peak_gbs": peak,
+            "frac": round(gbs / peak, 4), "keys": args.keys, "pq": args.pq}
+
+
 def write_path_summary(args, write: dict, local_keys: int, peak: float) -> dict:
     """The catalog write of one set (all heads): keys/s, projection TFLOP/s and the fraction of
     the measured HBM peak its algorithmic bytes reach (K read as bf16, k_low fp32 written, codes)."""
@@ -492,6 +544,8 @@ def gpu_arm(args):
     if world > 1:
         launches_per_query = 3 + shard.extra_launches
     line["gpu_launches"] = launches_per_query * qps * args.steps
+    if world == 1 and args.throughput_heads > 0:
+        line["throughput"] = throughput_measure(args, device, peak)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         times, threads = run_cpu_decoder(args, 1000, 1, args.cpu_seconds)
         cpu_us = 1e6 * sum(times) / len(times)

@@ -580,13 +580,56 @@ __global__ void __launch_bounds__(kThreads) decode_prep_kernel(const DecodeParam
 
 // LUT lookup of key j in the bank-replicated table: entry e lives at lut[e * 32 + lane], so
 // the 32 lanes of a warp read 32 different banks whatever their codes are.  C is a power of
-// two; codes are masked to it (a valid catalog never holds a code >= C).
+// two; codes are masked to it (a valid catalog never holds a code >= C).  The byte offset of a
+// lookup, code * 128 + lane * 4, is built from the code's byte in its 32-bit word with one
+// shift and one and-or (the lane bits 2..6 and the code bits 7.. do not overlap); the
+// subspace's table base is a constant offset.
+template <int S>
+__device__ __forceinline__ void code_pos(const Codes4<S>& c, int j, int s, uint32_t& word, int& byte) {
+  if (S == 1) {
+    word = c.a.x;
+    byte = j;
+  } else if (S == 2) {
+    word = (j < 2) ? c.a.x : c.a.y;
+    byte = 2 * (j & 1) + s;
+  } else if (S == 4) {
+    word = (j == 0) ? c.a.x : (j == 1) ? c.a.y : (j == 2) ? c.a.z : c.a.w;
+    byte = s;
+  } else {
+    const uint4& v = (j < 2) ? c.a : c.b;
+    word = ((j & 1) == 0) ? (s < 4 ? v.x : v.y) : (s < 4 ? v.z : v.w);
+    byte = s & 3;
+  }
+}
+
+// ld.shared.f32 at a 32-bit shared address plus a compile-time offset.
+template <int OFF>
+__device__ __forceinline__ float lds_f32(uint32_t addr) {
+  float v;
+  asm("ld.shared.f32 %0, [%1+%2];" : "=f"(v) : "r"(addr), "n"(OFF));
+  return v;
+}
+
+template <int S, int C, int s>
+__device__ __forceinline__ float adc_rep_from(const Codes4<S>& c, int j, uint32_t lane_base, float sum) {
+  if constexpr (s == S) {
+    return sum;
+  } else {
+    constexpr uint32_t kMask = static_cast<uint32_t>(C - 1) << 7;
+    uint32_t w;
+    int byte;
+    code_pos<S>(c, j, s, w, byte);
+    const int sh = 8 * byte - 7;  // compile-time after unrolling
+    const uint32_t off = ((sh >= 0 ? (w >> sh) : (w << -sh)) & kMask) + lane_base;
+    const float v = lds_f32<s * C * 128>(off);
+    return adc_rep_from<S, C, s + 1>(c, j, lane_base, s == 0 ? v : __fadd_rn(sum, v));
+  }
+}
+
+// lane_base = shared address of the replicated table + 4 * lane.
 template <int S, int C>
-__device__ __forceinline__ float adc_rep(const Codes4<S>& c, int j, const float* lut_lane) {
-  float sum = lut_lane[(code_at<S>(c, j, 0) & (C - 1)) * 32];
-#pragma unroll
-  for (int s = 1; s < S; ++s) sum = __fadd_rn(sum, lut_lane[(s * C + (code_at<S>(c, j, s) & (C - 1))) * 32]);
-  return sum;
+__device__ __forceinline__ float adc_rep(const Codes4<S>& c, int j, uint32_t lane_base) {
+  return adc_rep_from<S, C, 0>(c, j, lane_base, 0.f);
 }
 
 // scan: the single pass over the codes; keys >= T0 become candidates.  One CTA scans
@@ -647,10 +690,10 @@ __global__ void __launch_bounds__(kScanThreads, 4) decode_scan_kernel(const Deco
       const float scale = p.inv_sqrt_r;
       const int ngroups = static_cast<int>((i1 - i0) >> 2);
       const uint8_t* cbase = codes + i0 * S;
-      const float* lut_lane = lut + lane;
+      const uint32_t lane_base = static_cast<uint32_t>(__cvta_generic_to_shared(lut)) + static_cast<uint32_t>(lane) * 4u;
       auto score = [&](const Codes4<S>& c, int j) -> float {
         float sum;
-        if constexpr (kRep) sum = adc_rep<S, C>(c, j, lut_lane);
+        if constexpr (kRep) sum = adc_rep<S, C>(c, j, lane_base);
         else sum = adc_plain<S, C>(c, j, lut, p.a.codewords);
         if constexpr (POW2) return __fmul_rn(sum, scale);
         else return __fdiv_rn(sum, p.sqrt_r);
@@ -663,10 +706,14 @@ __global__ void __launch_bounds__(kScanThreads, 4) decode_scan_kernel(const Deco
         for (int u = 0; u < kInFlight; ++u) c[u] = load_codes4<S>(cbase, 4 * (gb + u * kScanThreads));
 #pragma unroll
         for (int u = 0; u < kInFlight; ++u) {
+          float sc[4];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float sc = score(c[u], j);
-            if (sc >= t0f) take(ordered_key(sc), i0 + 4 * (gb + u * kScanThreads) + j);
+          for (int j = 0; j < 4; ++j) sc[j] = score(c[u], j);
+          // one compare per group of four keys; candidates are rare
+          if (fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3])) >= t0f) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              if (sc[j] >= t0f) take(ordered_key(sc[j]), i0 + 4 * (gb + u * kScanThreads) + j);
           }
         }
       }
