@@ -20,8 +20,8 @@
 
 namespace sva {
 
-constexpr int kSelectBins = 2048;
-constexpr int kSelectDigit = 11;
+constexpr int kSelectBins = 1024;
+constexpr int kSelectDigit = 10;
 
 struct SelectThreshold {
   unsigned long long prefix;
@@ -36,23 +36,34 @@ __device__ __forceinline__ bool is_selected(const SelectThreshold& t, unsigned l
   return c != 0ull && (c & t.mask) >= t.prefix;
 }
 
-// Shared scratch for cta_radix_select: the bin counts plus a few broadcast slots.
+// Shared scratch for cta_radix_select: two bin-count buffers (a level counts into one while the
+// other is cleared for the next level) and per-buffer broadcast slots.
 struct SelectScratch {
-  uint32_t hist[kSelectBins];
+  uint32_t hist[2][kSelectBins];
   unsigned long long lo_part[32];
   unsigned long long hi_part[32];
-  int warp_tot[32];
-  unsigned long long base;
-  unsigned long long top;
-  int digit;
-  int above;
-  int count;
+  int warp_tot[2][32];
+  int digit[2];
+  int above[2];
+  int count[2];
 };
+
+// `ts` (measurement only, may be NULL): thread 0 writes the global timer after the range pass
+// and after each level into ts[0], ts[1], ... (at most ts_slots).
+__device__ __forceinline__ void select_stamp(unsigned long long* ts, int slot) {
+  if (ts && threadIdx.x == 0) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    ts[slot] = t;
+  }
+}
 
 // Requires blockDim.x in {256, 512, 1024}.  `k` should not exceed the number of non-zero items
 // (if it does, every non-zero item is selected).  All threads of the block must call it.
+// Barriers: one for the range, three per level.
 template <class ItemFn>
-__device__ SelectThreshold cta_radix_select(const ItemFn& item, int n, int k, SelectScratch* sc) {
+__device__ SelectThreshold cta_radix_select(const ItemFn& item, int n, int k, SelectScratch* sc,
+                                            unsigned long long* ts = nullptr, int ts_slots = 0) {
   SelectThreshold thr;
   thr.mask = ~0ull;
   if (k <= 0) {
@@ -61,12 +72,22 @@ __device__ SelectThreshold cta_radix_select(const ItemFn& item, int n, int k, Se
     return thr;
   }
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  // Item loops load kBatch items before using any of them, so their latencies overlap.
+  constexpr int kBatch = 4;
   unsigned long long mn = ~0ull, mx = 0ull;
-  for (int i = tid; i < n; i += blockDim.x) {
-    const unsigned long long c = item(i);
-    if (c != 0ull) {
-      mn = c < mn ? c : mn;
-      mx = c > mx ? c : mx;
+  for (int i0 = tid; i0 < n; i0 += kBatch * blockDim.x) {
+    unsigned long long c[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int i = i0 + u * blockDim.x;
+      c[u] = i < n ? item(i) : 0ull;
+    }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      if (c[u] != 0ull) {
+        mn = c[u] < mn ? c[u] : mn;
+        mx = c[u] > mx ? c[u] : mx;
+      }
     }
   }
 #pragma unroll
@@ -80,70 +101,83 @@ __device__ SelectThreshold cta_radix_select(const ItemFn& item, int n, int k, Se
     sc->lo_part[warp] = mn;
     sc->hi_part[warp] = mx;
   }
+  for (int b = tid; b < kSelectBins; b += blockDim.x) sc->hist[0][b] = 0u;
   __syncthreads();
-  if (tid == 0) {
-    unsigned long long a = ~0ull, b = 0ull;
-    for (int w = 0; w < nwarps; ++w) {
-      a = sc->lo_part[w] < a ? sc->lo_part[w] : a;
-      b = sc->hi_part[w] > b ? sc->hi_part[w] : b;
-    }
-    sc->base = a;
-    sc->top = b;
+  // every warp reduces the per-warp partials, one per lane
+  unsigned long long base = lane < nwarps ? sc->lo_part[lane] : ~0ull;
+  unsigned long long top = lane < nwarps ? sc->hi_part[lane] : 0ull;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long a = __shfl_xor_sync(0xFFFFFFFFu, base, o);
+    const unsigned long long b = __shfl_xor_sync(0xFFFFFFFFu, top, o);
+    base = a < base ? a : base;
+    top = b > top ? b : top;
   }
-  __syncthreads();
-  unsigned long long base = sc->base;
-  const unsigned long long top = sc->top;
-  __syncthreads();
+  if (ts_slots > 0) select_stamp(ts, 0);
   if (top == 0ull || top == base) {  // no items, or all non-zero items equal
     thr.prefix = base;
     return thr;
   }
   int hi = 63 - __clzll(static_cast<long long>(top - base));
   int remaining = k;
+  int buf = 0;
+  int lvl = 1;
   const int per = kSelectBins / blockDim.x;  // bins per thread in the scan
   for (;;) {
     const int lo = hi >= kSelectDigit - 1 ? hi - (kSelectDigit - 1) : 0;
-    for (int b = tid; b < kSelectBins; b += blockDim.x) sc->hist[b] = 0u;
-    if (tid == 0) sc->count = -1;
-    __syncthreads();
-    for (int i = tid; i < n; i += blockDim.x) {
-      const unsigned long long c = item(i);
-      if (c == 0ull || c < base) continue;
-      const unsigned long long d = c - base;
-      if (hi < 63 && (d >> (hi + 1)) != 0ull) continue;  // above the window [base, base + 2^(hi+1))
-      atomicAdd(&sc->hist[d >> lo], 1u);
+    for (int i0 = tid; i0 < n; i0 += kBatch * blockDim.x) {
+      unsigned long long c[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int i = i0 + u * blockDim.x;
+        c[u] = i < n ? item(i) : 0ull;
+      }
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const unsigned long long d = c[u] - base;
+        // in the window [base, base + 2^(hi+1))
+        if (c[u] != 0ull && c[u] >= base && (hi == 63 || (d >> (hi + 1)) == 0ull))
+          atomicAdd(&sc->hist[buf][d >> lo], 1u);
+      }
     }
+    for (int b = tid; b < kSelectBins; b += blockDim.x) sc->hist[buf ^ 1][b] = 0u;  // next level's buffer
     __syncthreads();
-    // Descending scan: thread t owns bins kSelectBins-1-per*t ... kSelectBins-per*(t+1).
+    // descending scan: thread t owns bins kSelectBins-1-per*t ... kSelectBins-per*(t+1)
     int cnt = 0;
-    for (int q = 0; q < per; ++q) cnt += static_cast<int>(sc->hist[kSelectBins - 1 - (per * tid + q)]);
-    int incl = warp_incl_scan(cnt);
-    if (lane == 31) sc->warp_tot[warp] = incl;
+    for (int q = 0; q < per; ++q) cnt += static_cast<int>(sc->hist[buf][kSelectBins - 1 - (per * tid + q)]);
+    const int incl_w = warp_incl_scan(cnt);
+    if (lane == 31) sc->warp_tot[buf][warp] = incl_w;
     __syncthreads();
-    for (int w = 0; w < warp; ++w) incl += sc->warp_tot[w];
+    // prefix of the warp totals, in every warp by shuffles
+    const int wt = lane < nwarps ? sc->warp_tot[buf][lane] : 0;
+    const int wincl = warp_incl_scan(wt);
+    const int total = __shfl_sync(0xFFFFFFFFu, wincl, 31);
+    const int wexcl = __shfl_sync(0xFFFFFFFFu, wincl - wt, warp);
+    const int incl = incl_w + wexcl;
     const int excl = incl - cnt;
     if (excl < remaining && incl >= remaining) {
       int run = excl;
       for (int q = 0; q < per; ++q) {
         const int b = kSelectBins - 1 - (per * tid + q);
-        const int v = static_cast<int>(sc->hist[b]);
+        const int v = static_cast<int>(sc->hist[buf][b]);
         if (run + v >= remaining) {
-          sc->digit = b;
-          sc->above = run;
-          sc->count = v;
+          sc->digit[buf] = b;
+          sc->above[buf] = run;
+          sc->count[buf] = v;
           break;
         }
         run += v;
       }
     }
     __syncthreads();
-    const int count = sc->count;
-    if (count < 0) break;  // fewer items than k: keep the window's base, select all
-    base += static_cast<unsigned long long>(sc->digit) << lo;
-    remaining -= sc->above;
-    __syncthreads();
+    if (total < remaining) break;  // fewer items than k: keep the window's base, select all
+    const int count = sc->count[buf];
+    base += static_cast<unsigned long long>(sc->digit[buf]) << lo;
+    remaining -= sc->above[buf];
+    if (lvl < ts_slots) select_stamp(ts, lvl++);
     if (count == remaining || lo == 0) break;
     hi = lo - 1;
+    buf ^= 1;
   }
   thr.prefix = base;
   return thr;
@@ -155,39 +189,45 @@ __device__ SelectThreshold cta_radix_select(const ItemFn& item, int n, int k, Se
 template <class ItemFn, class EmitFn>
 __device__ int cta_compact(const ItemFn& item, int n, const SelectThreshold& thr, const EmitFn& emit, int* scratch) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  constexpr int kBatch = 4;  // 32-item steps whose loads are issued together
   int per = (n + nwarps - 1) / nwarps;
   per = (per + 31) & ~31;
   const int lo = warp * per;
   const int hi = min(n, lo + per);
   int cnt = 0;
-  for (int base = lo; base < hi; base += 32) {
-    const int i = base + lane;
-    const bool sel = (i < hi) && is_selected(thr, item(i));
-    cnt += __popc(__ballot_sync(0xFFFFFFFFu, sel));
+  for (int base = lo; base < hi; base += kBatch * 32) {
+    bool sel[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int i = base + u * 32 + lane;
+      sel[u] = (i < hi) && is_selected(thr, item(i));
+    }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) cnt += __popc(__ballot_sync(0xFFFFFFFFu, sel[u]));
   }
   if (lane == 0) scratch[warp] = cnt;
   __syncthreads();
-  if (warp == 0) {
-    int v = (lane < nwarps) ? scratch[lane] : 0;
-    int incl = warp_incl_scan(v);
-    if (lane < nwarps) scratch[lane] = incl - v;
-    if (lane == nwarps - 1) scratch[nwarps] = incl;
-  }
-  __syncthreads();
-  int off = scratch[warp];
-  const int total = scratch[nwarps];
+  // every warp: exclusive prefix of the warp counts, by shuffles
+  const int v = lane < nwarps ? scratch[lane] : 0;
+  const int incl = warp_incl_scan(v);
+  const int total = __shfl_sync(0xFFFFFFFFu, incl, 31);
+  int off = __shfl_sync(0xFFFFFFFFu, incl - v, warp);
   const unsigned lt = (1u << lane) - 1u;
-  for (int base = lo; base < hi; base += 32) {
-    const int i = base + lane;
-    unsigned long long c = 0ull;
-    bool sel = false;
-    if (i < hi) {
-      c = item(i);
-      sel = is_selected(thr, c);
+  for (int base = lo; base < hi; base += kBatch * 32) {
+    unsigned long long c[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int i = base + u * 32 + lane;
+      c[u] = i < hi ? item(i) : 0ull;
     }
-    const unsigned b = __ballot_sync(0xFFFFFFFFu, sel);
-    if (sel) emit(off + __popc(b & lt), i, c);
-    off += __popc(b);
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int i = base + u * 32 + lane;
+      const bool sel = (i < hi) && is_selected(thr, c[u]);
+      const unsigned bm = __ballot_sync(0xFFFFFFFFu, sel);
+      if (sel) emit(off + __popc(bm & lt), i, c[u]);
+      off += __popc(bm);
+    }
   }
   __syncthreads();
   return total;

@@ -90,6 +90,7 @@ struct DecodeParams {
   int nseg;
   int vec_codes;  // codes aligned for 4-key vector loads
   int prep_rep;   // the prep kernel's sample lookups use a bank-replicated LUT
+  int kv_stage;   // the finish kernel stages the shortlist's K and V rows in shared memory
   DecodeSmem lay;
   float* ws_qlow;
   float* ws_lut;
@@ -273,9 +274,9 @@ __device__ void rescore_rows(const DecodeParams& p, int h, const float* ql, cons
   __syncthreads();
 }
 
-// Block copy of n uint2 from global to shared memory with 8 loads in flight per thread; ends
-// with a barrier.
-__device__ inline void copy_batched(uint2* dst, const uint2* src, int n) {
+// Block copy of n candidates (coarse key, index) from global memory into shared memory as
+// select composites (key << 32 | ~index), 8 loads in flight per thread; ends with a barrier.
+__device__ inline void copy_batched(unsigned long long* dst, const uint2* src, int n) {
   constexpr int U = 8;
   for (int base = 0; base < n; base += blockDim.x * U) {
     uint2 v[U];
@@ -287,11 +288,18 @@ __device__ inline void copy_batched(uint2* dst, const uint2* src, int n) {
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int i = base + threadIdx.x + u * blockDim.x;
-      if (i < n) dst[i] = v[u];
+      if (i < n) dst[i] = composite(v[u].x, v[u].y);
     }
   }
   __syncthreads();
 }
+
+// Select items held in an array (one select instantiation shared by the shortlist and budget
+// selects of a CTA, so the second runs from a warm instruction cache).
+struct U64Items {
+  const unsigned long long* a;
+  __device__ unsigned long long operator()(int i) const { return a[i]; }
+};
 
 // Ascending copies of the shortlist / final index sets for the debug outputs.
 __device__ void write_sorted(const int32_t* src, int n, int width, int32_t* dst, unsigned long long* tmp) {
@@ -773,11 +781,15 @@ __device__ int select_shortlist(const DecodeParams& p, int prob, int h, int t, i
   int n_sl = 0;
   if (n_cand >= k) {
     if (n_cand <= kCandSmem) {
-      copy_batched(cand, gc, n_cand);
+      unsigned long long* c64 = reinterpret_cast<unsigned long long*>(cand);
+      copy_batched(c64, gc, n_cand);
       if (tid == 0) stamp(p, prob, 12);
-      auto item = [&](int i) -> unsigned long long { return composite(cand[i].x, cand[i].y); };
+      const U64Items item{c64};
       const SelectThreshold thr = cta_radix_select(item, n_cand, k, sc);
-      n_sl = cta_compact(item, n_cand, thr, [&](int pos, int i, unsigned long long) { emit(pos, cand[i].x, cand[i].y); },
+      n_sl = cta_compact(item, n_cand, thr,
+                         [&](int pos, int, unsigned long long c) {
+                           emit(pos, static_cast<uint32_t>(c >> 32), ~static_cast<uint32_t>(c));
+                         },
                          scratch);
     } else {
       auto item = [&](int i) -> unsigned long long {
@@ -813,11 +825,15 @@ __device__ int select_shortlist(const DecodeParams& p, int prob, int h, int t, i
 }
 
 struct FinishSmem {
-  int qf, ql, lut, sc, scratch, misc, sl, rk, fin, lg, acc, parts, cand, total;
+  int qf, ql, lut, sc, scratch, misc, sl, rk, fin, fpos, lg, acc, parts, own, orow, olg, kv, cand, total;
+  int kv_rows;  // rows of each of the staged K and V slices (0: no staging)
 };
 
-__host__ __device__ inline FinishSmem finish_smem_layout(int head_dim, int sl_cap, int b_cap, int cand_entries) {
+// stage_row_bytes: bytes of one staged K (and one V) row, 0 for no staging.
+__host__ __device__ inline FinishSmem finish_smem_layout(int head_dim, int sl_cap, int b_cap, int cand_entries,
+                                                        int stage_row_bytes) {
   FinishSmem s;
+  const int chunk = (sl_cap + kCluster - 1) / kCluster;
   int o = 0;
   s.qf = o;      o = align16(o + 4 * head_dim);
   s.ql = o;      o = align16(o + 4 * kMaxRank);
@@ -828,15 +844,27 @@ __host__ __device__ inline FinishSmem finish_smem_layout(int head_dim, int sl_ca
   s.sl = o;      o = align16(o + 4 * sl_cap);
   s.rk = o;      o = align16(o + 4 * sl_cap);
   s.fin = o;     o = align16(o + 4 * b_cap);
+  s.fpos = o;    o = align16(o + 4 * b_cap);
   s.lg = o;      o = align16(o + 4 * b_cap);
   s.acc = o;     o = align16(o + 8 * ((kThreads / 32) * 64 + kMaxHeadDim));
   s.parts = o;   o = align16(o + 8 * kCluster * head_dim);
+  s.own = o;     o = align16(o + 4 * chunk);
+  s.orow = o;    o = align16(o + 4 * chunk);
+  s.olg = o;     o = align16(o + 4 * chunk);
+  s.kv_rows = stage_row_bytes > 0 ? chunk : 0;
+  s.kv = o;      o = align16(o + 2 * s.kv_rows * stage_row_bytes);
   s.cand = o;    o = align16(o + 8 * cand_entries);
   s.total = o;
   return s;
 }
 
-// finish: exact shortlist, rescore, budget select and verify for one problem per cluster.
+// One 16-byte global -> shared copy that does not wait (completion: cp.async.wait_all).
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
+
 template <typename T>
 __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
     decode_finish_kernel(const DecodeParams p, const FinishSmem lay) {
@@ -850,9 +878,13 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
   int32_t* sl = reinterpret_cast<int32_t*>(smem + lay.sl);
   uint32_t* rk = reinterpret_cast<uint32_t*>(smem + lay.rk);
   int32_t* fin = reinterpret_cast<int32_t*>(smem + lay.fin);
+  int32_t* fpos = reinterpret_cast<int32_t*>(smem + lay.fpos);
   float* lg = reinterpret_cast<float*>(smem + lay.lg);
   double* acc = reinterpret_cast<double*>(smem + lay.acc);
   double* parts = reinterpret_cast<double*>(smem + lay.parts);
+  int32_t* own = reinterpret_cast<int32_t*>(smem + lay.own);
+  int32_t* orow = reinterpret_cast<int32_t*>(smem + lay.orow);
+  float* olg = reinterpret_cast<float*>(smem + lay.olg);
   uint2* cand = reinterpret_cast<uint2*>(smem + lay.cand);
 
   cg::cluster_group cluster = cg::this_cluster();
@@ -884,50 +916,110 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
   cluster.sync();
 
   // ---- phase 2: rescore, split across the cluster -----------------------------------------
+  // CTA c owns shortlist positions [j0, j1).  With staging (p.kv_stage) it also copies the K
+  // and V rows of those keys into its shared memory with asynchronous copies issued before the
+  // rescore's k_low gathers, so all three gathers are in flight together and the logits and
+  // the weighted sum of the final keys it owns read shared memory.  Without staging the rows
+  // are only prefetched into L2.
   const int32_t* sl0 = cluster.map_shared_rank(sl, 0);
   uint32_t* rk0 = cluster.map_shared_rank(rk, 0);
   const int n_sl = *cluster.map_shared_rank(misc, 0);
+  const int chunk = (n_sl + kCluster - 1) / kCluster;
+  const int j0 = min(n_sl, crank * chunk);
+  const int j1 = min(n_sl, j0 + chunk);
+  const bool staged = p.kv_stage != 0;
+  T* kst = reinterpret_cast<T*>(smem + lay.kv);  // [kv_rows][D]
+  T* vst = kst + (size_t)lay.kv_rows * D;
   {
-    const int chunk = (n_sl + kCluster - 1) / kCluster;
-    const int j0 = min(n_sl, crank * chunk);
-    const int j1 = min(n_sl, j0 + chunk);
     for (int j = j0 + tid; j < j1; j += blockDim.x) sl[j - j0] = sl0[j];
     __syncthreads();
+    const T* kb = reinterpret_cast<const T*>(p.a.keys) + kvh * p.a.k_head_stride;
+    const T* vb = reinterpret_cast<const T*>(p.a.values) + kvh * p.a.v_head_stride;
+    if (staged) {
+      constexpr int kPer = 16 / static_cast<int>(sizeof(T));  // elements per 16-byte copy
+      const int cpr = D / kPer;
+      for (int e = tid; e < (j1 - j0) * cpr; e += blockDim.x) {
+        const int jj = e / cpr, q = e - jj * cpr;
+        const int64_t key = sl[jj];
+        cp_async16(kst + jj * D + q * kPer, kb + key * p.a.k_row_stride + q * kPer);
+        cp_async16(vst + jj * D + q * kPer, vb + key * p.a.v_row_stride + q * kPer);
+      }
+      asm volatile("cp.async.commit_group;\n" ::: "memory");
+    } else {
+      const int row_bytes = D * static_cast<int>(sizeof(T));
+      const int lines = (row_bytes + 127) / 128;
+      for (int e = tid; e < (j1 - j0) * lines; e += blockDim.x) {
+        const int j = e / lines, o = (e - j * lines) * 128;
+        const int64_t key = sl[j];
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(kb + key * p.a.k_row_stride) + o));
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(vb + key * p.a.v_row_stride) + o));
+      }
+    }
     rescore_rows<8>(p, h, ql, sl, j1 - j0, rk);
     for (int j = j0 + tid; j < j1; j += blockDim.x) rk0[j] = rk[j - j0];
   }
   cluster.sync();
   if (crank == 0 && tid == 0) stamp(p, prob, 4);
 
-  // ---- phase 3 (CTA 0): budget select --------------------------------------------------
+  // ---- phase 3 (CTA 0): budget select ------------------------------------------------------
   if (crank == 0) {
+    // composites in the (now free) candidate area, selected by the same code as the shortlist
     const int b = min(p.b_cap, n_sl);
-    auto item = [&](int j) -> unsigned long long { return composite(rk[j], static_cast<uint32_t>(sl[j])); };
-    const SelectThreshold thr = cta_radix_select(item, n_sl, b, sc);
-    const int n_fin = cta_compact(item, n_sl, thr, [&](int pos, int j, unsigned long long) { fin[pos] = sl[j]; },
+    unsigned long long* c64 = reinterpret_cast<unsigned long long*>(cand);
+    for (int j = tid; j < n_sl; j += blockDim.x) c64[j] = composite(rk[j], static_cast<uint32_t>(sl[j]));
+    __syncthreads();
+    const U64Items item{c64};
+    const SelectThreshold thr =
+        cta_radix_select(item, n_sl, b, sc, p.dbg_ts ? p.dbg_ts + (size_t)prob * 16 + 13 : nullptr, 3);
+    const int n_fin = cta_compact(item, n_sl, thr,
+                                  [&](int pos, int j, unsigned long long) {
+                                    fin[pos] = sl[j];
+                                    fpos[pos] = j;
+                                  },
                                   scratch);
     if (tid == 0) misc[1] = n_fin;
   }
   if (crank == 0 && tid == 0) stamp(p, prob, 5);
   cluster.sync();
 
-  // ---- phase 4: logits, split -------------------------------------------------------------
+  // ---- phase 4: logits of the final keys ----------------------------------------------------
   const int32_t* fin0 = cluster.map_shared_rank(fin, 0);
+  const int32_t* fpos0 = cluster.map_shared_rank(fpos, 0);
   float* lg0 = cluster.map_shared_rank(lg, 0);
   const int n_fin = *cluster.map_shared_rank(misc + 1, 0);
-  const int fchunk = (n_fin + kCluster - 1) / kCluster;
-  const int f0 = min(n_fin, crank * fchunk);
-  const int f1 = min(n_fin, f0 + fchunk);
-  // rows of this CTA's slice: CTA 0 reads its own final list (f0 == 0), the others copy theirs
-  int32_t* myrows = fin;
-  {
+  // rows this CTA verifies: staged -> the final keys of its own shortlist slice (own[i] = final
+  // position, orow[i] = staged row); else the slice [f0, f1) of the final list
+  int n_my;
+  int32_t* myrows;
+  if (staged) {
+    if (tid == 0) misc[3] = 0;
+    __syncthreads();
+    for (int q = tid; q < n_fin; q += blockDim.x) {
+      const int j = fpos0[q];
+      if (j >= j0 && j < j1) {
+        const int slot = atomicAdd(misc + 3, 1);
+        own[slot] = q;
+        orow[slot] = j - j0;
+      }
+    }
+    asm volatile("cp.async.wait_all;\n" ::: "memory");
+    __syncthreads();
+    n_my = misc[3];
+    myrows = orow;
+    verify_logits<T, true>(kst, 0, D, 0, qf, D, orow, n_my, p.a.softmax_scale, p.a.logits_mode, olg);
+    for (int i = tid; i < n_my; i += blockDim.x) lg0[own[i]] = olg[i];
+  } else {
+    const int fchunk = (n_fin + kCluster - 1) / kCluster;
+    const int f0 = min(n_fin, crank * fchunk);
+    const int f1 = min(n_fin, f0 + fchunk);
+    n_my = f1 - f0;
+    myrows = fin;  // CTA 0 reads its own final list (f0 == 0), the others copy theirs
     if (crank != 0)
       for (int j = f0 + tid; j < f1; j += blockDim.x) myrows[j - f0] = fin0[j];
     __syncthreads();
-    float* mylg = reinterpret_cast<float*>(rk);
-    verify_logits<T>(p.a.keys, p.a.k_head_stride, p.a.k_row_stride, kvh, qf, D, myrows, f1 - f0,
-                     p.a.softmax_scale, p.a.logits_mode, mylg, p.a.values, p.a.v_head_stride, p.a.v_row_stride);
-    for (int j = f0 + tid; j < f1; j += blockDim.x) lg0[j] = mylg[j - f0];
+    verify_logits<T>(p.a.keys, p.a.k_head_stride, p.a.k_row_stride, kvh, qf, D, myrows, n_my, p.a.softmax_scale,
+                     p.a.logits_mode, olg, p.a.values, p.a.v_head_stride, p.a.v_row_stride);
+    for (int i = tid; i < n_my; i += blockDim.x) lg0[f0 + i] = olg[i];
   }
   cluster.sync();
   if (crank == 0 && tid == 0) stamp(p, prob, 6);
@@ -941,10 +1033,13 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
     float mx, denom;
     softmax_stats(all, n_fin, scratch, acc, &mx, &denom);
     float* w = reinterpret_cast<float*>(rk);
-    for (int j = f0 + tid; j < f1; j += blockDim.x) w[j - f0] = round_to<T>(expf(all[j] - mx) / denom);
+    for (int i = tid; i < n_my; i += blockDim.x) w[i] = round_to<T>(expf(olg[i] - mx) / denom);
     __syncthreads();
     double* sums = acc + (kThreads / 32) * 64;
-    accumulate_rows<T>(p.a.values, p.a.v_head_stride, p.a.v_row_stride, kvh, D, myrows, w, f1 - f0, acc, sums);
+    if (staged)
+      accumulate_rows<T, true>(vst, 0, D, 0, D, myrows, w, n_my, acc, sums);
+    else
+      accumulate_rows<T>(p.a.values, p.a.v_head_stride, p.a.v_row_stride, kvh, D, myrows, w, n_my, acc, sums);
     double* parts0 = cluster.map_shared_rank(parts, 0);
     for (int d = tid; d < D; d += blockDim.x) parts0[crank * D + d] = sums[d];
   }
@@ -1039,8 +1134,18 @@ static int plan_decode(const sva_decode_args* a, DecodePlan* plan, bool force_gr
     p.lay = decode_smem_layout(a->head_dim, p.sl_cap, p.b_cap, cache_bytes);
     plan->smem_bytes = static_cast<size_t>(p.lay.total);
   } else {
-    const int cand_entries = std::max(kCandSmem, dbg_cap);
-    plan->fin_lay = finish_smem_layout(a->head_dim, p.sl_cap, p.b_cap, cand_entries);
+    // the candidate area also holds the budget select's composites (one per shortlist key)
+    const int cand_entries = std::max(std::max(kCandSmem, dbg_cap), p.sl_cap);
+    const int esz = a->qkv_dtype == SVA_DTYPE_F32 ? 4 : 2;
+    const int row_bytes = a->head_dim * esz;
+    const bool aligned = (row_bytes % 16 == 0) && ((a->k_row_stride * esz) % 16 == 0) &&
+                         ((a->v_row_stride * esz) % 16 == 0) && ((a->k_head_stride * esz) % 16 == 0) &&
+                         ((a->v_head_stride * esz) % 16 == 0) && (reinterpret_cast<uintptr_t>(a->keys) % 16 == 0) &&
+                         (reinterpret_cast<uintptr_t>(a->values) % 16 == 0);
+    plan->fin_lay = finish_smem_layout(a->head_dim, p.sl_cap, p.b_cap, cand_entries, aligned ? row_bytes : 0);
+    if (plan->fin_lay.total > kMaxDynSmem - 1024)
+      plan->fin_lay = finish_smem_layout(a->head_dim, p.sl_cap, p.b_cap, cand_entries, 0);
+    p.kv_stage = plan->fin_lay.kv_rows > 0 ? 1 : 0;
     plan->smem_bytes = static_cast<size_t>(plan->fin_lay.total);
     auto take = [&](size_t bytes) {
       size_t o = ws;

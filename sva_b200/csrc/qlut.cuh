@@ -10,11 +10,10 @@
 
 namespace sva {
 
+// q_low = (q . q_proj[h]) * scale[h] into ql (and q as fp32 into qf).  Ends with a barrier.
 template <typename T>
-__device__ void build_query_lut(const T* q, int D, int R, int S, int C, const float* q_proj_h, float scale_h,
-                                const float* codebooks_h, const float* lut_override, float* qf, float* ql, float* lut,
-                                float* stage) {
-  const int sub = R / S;
+__device__ void query_low_smem(const T* q, int D, int R, const float* q_proj_h, float scale_h, float* qf, float* ql,
+                               float* stage) {
   for (int d = threadIdx.x; d < D; d += blockDim.x) qf[d] = to_f32<T>(q[d]);
   const int DR = D * R;
   if ((reinterpret_cast<uintptr_t>(q_proj_h) & 15u) == 0 && (DR & 3) == 0) {
@@ -31,6 +30,14 @@ __device__ void build_query_lut(const T* q, int D, int R, int S, int C, const fl
     ql[r] = __fmul_rn(acc, scale_h);
   }
   __syncthreads();
+}
+
+// lut[s][c] = q_low[s-part] . codebook[s][c] (sequential order).  kCbShared: the codebook is
+// already in shared memory (plain loads).  Ends with a barrier.
+template <bool kCbShared = false>
+__device__ void query_lut(int R, int S, int C, const float* codebooks_h, const float* lut_override, const float* ql,
+                          float* lut) {
+  const int sub = R / S;
   const int SC = S * C;
   if (lut_override) {
     for (int e = threadIdx.x; e < SC; e += blockDim.x) lut[e] = lut_override[e];
@@ -44,7 +51,8 @@ __device__ void build_query_lut(const T* q, int D, int R, int S, int C, const fl
         float4 row[kMaxRank / 4];
 #pragma unroll
         for (int j = 0; j < kMaxRank / 4; ++j)
-          if (4 * j < sub) row[j] = __ldg(reinterpret_cast<const float4*>(cb) + j);
+          if (4 * j < sub)
+            row[j] = kCbShared ? reinterpret_cast<const float4*>(cb)[j] : __ldg(reinterpret_cast<const float4*>(cb) + j);
 #pragma unroll
         for (int j = 0; j < kMaxRank / 4; ++j) {
           if (4 * j < sub) {
@@ -55,12 +63,20 @@ __device__ void build_query_lut(const T* q, int D, int R, int S, int C, const fl
           }
         }
       } else {
-        for (int j = 0; j < sub; ++j) acc = mac(acc, qs[j], __ldg(cb + j));
+        for (int j = 0; j < sub; ++j) acc = mac(acc, qs[j], kCbShared ? cb[j] : __ldg(cb + j));
       }
       lut[e] = acc;
     }
   }
   __syncthreads();
+}
+
+template <typename T>
+__device__ void build_query_lut(const T* q, int D, int R, int S, int C, const float* q_proj_h, float scale_h,
+                                const float* codebooks_h, const float* lut_override, float* qf, float* ql, float* lut,
+                                float* stage) {
+  query_low_smem<T>(q, D, R, q_proj_h, scale_h, qf, ql, stage);
+  query_lut<false>(R, S, C, codebooks_h, lut_override, ql, lut);
 }
 
 }  // namespace sva

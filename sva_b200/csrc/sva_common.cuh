@@ -74,6 +74,17 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { retu
 template <>
 __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
 
+// The same from memory the read-only path cannot address (shared memory): plain loads.
+template <typename T>
+__device__ __forceinline__ float4 load4s(const T* row, int e, int n) {
+  float4 r;
+  r.x = (e + 0 < n) ? to_f32<T>(row[e + 0]) : 0.f;
+  r.y = (e + 1 < n) ? to_f32<T>(row[e + 1]) : 0.f;
+  r.z = (e + 2 < n) ? to_f32<T>(row[e + 2]) : 0.f;
+  r.w = (e + 3 < n) ? to_f32<T>(row[e + 3]) : 0.f;
+  return r;
+}
+
 // Four consecutive elements starting at e (elements at or beyond n read as 0).
 template <typename T>
 __device__ __forceinline__ float4 load4(const T* __restrict__ row, int e, int n) {

@@ -21,7 +21,8 @@ constexpr int kVerifyUnroll = 8;
 
 // `values` (optional): the V rows of the same keys are prefetched into L2 while the K rows load,
 // so that the weighted sum that follows reads them from L2.
-template <typename T>
+// kShared: the rows live in shared memory (staged copies), read with plain loads.
+template <typename T, bool kShared = false>
 __device__ void verify_logits(const void* keys, int64_t k_head_stride, int64_t k_row_stride, int kvh, const float* qf,
                               int D, const int32_t* rows, int n, float softmax_scale, int logits_mode, float* lg,
                               const void* values = nullptr, int64_t v_head_stride = 0, int64_t v_row_stride = 0) {
@@ -40,7 +41,12 @@ __device__ void verify_logits(const void* keys, int64_t k_head_stride, int64_t k
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int j = base + 2 * u + half;
-        k4[u] = (j < n && e < D) ? load4<T>(kb + (int64_t)rows[j] * k_row_stride, e, D) : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (j < n && e < D) {
+          const T* kr = kb + (int64_t)rows[j] * k_row_stride;
+          k4[u] = kShared ? load4s<T>(kr, e, D) : load4<T>(kr, e, D);
+        } else {
+          k4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
       }
       if (vb) {
         // one prefetch per 128-byte line of each row's chunk: lanes l16 = 0, 8 of every half-warp
@@ -127,7 +133,7 @@ __device__ void softmax_weights(float* lg, int n, float mx, float denom) {
 
 // out[d] = sum_j round_T(w[j] * V[rows[j]][d]) in fp64 for d < D (written by threads 0..63 per
 // 64-wide chunk).  `acc` needs (blockDim.x / 32) * 64 doubles.
-template <typename T>
+template <typename T, bool kShared = false>
 __device__ void accumulate_rows(const void* values, int64_t v_head_stride, int64_t v_row_stride, int kvh, int D,
                                 const int32_t* rows, const float* w, int n, double* acc, double* out) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
@@ -147,7 +153,8 @@ __device__ void accumulate_rows(const void* values, int64_t v_head_stride, int64
         v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
         wu[u] = 0.f;
         if (j < n && e < D) {
-          v[u] = load4<T>(vb + (int64_t)rows[j] * v_row_stride, e, D);
+          const T* vr = vb + (int64_t)rows[j] * v_row_stride;
+          v[u] = kShared ? load4s<T>(vr, e, D) : load4<T>(vr, e, D);
           wu[u] = w[j];
         }
       }
