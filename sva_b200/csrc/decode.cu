@@ -504,6 +504,7 @@ __global__ void __launch_bounds__(kThreads) decode_prep_kernel(const DecodeParam
   const int prob = blockIdx.x;
   const int h = prob / p.a.n_queries, t = prob - h * p.a.n_queries;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_launch_dependents();  // the scan may be scheduled now; it waits for this grid's results
   if (tid == 0) stamp(p, prob, 0);
   const int64_t len_t = allowed_length(p, t);
   const uint8_t* codes = p.a.codes + h * p.a.codes_head_stride;
@@ -516,7 +517,15 @@ __global__ void __launch_bounds__(kThreads) decode_prep_kernel(const DecodeParam
     }
     asm volatile("cp.async.commit_group;\n" ::: "memory");
   }
-  build_qlut<T>(p, h, t, qf, ql, lut, stage);
+  {
+    // q_proj (a weight) is staged before waiting for the predecessor; q, and every write to the
+    // workspace the previous decode's finish kernel reads, come after the wait
+    const int D = p.a.head_dim, R = p.a.rank_dim, S2 = p.a.subspaces, C2 = p.a.codewords;
+    const T* q = reinterpret_cast<const T*>(p.a.query) + h * p.a.q_head_stride + t * p.a.q_row_stride;
+    const float* lo = p.a.lut_override ? p.a.lut_override + ((size_t)h * p.a.n_queries + t) * S2 * C2 : nullptr;
+    query_low_smem<T, true>(q, D, R, p.a.q_proj + (size_t)h * D * R, __ldg(p.a.scale + h), qf, ql, stage);
+    query_lut<false>(R, S2, C2, p.a.codebooks + (size_t)h * S2 * C2 * (R / S2), lo, ql, lut);
+  }
   if (tid == 0) stamp(p, prob, 9);
   const int C = p.a.codewords;
   const int SC = p.a.subspaces * C;
@@ -657,6 +666,8 @@ __global__ void __launch_bounds__(kScanThreads, 4) decode_scan_kernel(const Deco
   const int prob = blockIdx.y, seg = blockIdx.x;
   const int h = prob / p.a.n_queries, t = prob - h * p.a.n_queries;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_launch_dependents();
+  pdl_wait();  // prep's LUT, q_low and threshold
   uint32_t* ctrl = p.ws_ctrl + (size_t)prob * CTRL_WORDS;
   const uint32_t t0 = __ldcg(ctrl + CTRL_T0);
   const int SC = p.a.subspaces * p.a.codewords;
@@ -900,7 +911,9 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
 
   {
     const T* q = reinterpret_cast<const T*>(p.a.query) + h * p.a.q_head_stride + t * p.a.q_row_stride;
+    pdl_launch_dependents();  // a following decode's prep may start prefetching its inputs
     for (int d = tid; d < D; d += blockDim.x) qf[d] = to_f32<T>(q[d]);
+    pdl_wait();  // the scan's candidates (and prep's q_low)
     for (int r = tid; r < R; r += blockDim.x) ql[r] = __ldcg(p.ws_qlow + (size_t)prob * kMaxRank + r);
   }
   __syncthreads();
@@ -1071,6 +1084,23 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
 // host side
 // ---------------------------------------------------------------------------------------
 
+// Launch as a programmatic dependent of the previous kernel in the stream (see pdl_wait).
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                                   Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 static bool pow2_float(double x) {
   int e;
   const double m = frexp(x, &e);
@@ -1164,16 +1194,16 @@ static int plan_decode(const sva_decode_args* a, DecodePlan* plan, bool force_gr
 
 template <int S, int C>
 static void launch_scan(const DecodeParams& p, int P, cudaStream_t stream) {
-  if (p.sqrt_r_pow2) decode_scan_kernel<S, C, true><<<dim3(p.nseg, P), kScanThreads, 0, stream>>>(p);
-  else decode_scan_kernel<S, C, false><<<dim3(p.nseg, P), kScanThreads, 0, stream>>>(p);
+  if (p.sqrt_r_pow2) launch_dependent(decode_scan_kernel<S, C, true>, dim3(p.nseg, P), dim3(kScanThreads), 0, stream, p);
+  else launch_dependent(decode_scan_kernel<S, C, false>, dim3(p.nseg, P), dim3(kScanThreads), 0, stream, p);
 }
 
 template <typename T, int S>
 static int launch_prep(const DecodeParams& p, int P, int smem, cudaStream_t stream) {
   int rc = ensure_smem_attr(reinterpret_cast<const void*>(decode_prep_kernel<T, S>), smem);
   if (rc != SVA_OK) return rc;
-  decode_prep_kernel<T, S><<<P, kThreads, smem, stream>>>(p);
-  return SVA_OK;
+  const cudaError_t e = launch_dependent(decode_prep_kernel<T, S>, dim3(P), dim3(kThreads), smem, stream, p);
+  return e == cudaSuccess ? SVA_OK : set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
 }
 
 // Points the planned workspace offsets at `ws`.
@@ -1247,7 +1277,9 @@ static int launch_decode(DecodePlan& plan, void* ws, cudaStream_t stream) {
     if (rc != SVA_OK) return rc;
     rc = ensure_smem_attr(reinterpret_cast<const void*>(decode_finish_kernel<T>), static_cast<int>(plan.smem_bytes));
     if (rc != SVA_OK) return rc;
-    decode_finish_kernel<T><<<P * kCluster, kThreads, plan.smem_bytes, stream>>>(p, plan.fin_lay);
+    cudaError_t le = launch_dependent(decode_finish_kernel<T>, dim3(P * kCluster), dim3(kThreads), plan.smem_bytes,
+                                      stream, p, plan.fin_lay);
+    if (le != cudaSuccess) return set_error(SVA_ERR_CUDA, cudaGetErrorString(le));
     profile_mark(2, stream);
   }
   cudaError_t e = cudaGetLastError();

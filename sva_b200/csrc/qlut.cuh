@@ -11,10 +11,13 @@
 namespace sva {
 
 // q_low = (q . q_proj[h]) * scale[h] into ql (and q as fp32 into qf).  Ends with a barrier.
-template <typename T>
+// kWaitForQ: q_proj is staged first, then the kernel waits for its predecessor (pdl_wait)
+// before reading q.
+template <typename T, bool kWaitForQ = false>
 __device__ void query_low_smem(const T* q, int D, int R, const float* q_proj_h, float scale_h, float* qf, float* ql,
                                float* stage) {
-  for (int d = threadIdx.x; d < D; d += blockDim.x) qf[d] = to_f32<T>(q[d]);
+  if (!kWaitForQ)
+    for (int d = threadIdx.x; d < D; d += blockDim.x) qf[d] = to_f32<T>(q[d]);
   const int DR = D * R;
   if ((reinterpret_cast<uintptr_t>(q_proj_h) & 15u) == 0 && (DR & 3) == 0) {
     const float4* src = reinterpret_cast<const float4*>(q_proj_h);
@@ -22,6 +25,10 @@ __device__ void query_low_smem(const T* q, int D, int R, const float* q_proj_h, 
     for (int e = threadIdx.x; e < DR / 4; e += blockDim.x) dst[e] = __ldg(src + e);
   } else {
     for (int e = threadIdx.x; e < DR; e += blockDim.x) stage[e] = __ldg(q_proj_h + e);
+  }
+  if (kWaitForQ) {
+    pdl_wait();
+    for (int d = threadIdx.x; d < D; d += blockDim.x) qf[d] = to_f32<T>(q[d]);
   }
   __syncthreads();
   for (int r = threadIdx.x; r < R; r += blockDim.x) {

@@ -130,6 +130,13 @@ __device__ __forceinline__ float4 load4<__nv_bfloat16>(const __nv_bfloat16* __re
 // canonical dot products
 // ---------------------------------------------------------------------------------------
 
+// Programmatic dependent launch: a kernel launched with programmatic stream serialization may
+// start while its predecessor in the stream still runs; it waits here before touching anything
+// the predecessor writes (a no-op for an ordinary launch).  The predecessor lets it start once
+// every one of its CTAs has run launch_dependents.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ float mac(float acc, float a, float b) { return __fadd_rn(acc, __fmul_rn(a, b)); }
 
 // Partial of one tree_dot lane: elements 4j..4j+3 summed in order from 0.
