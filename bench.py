@@ -236,7 +236,7 @@ def reference_arm(args):
                          "sample": f"{args.heads} heads x {args.keys} keys ({args.pq}), 1 query token per step"},
         "e2e": {"value": round(us, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -553,7 +553,7 @@ def gpu_arm(args):
                                 "sample": f"{len(times)} query tokens x {args.heads} heads x {args.keys} keys "
                                           f"({args.pq}), random catalog"}
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
     if group is not None:
         del graph
         torch.distributed.barrier(group)
@@ -606,8 +606,24 @@ def e2e_measure(args, sets, one_query, device, group):
                     + " (eager ctypes calls per query) with pinned host q/out"}
 
 
+# The JSON line is the only thing bench.py writes to its standard output: file descriptor 1 is
+# pointed at stderr for everything else (NCCL's version banner, library messages), and the line
+# goes to a duplicate of the original stdout.
+_JSON_OUT = None
+
+
+def emit(line: dict) -> None:
+    out = _JSON_OUT if _JSON_OUT is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 def main():
+    global _JSON_OUT
     args = parse_args()
+    sys.stdout.flush()
+    _JSON_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     if args.impl == "reference":
         return reference_arm(args)
     return gpu_arm(args)
