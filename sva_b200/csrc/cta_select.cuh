@@ -6,14 +6,18 @@
 // the CPU oracle applies to every torch.topk of the reference (sva/llama.py:278, :295, :100,
 // :113).
 //
-// The select first finds the range [min, max] of the non-zero items, then runs an MSB-first
-// radix select on (c - min) with 11-bit digits starting at the highest bit of (max - min): each
-// level divides the current window into 2048 equal bins, counts the items of the window per bin
-// (a functor call per item, so items may live in shared memory or be re-read from global
-// memory) and keeps the bin holding the k-th item.  Starting at the range's own top bit keeps
-// items that share their high bits (every candidate above a threshold does) from piling into
-// one bin.  It stops as soon as the boundary bin holds exactly the number of items still
-// needed.  The result is a plain threshold: an item is selected iff c != 0 and c >= prefix.
+// Two selects, both exact and both returning a plain threshold (an item is selected iff c != 0
+// and c >= prefix):
+// * cta_radix_select finds the range [min, max] of the non-zero items, then runs an MSB-first
+//   radix select on (c - min) with 10-bit digits starting at the highest bit of (max - min):
+//   each level divides the current window into 1024 equal bins, counts the items of the window
+//   per bin (a functor call per item, so items may live in shared memory or be re-read from
+//   global memory) and keeps the bin holding the k-th item.  Starting at the range's own top
+//   bit keeps items that share their high bits (every candidate above a threshold does) from
+//   piling into one bin.  It stops as soon as the boundary bin holds exactly the number of
+//   items still needed.
+// * cta_select_linear takes a known score range, counts the items into 1024 equal-width score
+//   bins in one pass and ranks the few items of the boundary bin directly.
 #pragma once
 
 #include "sva_common.cuh"
@@ -183,6 +187,140 @@ __device__ SelectThreshold cta_radix_select(const ItemFn& item, int n, int k, Se
   return thr;
 }
 
+// Locates the bin holding the k-th largest item of hist[0, kSelectBins) counted from the top:
+// writes the bin to sc->digit[buf], the items in higher bins to sc->above[buf] and the bin's
+// count to sc->count[buf]; returns the total count.  Two barriers; the results are visible to
+// every thread on return.
+__device__ __forceinline__ int select_find_bin(const uint32_t* hist, int remaining, SelectScratch* sc, int buf) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  const int per = kSelectBins / blockDim.x;
+  int cnt = 0;
+  for (int q = 0; q < per; ++q) cnt += static_cast<int>(hist[kSelectBins - 1 - (per * tid + q)]);
+  const int incl_w = warp_incl_scan(cnt);
+  if (lane == 31) sc->warp_tot[buf][warp] = incl_w;
+  __syncthreads();
+  const int wt = lane < nwarps ? sc->warp_tot[buf][lane] : 0;
+  const int wincl = warp_incl_scan(wt);
+  const int total = __shfl_sync(0xFFFFFFFFu, wincl, 31);
+  const int wexcl = __shfl_sync(0xFFFFFFFFu, wincl - wt, warp);
+  const int incl = incl_w + wexcl;
+  const int excl = incl - cnt;
+  if (excl < remaining && incl >= remaining) {
+    int run = excl;
+    for (int q = 0; q < per; ++q) {
+      const int b = kSelectBins - 1 - (per * tid + q);
+      const int v = static_cast<int>(hist[b]);
+      if (run + v >= remaining) {
+        sc->digit[buf] = b;
+        sc->above[buf] = run;
+        sc->count[buf] = v;
+        break;
+      }
+      run += v;
+    }
+  }
+  __syncthreads();
+  return total;
+}
+
+constexpr int kLinearRankMax = kSelectBins / 2;  // boundary-bin items ranked directly (u64 in hist[1])
+
+// Exact top-k like cta_radix_select, for items whose scores are known to lie in [lo, hi] (the
+// score of item c is key_to_float(c >> 32)).  One counting pass puts every item into one of
+// kSelectBins equal-width bins of [lo, hi]; the bin index is a monotone function of the score
+// (scores outside the range land in the end bins), so every item of a higher bin ranks above
+// every item of a lower one.  The items of the bin holding the k-th item are then ranked among
+// themselves by composite.  Uses fallback() (another exact select) when the range is empty or
+// not finite, or the boundary bin holds more than kLinearRankMax items.  Barriers: five.
+template <class ItemFn, class Fallback>
+__device__ SelectThreshold cta_select_linear(const ItemFn& item, int n, int k, float lo, float hi, SelectScratch* sc,
+                                             const Fallback& fallback) {
+  SelectThreshold thr;
+  thr.mask = ~0ull;
+  if (k <= 0) {
+    thr.prefix = ~0ull;
+    thr.mask = 0ull;
+    return thr;
+  }
+  const float span = hi - lo;
+  if (!(span > 0.f) || !isfinite(span)) return fallback();
+  const float scale = (static_cast<float>(kSelectBins) - 0.5f) / span;
+  if (!isfinite(scale) || !(scale > 0.f)) return fallback();
+  const int tid = threadIdx.x;
+  auto bin_of = [&](unsigned long long c) -> int {
+    const uint32_t key = static_cast<uint32_t>(c >> 32);
+    const float x = __fmul_rn(__fsub_rn(key_to_float(key), lo), scale);
+    if (x != x) return key >= 0x80000000u ? kSelectBins - 1 : 0;  // NaN: where its key orders it
+    return x > 0.f ? static_cast<int>(fminf(x, static_cast<float>(kSelectBins - 1))) : 0;
+  };
+  uint32_t* hist = sc->hist[0];
+  for (int b = tid; b < kSelectBins; b += blockDim.x) hist[b] = 0u;
+  if (tid == 0) sc->count[1] = 0;
+  __syncthreads();
+  constexpr int kBatch = 8;
+  for (int i0 = tid; i0 < n; i0 += kBatch * blockDim.x) {
+    unsigned long long c[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int i = i0 + u * blockDim.x;
+      c[u] = i < n ? item(i) : 0ull;
+    }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u)
+      if (c[u] != 0ull) atomicAdd(&hist[bin_of(c[u])], 1u);
+  }
+  __syncthreads();
+  const int total = select_find_bin(hist, k, sc, 0);
+  if (total < k) {  // fewer items than k: every non-zero item
+    thr.prefix = 1ull;
+    return thr;
+  }
+  const int bstar = sc->digit[0], need = k - sc->above[0], cnt = sc->count[0];
+  if (cnt > kLinearRankMax) return fallback();
+  unsigned long long* list = reinterpret_cast<unsigned long long*>(sc->hist[1]);
+  for (int i0 = tid; i0 < n; i0 += kBatch * blockDim.x) {
+    unsigned long long c[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int i = i0 + u * blockDim.x;
+      c[u] = i < n ? item(i) : 0ull;
+    }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u)
+      if (c[u] != 0ull && bin_of(c[u]) == bstar) list[atomicAdd(&sc->count[1], 1)] = c[u];
+  }
+  __syncthreads();
+  // the need-th largest composite of the boundary bin (composites are distinct)
+  for (int i = tid; i < cnt; i += blockDim.x) {
+    const unsigned long long v = list[i];
+    int above = 0;
+    for (int j = 0; j < cnt; ++j) above += list[j] > v;
+    if (above == need - 1) sc->lo_part[0] = v;
+  }
+  __syncthreads();
+  thr.prefix = sc->lo_part[0];
+  return thr;
+}
+
+// Items held in a shared-memory array.
+struct U64Items {
+  const unsigned long long* a;
+  __device__ unsigned long long operator()(int i) const { return a[i]; }
+};
+
+// Selects over a shared-memory array of composites (one instantiation serves every caller in a
+// kernel).
+static __device__ __forceinline__ SelectThreshold radix_select_u64(const unsigned long long* a, int n, int k,
+                                                                  SelectScratch* sc) {
+  return cta_radix_select(U64Items{a}, n, k, sc);
+}
+
+// cta_select_linear over a[0, n) (fallback: radix_select_u64).
+static __device__ __forceinline__ SelectThreshold select_u64(const unsigned long long* a, int n, int k, float lo,
+                                                            float hi, SelectScratch* sc) {
+  return cta_select_linear(U64Items{a}, n, k, lo, hi, sc, [&]() { return radix_select_u64(a, n, k, sc); });
+}
+
 // Stable compaction of the selected items in item order: emit(pos, i, c) is called once per
 // selected item with consecutive positions from 0.  Returns the number emitted.  Warps own
 // contiguous item ranges, so output order equals item order.
@@ -253,6 +391,17 @@ __device__ __forceinline__ void cta_bitonic_sort_u64(unsigned long long* v, int 
       __syncthreads();
     }
   }
+}
+
+}  // namespace sva
+
+namespace sva {
+
+// Stable compaction of the selected items of a[0, n): out[pos] = i for the pos-th selected item
+// i in item order.  Returns the count; ends with a barrier.
+static __device__ __forceinline__ int compact_u64(const unsigned long long* a, int n, SelectThreshold thr, int32_t* out,
+                                                  int* scratch) {
+  return cta_compact(U64Items{a}, n, thr, [&](int pos, int i, unsigned long long) { out[pos] = i; }, scratch);
 }
 
 }  // namespace sva

@@ -38,20 +38,31 @@ namespace sva {
 namespace cg = cooperative_groups;
 
 constexpr int kThreads = 512;
-constexpr int kScanKeys = 16384;         // keys per scan CTA
+constexpr int kScanKeys = 32768;         // keys per scan CTA
 constexpr int kFusedMaxKeys = 32768;
 constexpr int kCandSmem = 12288;         // candidates selected in shared memory
-constexpr int kScanThreads = 256;
+constexpr int kScanThreads = 512;
 constexpr int kGroupsInFlight = 4;
 constexpr int kSampleRuns = 64;
 constexpr int kSampleRunKeys = 256;
 constexpr int kSample = kSampleRuns * kSampleRunKeys;
-constexpr int kPrepSmemLimit = 192 * 1024;  // dynamic shared memory of the prep kernel
+constexpr int kPrepCtas = 4;                // prep CTAs per problem, each samples kSample / kPrepCtas keys
+constexpr int kPrepGroups = kSample / kPrepCtas / 4 / kThreads;  // 4-key sample groups per prep thread
+constexpr int kPrepSmemLimit = 200 * 1024;  // dynamic shared memory of the prep kernel
 constexpr int kCluster = 8;
 constexpr int kScanLocalCands = 1024;
 constexpr int kRepEntries = 256;  // largest S * C of the bank-replicated scan LUT
 
-enum { CTRL_NCAND = 0, CTRL_T0, CTRL_WORDS = 4 };
+// Control words per problem: the candidate count, the largest candidate key, and one threshold
+// per prep CTA (the scan's threshold T0 is their minimum).
+enum { CTRL_NCAND = 0, CTRL_MAXKEY, CTRL_T0, CTRL_WORDS = CTRL_T0 + kPrepCtas + 2 };
+
+__device__ __forceinline__ uint32_t read_t0(const uint32_t* ctrl) {
+  uint32_t t0 = __ldcg(ctrl + CTRL_T0);
+#pragma unroll
+  for (int c = 1; c < kPrepCtas; ++c) t0 = min(t0, __ldcg(ctrl + CTRL_T0 + c));
+  return t0;
+}
 
 struct DecodeSmem {
   int qf, ql, lut, sc, scratch, sl, rk, fin, lg, acc, cache, total;
@@ -247,37 +258,53 @@ __device__ __forceinline__ int block_sum_int(int v, int* scratch) {
 // ---------------------------------------------------------------------------------------
 
 // Rank keys of shortlist rows [0, n): two rows per warp step (one per half-warp), U steps in
-// flight.  `rows` are key indices; rk[j] receives the ordered rank score of rows[j].
-template <int U>
-__device__ void rescore_rows(const DecodeParams& p, int h, const float* ql, const int32_t* rows, int n, uint32_t* rk) {
+// flight.  `rows` are key indices; rk[j] receives the ordered rank score of rows[j].  Each
+// thread calls after_first_loads() once, after issuing its first round of row loads and before
+// using them (so that other gathers can be issued while those are in flight).  Ends with a
+// barrier.
+struct NoHook {
+  __device__ void operator()() const {}
+};
+
+template <int U, class Hook = NoHook>
+__device__ void rescore_rows(const DecodeParams& p, int h, const float* ql, const int32_t* rows, int n, uint32_t* rk,
+                             const Hook& after_first_loads = Hook()) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int half = lane >> 4, l16 = lane & 15;
   const int R = p.a.rank_dim;
   const float4 q4 = (4 * l16 < R) ? make_float4(ql[4 * l16], ql[4 * l16 + 1], ql[4 * l16 + 2], ql[4 * l16 + 3])
                                   : make_float4(0.f, 0.f, 0.f, 0.f);
   const float* klb = p.a.k_low + h * p.a.k_low_head_stride;
-  for (int base = warp * 2 * U; base < n; base += nwarps * 2 * U) {
-    float4 r[U];
+  float4 r[U];
+  auto load = [&](int base) {
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int j = base + 2 * u + half;
       r[u] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (j < n && 4 * l16 < R) r[u] = load4<float>(klb + (int64_t)rows[j] * R, 4 * l16, R);
     }
+  };
+  int base = warp * 2 * U;
+  load(base);
+  after_first_loads();
+  for (;;) {
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int j = base + 2 * u + half;
       const float s = tree16(lane4(r[u], q4));
       if (j < n && l16 == 0) rk[j] = ordered_key(finish_score(s, p));
     }
+    base += nwarps * 2 * U;
+    if (base >= n) break;
+    load(base);
   }
   __syncthreads();
 }
 
 // Block copy of n candidates (coarse key, index) from global memory into shared memory as
-// select composites (key << 32 | ~index), 8 loads in flight per thread; ends with a barrier.
+// select composites (key << 32 | ~index), 16 loads in flight per thread; ends with a barrier.
 __device__ inline void copy_batched(unsigned long long* dst, const uint2* src, int n) {
-  constexpr int U = 8;
+  constexpr int U = 16;
   for (int base = 0; base < n; base += blockDim.x * U) {
     uint2 v[U];
 #pragma unroll
@@ -293,13 +320,6 @@ __device__ inline void copy_batched(unsigned long long* dst, const uint2* src, i
   }
   __syncthreads();
 }
-
-// Select items held in an array (one select instantiation shared by the shortlist and budget
-// selects of a CTA, so the second runs from a warm instruction cache).
-struct U64Items {
-  const unsigned long long* a;
-  __device__ unsigned long long operator()(int i) const { return a[i]; }
-};
 
 // Ascending copies of the shortlist / final index sets for the debug outputs.
 __device__ void write_sorted(const int32_t* src, int n, int width, int32_t* dst, unsigned long long* tmp) {
@@ -427,11 +447,11 @@ __device__ __forceinline__ void scan_segment(const DecodeParams& p, const uint8_
   }
 }
 
-// Start key of this thread's u-th sample group: groups g = tid + u * kThreads of four consecutive
-// keys; group g lies in run g / (kSampleRunKeys / 4); runs start on multiples of four keys.
-__device__ __forceinline__ int64_t sample_group_start(int64_t len_t, int u) {
+// Start key of sample group g (of kSample / 4): groups of four consecutive keys, group g lies in
+// run g / (kSampleRunKeys / 4); the kSampleRuns runs are evenly spaced over the allowed range and
+// start on multiples of four keys.
+__device__ __forceinline__ int64_t sample_group_start(int64_t len_t, int g) {
   constexpr int kRunGroups = kSampleRunKeys / 4;
-  const int g = threadIdx.x + u * kThreads;
   const int run = g / kRunGroups, off = (g - run * kRunGroups) * 4;
   return ((len_t * run) / kSampleRuns & ~static_cast<int64_t>(3)) + off;
 }
@@ -452,11 +472,24 @@ __device__ __forceinline__ void copy_group_async(uint8_t* dst, const uint8_t* sr
   }
 }
 
-// Dynamic shared memory of the prep kernel: the LUT stage (later the sample's keys), then,
-// for the vector-code variants, the sampled codes (kSample keys x S bytes), then, when
-// S * C <= kRepEntries, the bank-replicated LUT.
-__host__ __device__ inline int prep_stage_bytes(int head_dim, int rank_dim) {
-  return 4 * head_dim * rank_dim > 4 * kSample ? 4 * head_dim * rank_dim : 4 * kSample;
+// Dynamic shared memory of a prep CTA: q_proj[h] (later the sampled keys), the codebooks of h,
+// the sampled codes of the vector-code variants, and the bank-replicated LUT when S * C <=
+// kRepEntries.
+struct PrepSmem {
+  int stage, cb, sample, rep, total;
+};
+
+__host__ __device__ inline PrepSmem prep_smem_layout(int head_dim, int rank_dim, int codewords, int S_vec, bool rep) {
+  PrepSmem s;
+  int o = 0;
+  const int keys_bytes = 4 * 4 * kThreads * kPrepGroups;
+  const int stage = 4 * head_dim * rank_dim > keys_bytes ? 4 * head_dim * rank_dim : keys_bytes;
+  s.stage = o;  o = align16(o + stage);
+  s.cb = o;     o = align16(o + 4 * codewords * rank_dim);
+  s.sample = o; o = align16(o + 4 * kThreads * kPrepGroups * S_vec);
+  s.rep = o;    o = align16(o + (rep ? 4 * 32 * kRepEntries : 0));
+  s.total = o;
+  return s;
 }
 
 // ADC sum of key j from a bank-replicated LUT with a runtime codeword count (codes clamped to
@@ -470,68 +503,88 @@ __device__ __forceinline__ float adc_rep_rt(const Codes4<S>& c, int j, const flo
   return sum;
 }
 
-// Keeps the four largest values seen, t[0] >= t[1] >= t[2] >= t[3].
-__device__ __forceinline__ void top4_insert(uint32_t (&t)[4], uint32_t x) {
-#pragma unroll
-  for (int q = 0; q < 3; ++q) {
-    const uint32_t hi = max(t[q], x);
-    x = min(t[q], x);
-    t[q] = hi;
+// 16-byte-vector copy of n floats (n % 4 == 0, both 16-byte aligned) or a scalar copy.
+__device__ __forceinline__ void stage_floats(float* dst, const float* src, int n) {
+  if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0 && (n & 3) == 0) {
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    float4* d4 = reinterpret_cast<float4*>(dst);
+    for (int e = threadIdx.x; e < n / 4; e += blockDim.x) d4[e] = __ldg(s4 + e);
+  } else {
+    for (int e = threadIdx.x; e < n; e += blockDim.x) dst[e] = __ldg(src + e);
   }
-  t[3] = max(t[3], x);
 }
 
-// prep: q_low + LUT, and the sampled threshold T0 (an ordered key; 1 = every allowed key).
-// The sample is kSampleRuns evenly spaced runs of kSampleRunKeys keys over the allowed range;
-// its codes are copied to shared memory asynchronously while the query LUT is built.  T0 is
-// the r-th best key of the sample, r chosen so that about 2x the shortlist plus a margin is
-// expected at or above it.  When r <= 4 * kThreads the select runs over the four best keys of
-// every thread's share, whose r-th best can only be lower than the sample's (a safe, slightly
-// larger candidate set); otherwise over the whole sample.
+// prep: q_low + LUT, and the sampled thresholds.  kPrepCtas CTAs per problem; CTA `part` scores
+// the sample groups [part * kThreads * kPrepGroups, ...) (kSample / kPrepCtas keys) and writes
+// T0_part, a lower bound of the r-th best of its sampled keys with r = ceil(2 * shortlist *
+// n_part / len), n_part its number of allowed sampled keys.  The scan keeps keys >= T0 = min
+// over parts: at least sum(r) >= 2 * shortlist * n / len keys of the whole sample are >= T0, so
+// about twice the shortlist is expected among all keys, and fewer than the shortlist only if
+// every part's estimate errs high together.  T0 only sizes the candidate set: if fewer keys
+// than the shortlist reach it, the finish kernel selects over every key.  The bound is the lower
+// edge of the bin below the one holding the r-th best key, in 1024 equal-width bins over the
+// part's sampled score range (one counting pass, no exact select).  Every part computes q_low
+// and the LUT (part 0 publishes them).  Inputs that are weights (q_proj, codebooks, the sampled
+// codes) are staged before waiting for the predecessor; q and every workspace write come after.
 template <typename T, int S>
-__global__ void __launch_bounds__(kThreads) decode_prep_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(kThreads) decode_prep_kernel(const DecodeParams p, const PrepSmem lay) {
   extern __shared__ __align__(16) unsigned char dyn[];
   __shared__ float qf[kMaxHeadDim];
   __shared__ float ql[kMaxRank];
   __shared__ float lut[kMaxLut];
-  __shared__ int scratch[64];
   __shared__ SelectScratch sel;
-  __shared__ __align__(16) uint32_t tops[4 * kThreads];
-  float* stage = reinterpret_cast<float*>(dyn);
-  const int stage_bytes = prep_stage_bytes(p.a.head_dim, p.a.rank_dim);
-  uint8_t* sample = dyn + stage_bytes;
-  float* lut_rep = reinterpret_cast<float*>(dyn + stage_bytes + (S > 0 ? kSample * S : 0));
-  const int prob = blockIdx.x;
+  float* stage = reinterpret_cast<float*>(dyn + lay.stage);
+  float* cbs = reinterpret_cast<float*>(dyn + lay.cb);
+  uint8_t* sample = dyn + lay.sample;
+  float* lut_rep = reinterpret_cast<float*>(dyn + lay.rep);
+  uint32_t* skeys = reinterpret_cast<uint32_t*>(dyn + lay.stage);  // after q_low: the sampled keys
+  const int prob = blockIdx.x / kPrepCtas, part = blockIdx.x - prob * kPrepCtas;
   const int h = prob / p.a.n_queries, t = prob - h * p.a.n_queries;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int D = p.a.head_dim, R = p.a.rank_dim, S2 = p.a.subspaces, C = p.a.codewords;
+  const int SC = S2 * C;
   pdl_launch_dependents();  // the scan may be scheduled now; it waits for this grid's results
-  if (tid == 0) stamp(p, prob, 0);
+  if (part == 0 && tid == 0) stamp(p, prob, 0);
   const int64_t len_t = allowed_length(p, t);
   const uint8_t* codes = p.a.codes + h * p.a.codes_head_stride;
-  constexpr int kGroups = kSample / kThreads / 4;
+  const int g_first = part * kThreads * kPrepGroups;
   if constexpr (S > 0) {
 #pragma unroll
-    for (int u = 0; u < kGroups; ++u) {
-      const int64_t g0 = sample_group_start(len_t, u);
-      if (g0 + 3 < len_t) copy_group_async<S>(sample + (tid + u * kThreads) * 4 * S, codes + g0 * S);
+    for (int u = 0; u < kPrepGroups; ++u) {
+      const int gl = tid + u * kThreads;
+      const int64_t g0 = sample_group_start(len_t, g_first + gl);
+      if (g0 + 3 < len_t) copy_group_async<S>(sample + gl * 4 * S, codes + g0 * S);
     }
     asm volatile("cp.async.commit_group;\n" ::: "memory");
   }
+  const float* lo = p.a.lut_override ? p.a.lut_override + ((size_t)h * p.a.n_queries + t) * SC : nullptr;
+  stage_floats(stage, p.a.q_proj + (size_t)h * D * R, D * R);
+  if (!lo) stage_floats(cbs, p.a.codebooks + (size_t)h * C * R, C * R);
+  pdl_wait();
   {
-    // q_proj (a weight) is staged before waiting for the predecessor; q, and every write to the
-    // workspace the previous decode's finish kernel reads, come after the wait
-    const int D = p.a.head_dim, R = p.a.rank_dim, S2 = p.a.subspaces, C2 = p.a.codewords;
     const T* q = reinterpret_cast<const T*>(p.a.query) + h * p.a.q_head_stride + t * p.a.q_row_stride;
-    const float* lo = p.a.lut_override ? p.a.lut_override + ((size_t)h * p.a.n_queries + t) * S2 * C2 : nullptr;
-    query_low_smem<T, true>(q, D, R, p.a.q_proj + (size_t)h * D * R, __ldg(p.a.scale + h), qf, ql, stage);
-    query_lut<false>(R, S2, C2, p.a.codebooks + (size_t)h * S2 * C2 * (R / S2), lo, ql, lut);
+    for (int d = tid; d < D; d += blockDim.x) qf[d] = to_f32<T>(q[d]);
   }
-  if (tid == 0) stamp(p, prob, 9);
-  const int C = p.a.codewords;
-  const int SC = p.a.subspaces * C;
-  float* gl = p.ws_lut + (size_t)prob * kMaxLut;
-  for (int e = tid; e < SC; e += blockDim.x) gl[e] = lut[e];
-  for (int r = tid; r < p.a.rank_dim; r += blockDim.x) p.ws_qlow[(size_t)prob * kMaxRank + r] = ql[r];
+  __syncthreads();
+  if (tid < R) {
+    const float sc_h = __ldg(p.a.scale + h);
+    float acc = 0.f;
+#pragma unroll 16
+    for (int d = 0; d < D; ++d) acc = mac(acc, qf[d], stage[d * R + tid]);
+    ql[tid] = __fmul_rn(acc, sc_h);
+  }
+  __syncthreads();
+  query_lut<true>(R, S2, C, cbs, lo, ql, lut);
+  if (part == 0 && tid == 0) stamp(p, prob, 9);
+  if (part == 0) {
+    float* gl = p.ws_lut + (size_t)prob * kMaxLut;
+    for (int e = tid; e < SC; e += blockDim.x) gl[e] = lut[e];
+    for (int r = tid; r < R; r += blockDim.x) p.ws_qlow[(size_t)prob * kMaxRank + r] = ql[r];
+    if (tid == 0) {
+      p.ws_ctrl[(size_t)prob * CTRL_WORDS + CTRL_NCAND] = 0u;
+      p.ws_ctrl[(size_t)prob * CTRL_WORDS + CTRL_MAXKEY] = 0u;
+    }
+  }
   const bool rep = S > 0 && p.prep_rep;
   if (rep) {
     for (int e0 = warp * 32; e0 < SC; e0 += blockDim.x) {
@@ -543,19 +596,18 @@ __global__ void __launch_bounds__(kThreads) decode_prep_kernel(const DecodeParam
       }
     }
   }
-  uint32_t* skeys = reinterpret_cast<uint32_t*>(dyn);  // kSample keys; the stage is no longer needed
   if constexpr (S > 0) asm volatile("cp.async.wait_all;\n" ::: "memory");
   __syncthreads();
   int nv = 0;
-  uint32_t top[4] = {0u, 0u, 0u, 0u};
+  float smin = INFINITY, smax = -INFINITY;
   const float* rep_lane = lut_rep + lane;
-#pragma unroll 1
-  for (int u = 0; u < kGroups; ++u) {
-    const int g = tid + u * kThreads;
-    const int64_t g0 = sample_group_start(len_t, u);
+#pragma unroll
+  for (int u = 0; u < kPrepGroups; ++u) {
+    const int gl = tid + u * kThreads;
+    const int64_t g0 = sample_group_start(len_t, g_first + gl);
     uint32_t k4[4];
     if (S > 0 && g0 + 3 < len_t) {
-      const Codes4<(S > 0 ? S : 1)> c = load_codes4_shared<(S > 0 ? S : 1)>(sample, g * 4);
+      const Codes4<(S > 0 ? S : 1)> c = load_codes4_shared<(S > 0 ? S : 1)>(sample, gl * 4);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float sum = rep ? adc_rep_rt<(S > 0 ? S : 1)>(c, j, rep_lane, C)
@@ -566,32 +618,74 @@ __global__ void __launch_bounds__(kThreads) decode_prep_kernel(const DecodeParam
 #pragma unroll
       for (int j = 0; j < 4; ++j) k4[j] = adc_key(p, codes, lut, t, g0 + j, len_t);
     }
-    *reinterpret_cast<uint4*>(skeys + 4 * g) = make_uint4(k4[0], k4[1], k4[2], k4[3]);
+    *reinterpret_cast<uint4*>(skeys + 4 * gl) = make_uint4(k4[0], k4[1], k4[2], k4[3]);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      top4_insert(top, k4[j]);
-      nv += k4[j] != 0u;
+      if (k4[j] != 0u) {
+        const float sc = key_to_float(k4[j]);
+        smin = fminf(smin, sc);
+        smax = fmaxf(smax, sc);
+        ++nv;
+      }
     }
   }
-  *reinterpret_cast<uint4*>(tops + 4 * tid) = make_uint4(top[0], top[1], top[2], top[3]);
-  if (tid == 0) stamp(p, prob, 10);
-  const int n_s = block_sum_int(nv, scratch);  // ends with a barrier: skeys and tops are complete
-  if (tid == 0) stamp(p, prob, 11);
+  if (part == 0 && tid == 0) stamp(p, prob, 10);
+  // block totals of (count, min, max) in one barrier
+  nv = __reduce_add_sync(0xFFFFFFFFu, nv);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    smin = fminf(smin, __shfl_xor_sync(0xFFFFFFFFu, smin, o));
+    smax = fmaxf(smax, __shfl_xor_sync(0xFFFFFFFFu, smax, o));
+  }
+  if (lane == 0) {
+    sel.warp_tot[1][warp] = nv;
+    sel.lo_part[warp] = __float_as_uint(smin);
+    sel.hi_part[warp] = __float_as_uint(smax);
+  }
+  for (int b = tid; b < kSelectBins; b += blockDim.x) sel.hist[0][b] = 0u;
+  __syncthreads();
+  {
+    const int nw = blockDim.x >> 5;
+    int c = lane < nw ? sel.warp_tot[1][lane] : 0;
+    float a = lane < nw ? __uint_as_float(static_cast<uint32_t>(sel.lo_part[lane])) : INFINITY;
+    float b = lane < nw ? __uint_as_float(static_cast<uint32_t>(sel.hi_part[lane])) : -INFINITY;
+    c = __reduce_add_sync(0xFFFFFFFFu, c);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      a = fminf(a, __shfl_xor_sync(0xFFFFFFFFu, a, o));
+      b = fmaxf(b, __shfl_xor_sync(0xFFFFFFFFu, b, o));
+    }
+    nv = c;
+    smin = a;
+    smax = b;
+  }
+  const int n_s = nv;
   const int64_t k_est = imin64(p.sl_cap, len_t);
-  const int64_t r = (2 * k_est * n_s + len_t - 1) / (len_t > 0 ? len_t : 1) + 8;
+  const int64_t r = len_t > 0 ? (2 * k_est * n_s + len_t - 1) / len_t : 0;
   uint32_t t0 = 1u;
-  if (n_s > 0 && r < n_s) {
-    const bool small = r <= 4 * kThreads;
-    const uint32_t* items = small ? tops : skeys;
-    auto item = [&](int i) -> unsigned long long { return static_cast<unsigned long long>(items[i]); };
-    const SelectThreshold thr = cta_radix_select(item, small ? 4 * kThreads : kSample, static_cast<int>(r), &sel);
-    t0 = static_cast<uint32_t>(thr.prefix);
+  const float span = smax - smin;
+  if (n_s > 0 && r >= 1 && r < n_s && isfinite(span)) {
+    if (!(span > 0.f)) {
+      t0 = ordered_key(smin);
+    } else {
+      const float scale = (static_cast<float>(kSelectBins) - 0.5f) / span;
+      uint32_t* hist = sel.hist[0];
+      for (int i = tid; i < 4 * kThreads * kPrepGroups; i += blockDim.x) {
+        const uint32_t kk = skeys[i];
+        if (kk != 0u) {
+          const float x = __fmul_rn(__fsub_rn(key_to_float(kk), smin), scale);
+          atomicAdd(&hist[x > 0.f ? static_cast<int>(fminf(x, static_cast<float>(kSelectBins - 1))) : 0], 1u);
+        }
+      }
+      __syncthreads();
+      (void)select_find_bin(hist, static_cast<int>(r), &sel, 0);
+      const int bstar = sel.digit[0];
+      t0 = ordered_key(bstar >= 1 ? __fadd_rn(smin, __fdiv_rn(static_cast<float>(bstar - 1), scale)) : smin);
+    }
   }
   if (tid == 0) {
-    uint32_t* ctrl = p.ws_ctrl + (size_t)prob * CTRL_WORDS;
-    ctrl[CTRL_NCAND] = 0u;
-    ctrl[CTRL_T0] = t0 > 1u ? t0 : 1u;
-    stamp(p, prob, 1);
+    p.ws_ctrl[(size_t)prob * CTRL_WORDS + CTRL_T0 + part] = t0 > 1u ? t0 : 1u;
+    if (part == 0) stamp(p, prob, 1);
   }
 }
 
@@ -656,20 +750,21 @@ __device__ __forceinline__ float adc_rep(const Codes4<S>& c, int j, uint32_t lan
 // (about 2x the shortlist among all keys), so each one takes a shared atomic of its own and the
 // CTA publishes its list with one global atomic.
 template <int S, int C, bool POW2>
-__global__ void __launch_bounds__(kScanThreads, 4) decode_scan_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(kScanThreads, 2) decode_scan_kernel(const DecodeParams p) {
   constexpr bool kRep = (S > 0) && (C > 0) && (S * C <= kRepEntries);
   constexpr int kInFlight = S == 8 ? 2 : kGroupsInFlight;  // 4-key groups loaded ahead per thread
   __shared__ float lut[kRep ? kRepEntries * 32 : kMaxLut];
   __shared__ uint2 local[kScanLocalCands];  // this CTA's candidates, flushed with one atomic
   __shared__ uint32_t n_local;
   __shared__ uint32_t flush_base;
+  __shared__ uint32_t max_key;
   const int prob = blockIdx.y, seg = blockIdx.x;
   const int h = prob / p.a.n_queries, t = prob - h * p.a.n_queries;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   pdl_launch_dependents();
   pdl_wait();  // prep's LUT, q_low and threshold
   uint32_t* ctrl = p.ws_ctrl + (size_t)prob * CTRL_WORDS;
-  const uint32_t t0 = __ldcg(ctrl + CTRL_T0);
+  const uint32_t t0 = read_t0(ctrl);
   const int SC = p.a.subspaces * p.a.codewords;
   const float* glut = p.ws_lut + (size_t)prob * kMaxLut;
   const int64_t len_t = allowed_length(p, t);
@@ -690,11 +785,16 @@ __global__ void __launch_bounds__(kScanThreads, 4) decode_scan_kernel(const Deco
   } else {
     for (int e = tid; e < SC; e += blockDim.x) lut[e] = __ldcg(glut + e);
   }
-  if (tid == 0) n_local = 0u;
+  if (tid == 0) {
+    n_local = 0u;
+    max_key = 0u;
+  }
   __syncthreads();
   const uint8_t* codes = p.a.codes + h * p.a.codes_head_stride;
   uint2* cand = p.ws_cand + (size_t)prob * p.a.key_len;
+  uint32_t my_max = 0u;  // largest key this thread took
   auto take = [&](uint32_t key, int64_t i) {
+    my_max = max(my_max, key);
     const uint32_t pos = atomicAdd(&n_local, 1u);
     if (pos < static_cast<uint32_t>(kScanLocalCands)) {
       local[pos] = make_uint2(key, static_cast<uint32_t>(i));
@@ -752,9 +852,12 @@ __global__ void __launch_bounds__(kScanThreads, 4) decode_scan_kernel(const Deco
       if (key != 0u && key >= t0) take(key, i);
     });
   }
+  my_max = __reduce_max_sync(0xFFFFFFFFu, my_max);
+  if (lane == 0 && my_max != 0u) atomicMax(&max_key, my_max);
   __syncthreads();
   const uint32_t nl = min(n_local, static_cast<uint32_t>(kScanLocalCands));
   if (tid == 0 && nl > 0) flush_base = atomicAdd(ctrl + CTRL_NCAND, nl);
+  if (tid == 0 && max_key != 0u) atomicMax(ctrl + CTRL_MAXKEY, max_key);
   __syncthreads();
   for (uint32_t e = tid; e < nl; e += blockDim.x) {
     const uint32_t g = flush_base + e;
@@ -762,19 +865,56 @@ __global__ void __launch_bounds__(kScanThreads, 4) decode_scan_kernel(const Deco
   }
 }
 
+// Shortlist select over candidates streamed from L2 (more than fit in shared memory).  Writes
+// out_idx[pos] = candidate position; returns the count.
+static __device__ __forceinline__ int shortlist_from_l2(const uint2* gc, int n_cand, int k, float lo, float hi,
+                                                       SelectScratch* sc, int* scratch, int32_t* out_idx) {
+  auto item = [&](int i) -> unsigned long long {
+    const uint2 v = __ldcg(gc + i);
+    return composite(v.x, v.y);
+  };
+  const SelectThreshold thr =
+      cta_select_linear(item, n_cand, k, lo, hi, sc, [&]() { return cta_radix_select(item, n_cand, k, sc); });
+  return cta_compact(item, n_cand, thr, [&](int pos, int i, unsigned long long) { out_idx[pos] = i; }, scratch);
+}
+
+// Shortlist select over every allowed key (the sampled threshold was above the k-th best key).
+// Writes out_idx[pos] = key index and, when out_c is set, out_c[pos] = its composite.
+static __device__ __forceinline__ int shortlist_from_all(const DecodeParams& p, int prob, int h, int t, int64_t len_t,
+                                                        int k, float* lut, SelectScratch* sc, int* scratch,
+                                                        int32_t* out_idx, unsigned long long* out_c) {
+  for (int e = threadIdx.x; e < p.a.subspaces * p.a.codewords; e += blockDim.x)
+    lut[e] = __ldcg(p.ws_lut + (size_t)prob * kMaxLut + e);
+  __syncthreads();
+  const uint8_t* codes = p.a.codes + h * p.a.codes_head_stride;
+  auto item = [&](int i) -> unsigned long long {
+    const uint32_t key = adc_key(p, codes, lut, t, i, len_t);
+    return key ? composite(key, static_cast<uint32_t>(i)) : 0ull;
+  };
+  const SelectThreshold thr = cta_radix_select(item, static_cast<int>(len_t), k, sc);
+  return cta_compact(item, static_cast<int>(len_t), thr,
+                     [&](int pos, int i, unsigned long long c) {
+                       out_idx[pos] = i;
+                       if (out_c) out_c[pos] = c;
+                     },
+                     scratch);
+}
+
 // The exact shortlist of problem `prob` from the scan's candidates (CTA-cooperative):
 // k = min(shortlist, allowed keys) keys by (coarse key desc, key index asc).  The candidates are
 // selected in shared memory when they fit (`cand`, kCandSmem entries), else streamed from L2; if
 // fewer than k keys reached the threshold the select runs exactly over every allowed key (using
-// `lut`) and a fallback is counted.  emit(pos, key32, idx) is called once per selected key with
-// consecutive positions; returns the number selected.
-template <class Emit>
-__device__ int select_shortlist(const DecodeParams& p, int prob, int h, int t, int64_t len_t, uint2* cand, float* lut,
-                                SelectScratch* sc, int* scratch, const Emit& emit) {
+// `lut`) and a fallback is counted when count_fallback is set.  Writes the selected keys'
+// indices to out_idx[0, n) (and their composites to out_c when it is set) in a deterministic
+// order; returns n.  Ends with a barrier.
+static __device__ __forceinline__ int select_shortlist(const DecodeParams& p, int prob, int h, int t, int64_t len_t,
+                                                      uint2* cand, float* lut, SelectScratch* sc, int* scratch,
+                                                      int32_t* out_idx, unsigned long long* out_c,
+                                                      bool count_fallback) {
   const int tid = threadIdx.x;
   const int64_t L = p.a.key_len;
   const uint32_t* ctrl = p.ws_ctrl + (size_t)prob * CTRL_WORDS;
-  const uint32_t t0 = __ldcg(ctrl + CTRL_T0);
+  const uint32_t t0 = read_t0(ctrl);
   const int64_t n_cand64 = __ldcg(ctrl + CTRL_NCAND);
   const int n_cand = static_cast<int>(n_cand64 < L ? n_cand64 : L);
   int64_t n_allowed = n_cand;
@@ -789,56 +929,51 @@ __device__ int select_shortlist(const DecodeParams& p, int prob, int h, int t, i
   }
   const int k = static_cast<int>(imin64(p.sl_cap, n_allowed));
   const uint2* gc = p.ws_cand + (size_t)prob * L;
+  // every candidate key lies in [T0, the scan's largest candidate key]
+  const uint32_t kmax = __ldcg(ctrl + CTRL_MAXKEY);
+  const float lo = t0 > 1u ? key_to_float(t0) : -INFINITY;
+  const float hi = kmax != 0u ? key_to_float(kmax) : INFINITY;
   int n_sl = 0;
   if (n_cand >= k) {
     if (n_cand <= kCandSmem) {
       unsigned long long* c64 = reinterpret_cast<unsigned long long*>(cand);
       copy_batched(c64, gc, n_cand);
       if (tid == 0) stamp(p, prob, 12);
-      const U64Items item{c64};
-      const SelectThreshold thr = cta_radix_select(item, n_cand, k, sc);
-      n_sl = cta_compact(item, n_cand, thr,
-                         [&](int pos, int, unsigned long long c) {
-                           emit(pos, static_cast<uint32_t>(c >> 32), ~static_cast<uint32_t>(c));
-                         },
-                         scratch);
+      const SelectThreshold thr = select_u64(c64, n_cand, k, lo, hi, sc);
+      n_sl = compact_u64(c64, n_cand, thr, out_idx, scratch);
+      for (int pos = tid; pos < n_sl; pos += blockDim.x) {
+        const unsigned long long c = c64[out_idx[pos]];
+        out_idx[pos] = static_cast<int32_t>(~static_cast<uint32_t>(c));
+        if (out_c) out_c[pos] = c;
+      }
     } else {
-      auto item = [&](int i) -> unsigned long long {
-        const uint2 v = __ldcg(gc + i);
-        return composite(v.x, v.y);
-      };
-      const SelectThreshold thr = cta_radix_select(item, n_cand, k, sc);
-      n_sl = cta_compact(item, n_cand, thr,
-                         [&](int pos, int, unsigned long long c) {
-                           emit(pos, static_cast<uint32_t>(c >> 32), ~static_cast<uint32_t>(c));
-                         },
-                         scratch);
+      n_sl = shortlist_from_l2(gc, n_cand, k, lo, hi, sc, scratch, out_idx);
+      for (int pos = tid; pos < n_sl; pos += blockDim.x) {
+        const uint2 v = __ldcg(gc + out_idx[pos]);
+        out_idx[pos] = static_cast<int32_t>(v.y);
+        if (out_c) out_c[pos] = composite(v.x, v.y);
+      }
     }
   } else {
-    // the sampled threshold was above the k-th best key: exact select over every key
-    for (int e = tid; e < p.a.subspaces * p.a.codewords; e += blockDim.x)
-      lut[e] = __ldcg(p.ws_lut + (size_t)prob * kMaxLut + e);
-    __syncthreads();
-    const uint8_t* codes = p.a.codes + h * p.a.codes_head_stride;
-    auto item = [&](int i) -> unsigned long long {
-      const uint32_t key = adc_key(p, codes, lut, t, i, len_t);
-      return key ? composite(key, static_cast<uint32_t>(i)) : 0ull;
-    };
-    const SelectThreshold thr = cta_radix_select(item, static_cast<int>(len_t), k, sc);
-    n_sl = cta_compact(item, static_cast<int>(len_t), thr,
-                       [&](int pos, int i, unsigned long long c) {
-                         emit(pos, static_cast<uint32_t>(c >> 32), static_cast<uint32_t>(i));
-                       },
-                       scratch);
-    if (p.a.stats && tid == 0) atomicAdd(p.a.stats + SVA_STAT_SELECT_FALLBACKS, 1ull);
+    n_sl = shortlist_from_all(p, prob, h, t, len_t, k, lut, sc, scratch, out_idx, out_c);
+    if (count_fallback && p.a.stats && tid == 0) atomicAdd(p.a.stats + SVA_STAT_SELECT_FALLBACKS, 1ull);
   }
+  __syncthreads();
   return n_sl;
 }
 
 struct FinishSmem {
-  int qf, ql, lut, sc, scratch, misc, sl, rk, fin, fpos, lg, acc, parts, own, orow, olg, kv, cand, total;
+  int qf, ql, lut, sc, scratch, misc, sl, rk, fin, lg, acc, parts, wt, orow, olg, fmark, kv, cand, total;
   int kv_rows;  // rows of each of the staged K and V slices (0: no staging)
 };
+
+// Entries of the finish kernel's candidate area: the shortlist select's candidates, later the
+// budget select's composites followed by the shortlist logits (12 bytes per shortlist key).
+__host__ __device__ inline int finish_cand_entries(int sl_cap, int dbg_cap) {
+  const int need = (3 * sl_cap + 1) / 2;
+  const int e = kCandSmem > dbg_cap ? kCandSmem : dbg_cap;
+  return e > need ? e : need;
+}
 
 // stage_row_bytes: bytes of one staged K (and one V) row, 0 for no staging.
 __host__ __device__ inline FinishSmem finish_smem_layout(int head_dim, int sl_cap, int b_cap, int cand_entries,
@@ -855,13 +990,13 @@ __host__ __device__ inline FinishSmem finish_smem_layout(int head_dim, int sl_ca
   s.sl = o;      o = align16(o + 4 * sl_cap);
   s.rk = o;      o = align16(o + 4 * sl_cap);
   s.fin = o;     o = align16(o + 4 * b_cap);
-  s.fpos = o;    o = align16(o + 4 * b_cap);
   s.lg = o;      o = align16(o + 4 * b_cap);
   s.acc = o;     o = align16(o + 8 * ((kThreads / 32) * 64 + kMaxHeadDim));
   s.parts = o;   o = align16(o + 8 * kCluster * head_dim);
-  s.own = o;     o = align16(o + 4 * chunk);
+  s.wt = o;      o = align16(o + 4 * chunk);
   s.orow = o;    o = align16(o + 4 * chunk);
   s.olg = o;     o = align16(o + 4 * chunk);
+  s.fmark = o;   o = align16(o + chunk);
   s.kv_rows = stage_row_bytes > 0 ? chunk : 0;
   s.kv = o;      o = align16(o + 2 * s.kv_rows * stage_row_bytes);
   s.cand = o;    o = align16(o + 8 * cand_entries);
@@ -876,6 +1011,21 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
                : "memory");
 }
 
+// Split cluster barrier: arrive (release this CTA's shared-memory writes) without waiting, and
+// the matching wait.  Every thread of every CTA of the cluster executes both, in this order.
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory"); }
+
+// finish: one cluster of kCluster CTAs per problem.
+//   1. every CTA selects the exact shortlist from the scan's candidates (the same deterministic
+//      select in each, so no exchange is needed) and takes the slice [j0, j1) of it;
+//   2. each CTA rescores its slice against k_low, stages the slice's K and V rows in its shared
+//      memory (or prefetches them into L2), computes the slice's logits, and writes the rank keys,
+//      the logits and the slice's rank-key range into CTA 0;
+//   3. CTA 0 selects the budget, marks each final key in its owner CTA, and computes the softmax
+//      max and fp64 denominator over the final logits;
+//   4. each CTA forms the rounded weights of its own final keys and their fp64 weighted V sum;
+//   5. CTA 0 adds the kCluster partial sums in CTA order and writes the output.
 template <typename T>
 __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
     decode_finish_kernel(const DecodeParams p, const FinishSmem lay) {
@@ -889,13 +1039,13 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
   int32_t* sl = reinterpret_cast<int32_t*>(smem + lay.sl);
   uint32_t* rk = reinterpret_cast<uint32_t*>(smem + lay.rk);
   int32_t* fin = reinterpret_cast<int32_t*>(smem + lay.fin);
-  int32_t* fpos = reinterpret_cast<int32_t*>(smem + lay.fpos);
   float* lg = reinterpret_cast<float*>(smem + lay.lg);
   double* acc = reinterpret_cast<double*>(smem + lay.acc);
   double* parts = reinterpret_cast<double*>(smem + lay.parts);
-  int32_t* own = reinterpret_cast<int32_t*>(smem + lay.own);
+  float* wt = reinterpret_cast<float*>(smem + lay.wt);
   int32_t* orow = reinterpret_cast<int32_t*>(smem + lay.orow);
   float* olg = reinterpret_cast<float*>(smem + lay.olg);
+  uint8_t* fmark = smem + lay.fmark;
   uint2* cand = reinterpret_cast<uint2*>(smem + lay.cand);
 
   cg::cluster_group cluster = cg::this_cluster();
@@ -904,9 +1054,8 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
   const int h = prob / p.a.n_queries;
   const int t = prob - h * p.a.n_queries;
   const int kvh = h / p.groups;
-  const int64_t L = p.a.key_len;
   const int64_t len_t = allowed_length(p, t);
-  const int D = p.a.head_dim, R = p.a.rank_dim;
+  const int D = p.a.head_dim;
   const int tid = threadIdx.x;
 
   {
@@ -914,169 +1063,174 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
     pdl_launch_dependents();  // a following decode's prep may start prefetching its inputs
     for (int d = tid; d < D; d += blockDim.x) qf[d] = to_f32<T>(q[d]);
     pdl_wait();  // the scan's candidates (and prep's q_low)
-    for (int r = tid; r < R; r += blockDim.x) ql[r] = __ldcg(p.ws_qlow + (size_t)prob * kMaxRank + r);
+    for (int r = tid; r < p.a.rank_dim; r += blockDim.x) ql[r] = __ldcg(p.ws_qlow + (size_t)prob * kMaxRank + r);
+    if (tid == 0) {
+      misc[3] = 0;
+      misc[6] = -1;  // smallest and largest rank key of the shortlist (CTA 0; atomics from all)
+      misc[7] = 0;
+    }
   }
   __syncthreads();
 
-  // ---- phase 1 (CTA 0): the exact shortlist ------------------------------------------------
+  // ---- phase 1 (every CTA): the exact shortlist ---------------------------------------------
   if (crank == 0 && tid == 0) stamp(p, prob, 2);
-  if (crank == 0) {
-    const int n_sl = select_shortlist(p, prob, h, t, len_t, cand, lut, sc, scratch,
-                                      [&](int pos, uint32_t, uint32_t idx) { sl[pos] = static_cast<int32_t>(idx); });
-    if (tid == 0) misc[0] = n_sl;
-  }
+  const int n_sl = select_shortlist(p, prob, h, t, len_t, cand, lut, sc, scratch, sl, nullptr, crank == 0);
   if (crank == 0 && tid == 0) stamp(p, prob, 3);
-  cluster.sync();
+  // CTA 0's candidate area and rank keys are written by the other CTAs below: arrive now, wait
+  // before writing
+  cluster_arrive();
 
-  // ---- phase 2: rescore, split across the cluster -----------------------------------------
-  // CTA c owns shortlist positions [j0, j1).  With staging (p.kv_stage) it also copies the K
-  // and V rows of those keys into its shared memory with asynchronous copies issued before the
-  // rescore's k_low gathers, so all three gathers are in flight together and the logits and
-  // the weighted sum of the final keys it owns read shared memory.  Without staging the rows
-  // are only prefetched into L2.
-  const int32_t* sl0 = cluster.map_shared_rank(sl, 0);
-  uint32_t* rk0 = cluster.map_shared_rank(rk, 0);
-  const int n_sl = *cluster.map_shared_rank(misc, 0);
+  // ---- phase 2: rescore, logits, K/V staging of this CTA's slice ----------------------------
   const int chunk = (n_sl + kCluster - 1) / kCluster;
   const int j0 = min(n_sl, crank * chunk);
   const int j1 = min(n_sl, j0 + chunk);
+  const int nj = j1 - j0;
+  const int32_t* mine = sl + j0;  // key indices of the slice
   const bool staged = p.kv_stage != 0;
   T* kst = reinterpret_cast<T*>(smem + lay.kv);  // [kv_rows][D]
   T* vst = kst + (size_t)lay.kv_rows * D;
-  {
-    for (int j = j0 + tid; j < j1; j += blockDim.x) sl[j - j0] = sl0[j];
-    __syncthreads();
-    const T* kb = reinterpret_cast<const T*>(p.a.keys) + kvh * p.a.k_head_stride;
-    const T* vb = reinterpret_cast<const T*>(p.a.values) + kvh * p.a.v_head_stride;
+  const T* kb = reinterpret_cast<const T*>(p.a.keys) + kvh * p.a.k_head_stride;
+  const T* vb = reinterpret_cast<const T*>(p.a.values) + kvh * p.a.v_head_stride;
+  // the K/V gathers of the slice, issued while the k_low rows of the rescore are in flight
+  auto gather_kv = [&]() {
     if (staged) {
       constexpr int kPer = 16 / static_cast<int>(sizeof(T));  // elements per 16-byte copy
       const int cpr = D / kPer;
-      for (int e = tid; e < (j1 - j0) * cpr; e += blockDim.x) {
-        const int jj = e / cpr, q = e - jj * cpr;
-        const int64_t key = sl[jj];
-        cp_async16(kst + jj * D + q * kPer, kb + key * p.a.k_row_stride + q * kPer);
-        cp_async16(vst + jj * D + q * kPer, vb + key * p.a.v_row_stride + q * kPer);
+      if (blockDim.x % cpr == 0) {
+        const int q = tid % cpr, step = blockDim.x / cpr;
+        for (int jj = tid / cpr; jj < nj; jj += step) {
+          const int64_t key = mine[jj];
+          cp_async16(kst + jj * D + q * kPer, kb + key * p.a.k_row_stride + q * kPer);
+          cp_async16(vst + jj * D + q * kPer, vb + key * p.a.v_row_stride + q * kPer);
+        }
+      } else {
+        for (int e = tid; e < nj * cpr; e += blockDim.x) {
+          const int jj = e / cpr, q = e - jj * cpr;
+          const int64_t key = mine[jj];
+          cp_async16(kst + jj * D + q * kPer, kb + key * p.a.k_row_stride + q * kPer);
+          cp_async16(vst + jj * D + q * kPer, vb + key * p.a.v_row_stride + q * kPer);
+        }
       }
       asm volatile("cp.async.commit_group;\n" ::: "memory");
     } else {
       const int row_bytes = D * static_cast<int>(sizeof(T));
       const int lines = (row_bytes + 127) / 128;
-      for (int e = tid; e < (j1 - j0) * lines; e += blockDim.x) {
+      for (int e = tid; e < nj * lines; e += blockDim.x) {
         const int j = e / lines, o = (e - j * lines) * 128;
-        const int64_t key = sl[j];
+        const int64_t key = mine[j];
         asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(kb + key * p.a.k_row_stride) + o));
         asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(vb + key * p.a.v_row_stride) + o));
       }
     }
-    rescore_rows<8>(p, h, ql, sl, j1 - j0, rk);
-    for (int j = j0 + tid; j < j1; j += blockDim.x) rk0[j] = rk[j - j0];
+  };
+  for (int jj = tid; jj < nj; jj += blockDim.x) fmark[jj] = 0;  // set by CTA 0 in phase 3
+  rescore_rows<8>(p, h, ql, mine, nj, rk, gather_kv);
+  uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
+  for (int jj = tid; jj < nj; jj += blockDim.x) {
+    kmin = min(kmin, rk[jj]);
+    kmax = max(kmax, rk[jj]);
+  }
+  kmin = __reduce_min_sync(0xFFFFFFFFu, kmin);
+  kmax = __reduce_max_sync(0xFFFFFFFFu, kmax);
+  if (staged) {
+    asm volatile("cp.async.wait_all;\n" ::: "memory");
+    __syncthreads();
+    verify_logits<T, true>(kst, 0, D, 0, qf, D, nullptr, nj, p.a.softmax_scale, p.a.logits_mode, olg);
+  } else {
+    verify_logits<T>(p.a.keys, p.a.k_head_stride, p.a.k_row_stride, kvh, qf, D, mine, nj, p.a.softmax_scale,
+                     p.a.logits_mode, olg);
+  }
+  cluster_wait();
+  {
+    uint32_t* rk0 = cluster.map_shared_rank(rk, 0);
+    float* lgs0 = reinterpret_cast<float*>(cluster.map_shared_rank(cand, 0) + n_sl);  // after the composites
+    for (int jj = tid; jj < nj; jj += blockDim.x) {
+      rk0[j0 + jj] = rk[jj];
+      lgs0[j0 + jj] = olg[jj];
+    }
+    if ((tid & 31) == 0 && kmax != 0u) {
+      unsigned* m0 = reinterpret_cast<unsigned*>(cluster.map_shared_rank(misc, 0));
+      atomicMin(m0 + 6, kmin);
+      atomicMax(m0 + 7, kmax);
+    }
   }
   cluster.sync();
   if (crank == 0 && tid == 0) stamp(p, prob, 4);
 
-  // ---- phase 3 (CTA 0): budget select ------------------------------------------------------
+  // ---- phase 3 (CTA 0): budget select, final marks, softmax statistics ----------------------
   if (crank == 0) {
-    // composites in the (now free) candidate area, selected by the same code as the shortlist
     const int b = min(p.b_cap, n_sl);
     unsigned long long* c64 = reinterpret_cast<unsigned long long*>(cand);
+    const float* lgs = reinterpret_cast<const float*>(c64 + n_sl);
     for (int j = tid; j < n_sl; j += blockDim.x) c64[j] = composite(rk[j], static_cast<uint32_t>(sl[j]));
     __syncthreads();
-    const U64Items item{c64};
-    const SelectThreshold thr =
-        cta_radix_select(item, n_sl, b, sc, p.dbg_ts ? p.dbg_ts + (size_t)prob * 16 + 13 : nullptr, 3);
-    const int n_fin = cta_compact(item, n_sl, thr,
-                                  [&](int pos, int j, unsigned long long) {
-                                    fin[pos] = sl[j];
-                                    fpos[pos] = j;
-                                  },
-                                  scratch);
-    if (tid == 0) misc[1] = n_fin;
-  }
-  if (crank == 0 && tid == 0) stamp(p, prob, 5);
-  cluster.sync();
-
-  // ---- phase 4: logits of the final keys ----------------------------------------------------
-  const int32_t* fin0 = cluster.map_shared_rank(fin, 0);
-  const int32_t* fpos0 = cluster.map_shared_rank(fpos, 0);
-  float* lg0 = cluster.map_shared_rank(lg, 0);
-  const int n_fin = *cluster.map_shared_rank(misc + 1, 0);
-  // rows this CTA verifies: staged -> the final keys of its own shortlist slice (own[i] = final
-  // position, orow[i] = staged row); else the slice [f0, f1) of the final list
-  int n_my;
-  int32_t* myrows;
-  if (staged) {
-    if (tid == 0) misc[3] = 0;
-    __syncthreads();
-    for (int q = tid; q < n_fin; q += blockDim.x) {
-      const int j = fpos0[q];
-      if (j >= j0 && j < j1) {
-        const int slot = atomicAdd(misc + 3, 1);
-        own[slot] = q;
-        orow[slot] = j - j0;
-      }
+    const SelectThreshold thr = select_u64(c64, n_sl, b, key_to_float(static_cast<uint32_t>(misc[6])),
+                                           key_to_float(static_cast<uint32_t>(misc[7])), sc);
+    const int n_fin = compact_u64(c64, n_sl, thr, fin, scratch);  // fin[pos] = shortlist position
+    for (int pos = tid; pos < n_fin; pos += blockDim.x) {
+      const int j = fin[pos];
+      fin[pos] = sl[j];
+      lg[pos] = lgs[j];
+      const int owner = j / chunk;
+      cluster.map_shared_rank(fmark, owner)[j - owner * chunk] = 1;
     }
-    asm volatile("cp.async.wait_all;\n" ::: "memory");
-    __syncthreads();
-    n_my = misc[3];
-    myrows = orow;
-    verify_logits<T, true>(kst, 0, D, 0, qf, D, orow, n_my, p.a.softmax_scale, p.a.logits_mode, olg);
-    for (int i = tid; i < n_my; i += blockDim.x) lg0[own[i]] = olg[i];
-  } else {
-    const int fchunk = (n_fin + kCluster - 1) / kCluster;
-    const int f0 = min(n_fin, crank * fchunk);
-    const int f1 = min(n_fin, f0 + fchunk);
-    n_my = f1 - f0;
-    myrows = fin;  // CTA 0 reads its own final list (f0 == 0), the others copy theirs
-    if (crank != 0)
-      for (int j = f0 + tid; j < f1; j += blockDim.x) myrows[j - f0] = fin0[j];
-    __syncthreads();
-    verify_logits<T>(p.a.keys, p.a.k_head_stride, p.a.k_row_stride, kvh, qf, D, myrows, n_my, p.a.softmax_scale,
-                     p.a.logits_mode, olg, p.a.values, p.a.v_head_stride, p.a.v_row_stride);
-    for (int i = tid; i < n_my; i += blockDim.x) lg0[f0 + i] = olg[i];
-  }
-  cluster.sync();
-  if (crank == 0 && tid == 0) stamp(p, prob, 6);
-
-  // ---- phase 5: softmax over all logits (same order in every CTA), weights and partial sums -
-  {
-    float* all = (crank == 0) ? lg : reinterpret_cast<float*>(cand);
-    if (crank != 0)
-      for (int j = tid; j < n_fin; j += blockDim.x) all[j] = lg0[j];
     __syncthreads();
     float mx, denom;
-    softmax_stats(all, n_fin, scratch, acc, &mx, &denom);
-    float* w = reinterpret_cast<float*>(rk);
-    for (int i = tid; i < n_my; i += blockDim.x) w[i] = round_to<T>(expf(olg[i] - mx) / denom);
-    __syncthreads();
-    double* sums = acc + (kThreads / 32) * 64;
-    if (staged)
-      accumulate_rows<T, true>(vst, 0, D, 0, D, myrows, w, n_my, acc, sums);
-    else
-      accumulate_rows<T>(p.a.values, p.a.v_head_stride, p.a.v_row_stride, kvh, D, myrows, w, n_my, acc, sums);
-    double* parts0 = cluster.map_shared_rank(parts, 0);
-    for (int d = tid; d < D; d += blockDim.x) parts0[crank * D + d] = sums[d];
+    softmax_stats(lg, n_fin, scratch, acc, &mx, &denom);
+    if (tid == 0) {
+      misc[1] = n_fin;
+      misc[4] = __float_as_int(mx);
+      misc[5] = __float_as_int(denom);
+    }
   }
   cluster.sync();
-  if (crank == 0 && tid == 0) stamp(p, prob, 7);
+  if (crank == 0 && tid == 0) stamp(p, prob, 5);
 
-  // ---- phase 6 (CTA 0): merge, outputs, counters ------------------------------------------
-  if (crank == 0) {
-    T* out = reinterpret_cast<T*>(p.a.out) + h * p.a.out_head_stride + t * p.a.out_row_stride;
-    for (int d = tid; d < D; d += blockDim.x) {
-      double tot = 0.0;
-      for (int c = 0; c < kCluster; ++c) tot += parts[c * D + d];
-      out[d] = from_f32<T>(n_fin > 0 ? static_cast<float>(tot) : 0.f);
+  // ---- phase 4: weights and the fp64 weighted V sum of this CTA's final keys ----------------
+  {
+    const int* misc0 = cluster.map_shared_rank(misc, 0);
+    const int n_fin = misc0[1];
+    const float mx = __int_as_float(misc0[4]);
+    const float denom = __int_as_float(misc0[5]);
+    for (int jj = tid; jj < nj; jj += blockDim.x) {
+      if (fmark[jj]) {
+        const int slot = atomicAdd(misc + 3, 1);
+        orow[slot] = staged ? jj : mine[jj];
+        wt[slot] = round_to<T>(expf(olg[jj] - mx) / denom);
+      }
     }
-    unsigned long long* tmp = reinterpret_cast<unsigned long long*>(cand);
-    if (p.a.shortlist_out) write_sorted(sl, n_sl, p.a.shortlist, p.a.shortlist_out + (size_t)prob * p.a.shortlist, tmp);
-    if (p.a.final_out) write_sorted(fin, n_fin, p.a.budget, p.a.final_out + (size_t)prob * p.a.budget, tmp);
-    if (p.a.stats && tid == 0) {
-      atomicAdd(p.a.stats + SVA_STAT_QUERIES, 1ull);
-      atomicAdd(p.a.stats + SVA_STAT_SUMMONED, static_cast<unsigned long long>(n_sl));
-      atomicAdd(p.a.stats + SVA_STAT_EXACT_SCORED, static_cast<unsigned long long>(n_fin));
-      atomicAdd(p.a.stats + SVA_STAT_VERIFIED, static_cast<unsigned long long>(n_fin));
+    __syncthreads();
+    const int n_my = misc[3];
+    double* sums = acc + (kThreads / 32) * 64;
+    if (staged)
+      accumulate_rows<T, true>(vst, 0, D, 0, D, orow, wt, n_my, acc, sums);
+    else
+      accumulate_rows<T>(p.a.values, p.a.v_head_stride, p.a.v_row_stride, kvh, D, orow, wt, n_my, acc, sums);
+    double* parts0 = cluster.map_shared_rank(parts, 0);
+    for (int d = tid; d < D; d += blockDim.x) parts0[crank * D + d] = sums[d];
+    if (crank == 0 && tid == 0) stamp(p, prob, 6);
+    cluster.sync();
+    if (crank == 0 && tid == 0) stamp(p, prob, 7);
+
+    // ---- phase 5 (CTA 0): merge, outputs, counters ------------------------------------------
+    if (crank == 0) {
+      T* out = reinterpret_cast<T*>(p.a.out) + h * p.a.out_head_stride + t * p.a.out_row_stride;
+      for (int d = tid; d < D; d += blockDim.x) {
+        double tot = 0.0;
+        for (int c = 0; c < kCluster; ++c) tot += parts[c * D + d];
+        out[d] = from_f32<T>(n_fin > 0 ? static_cast<float>(tot) : 0.f);
+      }
+      unsigned long long* tmp = reinterpret_cast<unsigned long long*>(cand);
+      if (p.a.shortlist_out) write_sorted(sl, n_sl, p.a.shortlist, p.a.shortlist_out + (size_t)prob * p.a.shortlist, tmp);
+      if (p.a.final_out) write_sorted(fin, n_fin, p.a.budget, p.a.final_out + (size_t)prob * p.a.budget, tmp);
+      if (p.a.stats && tid == 0) {
+        atomicAdd(p.a.stats + SVA_STAT_QUERIES, 1ull);
+        atomicAdd(p.a.stats + SVA_STAT_SUMMONED, static_cast<unsigned long long>(n_sl));
+        atomicAdd(p.a.stats + SVA_STAT_EXACT_SCORED, static_cast<unsigned long long>(n_fin));
+        atomicAdd(p.a.stats + SVA_STAT_VERIFIED, static_cast<unsigned long long>(n_fin));
+      }
+      if (tid == 0) stamp(p, prob, 8);
     }
-    if (tid == 0) stamp(p, prob, 8);
   }
 }
 
@@ -1164,8 +1318,8 @@ static int plan_decode(const sva_decode_args* a, DecodePlan* plan, bool force_gr
     p.lay = decode_smem_layout(a->head_dim, p.sl_cap, p.b_cap, cache_bytes);
     plan->smem_bytes = static_cast<size_t>(p.lay.total);
   } else {
-    // the candidate area also holds the budget select's composites (one per shortlist key)
-    const int cand_entries = std::max(std::max(kCandSmem, dbg_cap), p.sl_cap);
+    // the candidate area later holds the budget select's composites and the shortlist logits
+    const int cand_entries = finish_cand_entries(p.sl_cap, dbg_cap);
     const int esz = a->qkv_dtype == SVA_DTYPE_F32 ? 4 : 2;
     const int row_bytes = a->head_dim * esz;
     const bool aligned = (row_bytes % 16 == 0) && ((a->k_row_stride * esz) % 16 == 0) &&
@@ -1199,10 +1353,11 @@ static void launch_scan(const DecodeParams& p, int P, cudaStream_t stream) {
 }
 
 template <typename T, int S>
-static int launch_prep(const DecodeParams& p, int P, int smem, cudaStream_t stream) {
-  int rc = ensure_smem_attr(reinterpret_cast<const void*>(decode_prep_kernel<T, S>), smem);
+static int launch_prep(const DecodeParams& p, int P, const PrepSmem& lay, cudaStream_t stream) {
+  int rc = ensure_smem_attr(reinterpret_cast<const void*>(decode_prep_kernel<T, S>), lay.total);
   if (rc != SVA_OK) return rc;
-  const cudaError_t e = launch_dependent(decode_prep_kernel<T, S>, dim3(P), dim3(kThreads), smem, stream, p);
+  const cudaError_t e =
+      launch_dependent(decode_prep_kernel<T, S>, dim3(P * kPrepCtas), dim3(kThreads), lay.total, stream, p, lay);
   return e == cudaSuccess ? SVA_OK : set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
 }
 
@@ -1220,23 +1375,20 @@ template <typename T>
 static int launch_prep_scan(DecodeParams& p, cudaStream_t stream) {
   const int P = p.a.n_heads * p.a.n_queries;
   int rc;
-  const int prep_base = prep_stage_bytes(p.a.head_dim, p.a.rank_dim);
-  const bool prep_vec = p.vec_codes && prep_base + kSample * p.a.subspaces <= kPrepSmemLimit;
-  int prep_smem = prep_base + (prep_vec ? kSample * p.a.subspaces : 0);
-  const int rep_bytes = p.a.subspaces * p.a.codewords * 32 * 4;
-  p.prep_rep = (prep_vec && p.a.subspaces * p.a.codewords <= kRepEntries &&
-                prep_smem + rep_bytes <= kPrepSmemLimit) ? 1 : 0;
-  if (p.prep_rep) prep_smem += rep_bytes;
-  switch (prep_vec ? p.a.subspaces : 0) {
-    case 1: rc = launch_prep<T, 1>(p, P, prep_smem, stream); break;
-    case 2: rc = launch_prep<T, 2>(p, P, prep_smem, stream); break;
-    case 4: rc = launch_prep<T, 4>(p, P, prep_smem, stream); break;
-    case 8: rc = launch_prep<T, 8>(p, P, prep_smem, stream); break;
-    default: rc = launch_prep<T, 0>(p, P, prep_smem, stream); break;
+  const int D = p.a.head_dim, R = p.a.rank_dim, C = p.a.codewords, S = p.a.subspaces;
+  const bool prep_vec = p.vec_codes && prep_smem_layout(D, R, C, S, false).total <= kPrepSmemLimit;
+  const bool want_rep = prep_vec && S * C <= kRepEntries;
+  p.prep_rep = (want_rep && prep_smem_layout(D, R, C, S, true).total <= kPrepSmemLimit) ? 1 : 0;
+  const PrepSmem lay = prep_smem_layout(D, R, C, prep_vec ? S : 0, p.prep_rep != 0);
+  switch (prep_vec ? S : 0) {
+    case 1: rc = launch_prep<T, 1>(p, P, lay, stream); break;
+    case 2: rc = launch_prep<T, 2>(p, P, lay, stream); break;
+    case 4: rc = launch_prep<T, 4>(p, P, lay, stream); break;
+    case 8: rc = launch_prep<T, 8>(p, P, lay, stream); break;
+    default: rc = launch_prep<T, 0>(p, P, lay, stream); break;
   }
   if (rc != SVA_OK) return rc;
   profile_mark(0, stream);
-  const int C = p.a.codewords;
   switch (p.vec_codes ? p.a.subspaces : 0) {
     case 1:
       if (C == 256) launch_scan<1, 256>(p, P, stream);

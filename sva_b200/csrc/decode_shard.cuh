@@ -42,9 +42,10 @@ __global__ void __launch_bounds__(kThreads)
   const int SL = p.a.shortlist;
   unsigned long long* out = top_out + (size_t)prob * SL;
   const uint32_t off = static_cast<uint32_t>(key_offset);
-  const int n = select_shortlist(p, prob, h, t, len_t, cand, lut, &sc, scratch,
-                                 [&](int pos, uint32_t key, uint32_t idx) { out[pos] = composite(key, idx + off); });
-  for (int j = n + threadIdx.x; j < SL; j += blockDim.x) out[j] = 0ull;
+  int32_t* idx = reinterpret_cast<int32_t*>(smem + kCandSmem * sizeof(uint2));  // SL entries
+  const int n = select_shortlist(p, prob, h, t, len_t, cand, lut, &sc, scratch, idx, out, true);
+  for (int j = threadIdx.x; j < SL; j += blockDim.x)
+    out[j] = j < n ? composite(static_cast<uint32_t>(out[j] >> 32), static_cast<uint32_t>(idx[j]) + off) : 0ull;
 }
 
 // Item functors of the shard kernels (plain structs: lambdas here trip the compiler's front end).
@@ -221,7 +222,7 @@ static int shard_summon(DecodePlan& plan, int64_t key_offset, unsigned long long
   p.dbg_ts = nullptr;
   int rc = launch_prep_scan<T>(p, st);
   if (rc != SVA_OK) return rc;
-  const int smem = kCandSmem * static_cast<int>(sizeof(uint2));
+  const int smem = kCandSmem * static_cast<int>(sizeof(uint2)) + 4 * p.a.shortlist;
   rc = ensure_smem_attr(reinterpret_cast<const void*>(shard_top_kernel), smem);
   if (rc != SVA_OK) return rc;
   shard_top_kernel<<<p.a.n_heads, kThreads, smem, st>>>(p, key_offset, top_out);

@@ -85,6 +85,47 @@ __device__ __forceinline__ float4 load4s(const T* row, int e, int n) {
   return r;
 }
 
+// Vector forms of load4s when row + e is aligned to the four elements and in range.
+template <>
+__device__ __forceinline__ float4 load4s<float>(const float* row, int e, int n) {
+  if (e + 4 <= n && ((reinterpret_cast<uintptr_t>(row + e) & 15u) == 0)) return *reinterpret_cast<const float4*>(row + e);
+  float4 r;
+  r.x = (e + 0 < n) ? row[e + 0] : 0.f;
+  r.y = (e + 1 < n) ? row[e + 1] : 0.f;
+  r.z = (e + 2 < n) ? row[e + 2] : 0.f;
+  r.w = (e + 3 < n) ? row[e + 3] : 0.f;
+  return r;
+}
+template <>
+__device__ __forceinline__ float4 load4s<__nv_bfloat16>(const __nv_bfloat16* row, int e, int n) {
+  if (e + 4 <= n && ((reinterpret_cast<uintptr_t>(row + e) & 7u) == 0)) {
+    const uint2 raw = *reinterpret_cast<const uint2*>(row + e);
+    return make_float4(__uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xFFFF0000u), __uint_as_float(raw.y << 16),
+                       __uint_as_float(raw.y & 0xFFFF0000u));
+  }
+  float4 r;
+  r.x = (e + 0 < n) ? __bfloat162float(row[e + 0]) : 0.f;
+  r.y = (e + 1 < n) ? __bfloat162float(row[e + 1]) : 0.f;
+  r.z = (e + 2 < n) ? __bfloat162float(row[e + 2]) : 0.f;
+  r.w = (e + 3 < n) ? __bfloat162float(row[e + 3]) : 0.f;
+  return r;
+}
+template <>
+__device__ __forceinline__ float4 load4s<__half>(const __half* row, int e, int n) {
+  if (e + 4 <= n && ((reinterpret_cast<uintptr_t>(row + e) & 7u) == 0)) {
+    const uint2 raw = *reinterpret_cast<const uint2*>(row + e);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
+  float4 r;
+  r.x = (e + 0 < n) ? __half2float(row[e + 0]) : 0.f;
+  r.y = (e + 1 < n) ? __half2float(row[e + 1]) : 0.f;
+  r.z = (e + 2 < n) ? __half2float(row[e + 2]) : 0.f;
+  r.w = (e + 3 < n) ? __half2float(row[e + 3]) : 0.f;
+  return r;
+}
+
 // Four consecutive elements starting at e (elements at or beyond n read as 0).
 template <typename T>
 __device__ __forceinline__ float4 load4(const T* __restrict__ row, int e, int n) {

@@ -19,8 +19,9 @@ namespace sva {
 
 constexpr int kVerifyUnroll = 8;
 
-// `values` (optional): the V rows of the same keys are prefetched into L2 while the K rows load,
-// so that the weighted sum that follows reads them from L2.
+// `rows` are key indices; NULL means rows 0..n-1.  `values` (optional): the V rows of the same
+// keys are prefetched into L2 while the K rows load, so that the weighted sum that follows reads
+// them from L2.
 // kShared: the rows live in shared memory (staged copies), read with plain loads.
 template <typename T, bool kShared = false>
 __device__ void verify_logits(const void* keys, int64_t k_head_stride, int64_t k_row_stride, int kvh, const float* qf,
@@ -42,7 +43,7 @@ __device__ void verify_logits(const void* keys, int64_t k_head_stride, int64_t k
       for (int u = 0; u < U; ++u) {
         const int j = base + 2 * u + half;
         if (j < n && e < D) {
-          const T* kr = kb + (int64_t)rows[j] * k_row_stride;
+          const T* kr = kb + (int64_t)(rows ? rows[j] : j) * k_row_stride;
           k4[u] = kShared ? load4s<T>(kr, e, D) : load4<T>(kr, e, D);
         } else {
           k4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
