@@ -28,6 +28,8 @@
 // (reference sva/llama.py:286-292).
 #include <cooperative_groups.h>
 
+#include <type_traits>
+
 #include "cta_select.cuh"
 #include "qlut.cuh"
 #include "sva_internal.h"
@@ -721,7 +723,9 @@ __device__ __forceinline__ float lds_f32(uint32_t addr) {
   return v;
 }
 
-template <int S, int C, int s>
+// kOr: the table's shared address has no bit in common with the code field or 4 * lane, so the
+// offset is one and-or of the shifted word (else an and, then an add).
+template <int S, int C, int s, bool kOr>
 __device__ __forceinline__ float adc_rep_from(const Codes4<S>& c, int j, uint32_t lane_base, float sum) {
   if constexpr (s == S) {
     return sum;
@@ -731,16 +735,17 @@ __device__ __forceinline__ float adc_rep_from(const Codes4<S>& c, int j, uint32_
     int byte;
     code_pos<S>(c, j, s, w, byte);
     const int sh = 8 * byte - 7;  // compile-time after unrolling
-    const uint32_t off = ((sh >= 0 ? (w >> sh) : (w << -sh)) & kMask) + lane_base;
+    const uint32_t x = sh >= 0 ? (w >> sh) : (w << -sh);
+    const uint32_t off = kOr ? ((x & kMask) | lane_base) : ((x & kMask) + lane_base);
     const float v = lds_f32<s * C * 128>(off);
-    return adc_rep_from<S, C, s + 1>(c, j, lane_base, s == 0 ? v : __fadd_rn(sum, v));
+    return adc_rep_from<S, C, s + 1, kOr>(c, j, lane_base, s == 0 ? v : __fadd_rn(sum, v));
   }
 }
 
 // lane_base = shared address of the replicated table + 4 * lane.
-template <int S, int C>
+template <int S, int C, bool kOr = false>
 __device__ __forceinline__ float adc_rep(const Codes4<S>& c, int j, uint32_t lane_base) {
-  return adc_rep_from<S, C, 0>(c, j, lane_base, 0.f);
+  return adc_rep_from<S, C, 0, kOr>(c, j, lane_base, 0.f);
 }
 
 // scan: the single pass over the codes; keys >= T0 become candidates.  One CTA scans
@@ -753,7 +758,9 @@ template <int S, int C, bool POW2>
 __global__ void __launch_bounds__(kScanThreads, 2) decode_scan_kernel(const DecodeParams p) {
   constexpr bool kRep = (S > 0) && (C > 0) && (S * C <= kRepEntries);
   constexpr int kInFlight = S == 8 ? 2 : kGroupsInFlight;  // 4-key groups loaded ahead per thread
-  __shared__ float lut[kRep ? kRepEntries * 32 : kMaxLut];
+  // the LUT lives in dynamic shared memory (scan_lut_bytes), its start rounded up at run time to
+  // a multiple of its row field so that lookups can or the lane into the offset
+  extern __shared__ __align__(16) unsigned char scan_dyn[];
   __shared__ uint2 local[kScanLocalCands];  // this CTA's candidates, flushed with one atomic
   __shared__ uint32_t n_local;
   __shared__ uint32_t flush_base;
@@ -761,6 +768,9 @@ __global__ void __launch_bounds__(kScanThreads, 2) decode_scan_kernel(const Deco
   const int prob = blockIdx.y, seg = blockIdx.x;
   const int h = prob / p.a.n_queries, t = prob - h * p.a.n_queries;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr uint32_t kLutAlign = kRep ? static_cast<uint32_t>(C > 0 ? C : 1) * 128u : 16u;
+  const uint32_t dyn_base = static_cast<uint32_t>(__cvta_generic_to_shared(scan_dyn));
+  float* lut = reinterpret_cast<float*>(scan_dyn + ((kLutAlign - (dyn_base & (kLutAlign - 1u))) & (kLutAlign - 1u)));
   pdl_launch_dependents();
   pdl_wait();  // prep's LUT, q_low and threshold
   uint32_t* ctrl = p.ws_ctrl + (size_t)prob * CTRL_WORDS;
@@ -809,7 +819,10 @@ __global__ void __launch_bounds__(kScanThreads, 2) decode_scan_kernel(const Deco
       const float scale = p.inv_sqrt_r;
       const int ngroups = static_cast<int>((i1 - i0) >> 2);
       const uint8_t* cbase = codes + i0 * S;
-      const uint32_t lane_base = static_cast<uint32_t>(__cvta_generic_to_shared(lut)) + static_cast<uint32_t>(lane) * 4u;
+      const uint32_t lut_base = static_cast<uint32_t>(__cvta_generic_to_shared(lut));
+      const uint32_t lane_base = lut_base + static_cast<uint32_t>(lane) * 4u;
+      // the and-or offset needs a table address with no bit in the code field or below it
+      const bool or_ok = kRep && (lut_base & ((static_cast<uint32_t>(C > 0 ? C : 1) << 7) - 1u)) == 0u;
       auto score = [&](const Codes4<S>& c, int j) -> float {
         float sum;
         if constexpr (kRep) sum = adc_rep<S, C>(c, j, lane_base);
@@ -819,23 +832,35 @@ __global__ void __launch_bounds__(kScanThreads, 2) decode_scan_kernel(const Deco
       };
       const int tile = kScanThreads * kInFlight;
       const int nfull = ngroups - ngroups % tile;
-      for (int gb = tid; gb < nfull; gb += tile) {
-        Codes4<S> c[kInFlight];
+      auto main_loop = [&](auto or_tag) {
+        constexpr bool kOr = decltype(or_tag)::value;
+        auto score_fast = [&](const Codes4<S>& c, int j) -> float {
+          float sum;
+          if constexpr (kRep) sum = adc_rep<S, C, kOr>(c, j, lane_base);
+          else sum = adc_plain<S, C>(c, j, lut, p.a.codewords);
+          if constexpr (POW2) return __fmul_rn(sum, scale);
+          else return __fdiv_rn(sum, p.sqrt_r);
+        };
+        for (int gb = tid; gb < nfull; gb += tile) {
+          Codes4<S> c[kInFlight];
 #pragma unroll
-        for (int u = 0; u < kInFlight; ++u) c[u] = load_codes4<S>(cbase, 4 * (gb + u * kScanThreads));
+          for (int u = 0; u < kInFlight; ++u) c[u] = load_codes4<S>(cbase, 4 * (gb + u * kScanThreads));
 #pragma unroll
-        for (int u = 0; u < kInFlight; ++u) {
-          float sc[4];
+          for (int u = 0; u < kInFlight; ++u) {
+            float sc[4];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) sc[j] = score(c[u], j);
-          // one compare per group of four keys; candidates are rare
-          if (fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3])) >= t0f) {
+            for (int j = 0; j < 4; ++j) sc[j] = score_fast(c[u], j);
+            // one compare per group of four keys; candidates are rare
+            if (fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3])) >= t0f) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              if (sc[j] >= t0f) take(ordered_key(sc[j]), i0 + 4 * (gb + u * kScanThreads) + j);
+              for (int j = 0; j < 4; ++j)
+                if (sc[j] >= t0f) take(ordered_key(sc[j]), i0 + 4 * (gb + u * kScanThreads) + j);
+            }
           }
         }
-      }
+      };
+      if (or_ok) main_loop(std::true_type{});
+      else main_loop(std::false_type{});
       for (int g = nfull + tid; g < ngroups; g += kScanThreads) {
         const Codes4<S> c = load_codes4<S>(cbase, 4 * g);
 #pragma unroll
@@ -1346,10 +1371,20 @@ static int plan_decode(const sva_decode_args* a, DecodePlan* plan, bool force_gr
   return SVA_OK;
 }
 
+// Dynamic shared memory of the scan kernel: its LUT plus the slack that aligns it.
 template <int S, int C>
-static void launch_scan(const DecodeParams& p, int P, cudaStream_t stream) {
-  if (p.sqrt_r_pow2) launch_dependent(decode_scan_kernel<S, C, true>, dim3(p.nseg, P), dim3(kScanThreads), 0, stream, p);
-  else launch_dependent(decode_scan_kernel<S, C, false>, dim3(p.nseg, P), dim3(kScanThreads), 0, stream, p);
+constexpr int scan_lut_bytes() {
+  return (S > 0 && C > 0 && S * C <= kRepEntries) ? 4 * kRepEntries * 32 + C * 128 : 4 * kMaxLut;
+}
+
+template <int S, int C>
+static int launch_scan(const DecodeParams& p, int P, cudaStream_t stream) {
+  constexpr int smem = scan_lut_bytes<S, C>();
+  auto k = p.sqrt_r_pow2 ? decode_scan_kernel<S, C, true> : decode_scan_kernel<S, C, false>;
+  const int rc = ensure_smem_attr(reinterpret_cast<const void*>(k), smem);
+  if (rc != SVA_OK) return rc;
+  const cudaError_t e = launch_dependent(k, dim3(p.nseg, P), dim3(kScanThreads), smem, stream, p);
+  return e == cudaSuccess ? SVA_OK : set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
 }
 
 template <typename T, int S>
@@ -1390,24 +1425,13 @@ static int launch_prep_scan(DecodeParams& p, cudaStream_t stream) {
   if (rc != SVA_OK) return rc;
   profile_mark(0, stream);
   switch (p.vec_codes ? p.a.subspaces : 0) {
-    case 1:
-      if (C == 256) launch_scan<1, 256>(p, P, stream);
-      else launch_scan<1, 0>(p, P, stream);
-      break;
-    case 2:
-      if (C == 128) launch_scan<2, 128>(p, P, stream);
-      else launch_scan<2, 0>(p, P, stream);
-      break;
-    case 4:
-      if (C == 64) launch_scan<4, 64>(p, P, stream);
-      else launch_scan<4, 0>(p, P, stream);
-      break;
-    case 8:
-      if (C == 32) launch_scan<8, 32>(p, P, stream);
-      else launch_scan<8, 0>(p, P, stream);
-      break;
-    default: launch_scan<0, 0>(p, P, stream); break;
+    case 1: rc = C == 256 ? launch_scan<1, 256>(p, P, stream) : launch_scan<1, 0>(p, P, stream); break;
+    case 2: rc = C == 128 ? launch_scan<2, 128>(p, P, stream) : launch_scan<2, 0>(p, P, stream); break;
+    case 4: rc = C == 64 ? launch_scan<4, 64>(p, P, stream) : launch_scan<4, 0>(p, P, stream); break;
+    case 8: rc = C == 32 ? launch_scan<8, 32>(p, P, stream) : launch_scan<8, 0>(p, P, stream); break;
+    default: rc = launch_scan<0, 0>(p, P, stream); break;
   }
+  if (rc != SVA_OK) return rc;
   profile_mark(1, stream);
   return SVA_OK;
 }
