@@ -528,7 +528,12 @@ def gpu_arm(args):
                      "frac": round(step_gbs / peak, 4), "peak_kind": peak_kind}
 
     # end to end through the public op with pinned host buffers
-    e2e = e2e_measure(args, sets, one_query, device, group)
+    host_query = None
+    if world == 1:
+        def host_query(st, hq, ho):
+            kernels.decode(hq, st["q_proj"], st["scale"], st["cb"], st["codes"], st["k_low"], st["keys"],
+                           st["values"], args.shortlist, args.budget, softmax_scale=0.125, logits_mode=1, out=ho)
+    e2e = e2e_measure(args, sets, one_query, device, group, host_query)
 
     line = {
         "metric": METRIC, "value": round(us_query, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -568,9 +573,12 @@ def ctypes_voidp_array(vals):
     return arr
 
 
-def e2e_measure(args, sets, one_query, device, group):
-    """Each step: copy the query token of every head from pinned host memory, run the public decode
-    op, read the output back to pinned host memory; time per query on the device clock."""
+def e2e_measure(args, sets, one_query, device, group, host_query=None):
+    """Each step moves the query token of every head from pinned host memory to the GPU, runs the
+    public decode op, and moves the output back to pinned host memory; time per query on the
+    device clock.  With host_query (one GPU), the public op is given the pinned host tensors
+    themselves and its kernels read q from and write out to host memory; otherwise the step
+    copies them with torch around the op."""
     import torch
 
     n = args.e2e_queries
@@ -579,7 +587,10 @@ def e2e_measure(args, sets, one_query, device, group):
     host_out = [torch.empty_like(st["out"], device="cpu").pin_memory() for st in sets]
     for i in range(4):
         st = st_list[i % len(st_list)]
-        one_query(st)
+        if host_query is not None:
+            host_query(st, host_q[i % len(sets)], host_out[i % len(sets)])
+        else:
+            one_query(st)
     torch.cuda.synchronize()
     if group is not None:
         torch.distributed.barrier(group)
@@ -588,9 +599,12 @@ def e2e_measure(args, sets, one_query, device, group):
     for i in range(n):
         st = st_list[i]
         k = i % len(sets)
-        st["q"].copy_(host_q[k], non_blocking=True)
-        one_query(st)
-        host_out[k].copy_(st["out"], non_blocking=True)
+        if host_query is not None:
+            host_query(st, host_q[k], host_out[k])
+        else:
+            st["q"].copy_(host_q[k], non_blocking=True)
+            one_query(st)
+            host_out[k].copy_(st["out"], non_blocking=True)
     e.record()
     torch.cuda.synchronize()
     ms = s.elapsed_time(e)
@@ -602,8 +616,10 @@ def e2e_measure(args, sets, one_query, device, group):
     obytes = sets[0]["out"].numel() * sets[0]["out"].element_size()
     return {"value": round(1000.0 * ms / n, 3), "unit": UNIT, "h2d_bytes_per_step": qbytes,
             "d2h_bytes_per_step": obytes, "queries": n,
-            "path": ("sva_b200.kernels.decode" if group is None else "sva_b200.sharded.ShardedDecoder.decode")
-                    + " (eager ctypes calls per query) with pinned host q/out"}
+            "path": ("sva_b200.kernels.decode (eager calls per query) given pinned host q and out; its kernels "
+                     "read q from and write out to host memory" if host_query is not None else
+                     "sva_b200.sharded.ShardedDecoder.decode (eager calls per query) with torch copies of pinned "
+                     "host q and out around it")}
 
 
 # The JSON line is the only thing bench.py writes to its standard output: file descriptor 1 is

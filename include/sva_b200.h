@@ -62,6 +62,13 @@ const char* sva_last_error(void);
  * external events, so the hook also works inside CUDA-graph capture.  Pass n = 0 to clear. */
 int sva_profile_events(void* const* events, int32_t n);
 
+/* 1 if p is page-locked host memory that device code can read and write at the same address
+ * (cudaHostAlloc / cudaMallocHost memory, mapped in the unified address space), else 0.  No
+ * reference counterpart: sva_decode accepts such buffers for `query` and `out`, so that a host
+ * caller's per-token input and output cross PCIe inside the kernels instead of in separate copy
+ * operations; this is the check a caller makes before passing them. */
+int sva_host_buffer_device_accessible(const void* p);
+
 /* Phase-timestamp hook (no reference counterpart; measurement only).  When set on the calling
  * thread, the million-key schedule of sva_decode writes %globaltimer nanoseconds at its phase
  * boundaries into device_buffer[problem * 16 + slot] (slots 0..9).  Pass NULL to clear. */
@@ -131,7 +138,8 @@ typedef struct sva_decode_args {
   float softmax_scale;
   int64_t key_len;
   /* query side */
-  const void* query; /* [H][T][D] */
+  const void* query; /* [H][T][D]; device memory or page-locked host memory (see
+                       sva_host_buffer_device_accessible) */
   int64_t q_head_stride, q_row_stride;
   const float* q_proj;       /* [H][D][R] */
   const float* scale;        /* [H], clamp(exp(logit_scale), 0.01, 100) */
@@ -152,7 +160,7 @@ typedef struct sva_decode_args {
   const uint8_t* allowed_mask;
   int64_t mask_row_stride;
   /* outputs */
-  void* out; /* [H][T][D] */
+  void* out; /* [H][T][D]; device memory or page-locked host memory */
   int64_t out_head_stride, out_row_stride;
   int32_t* shortlist_out;    /* [H][T][shortlist] ascending key index, -1 padded, or NULL */
   int32_t* final_out;        /* [H][T][budget] ascending key index, -1 padded, or NULL */

@@ -41,6 +41,7 @@ EXPORTED = (
     "sva_last_error",
     "sva_profile_events",
     "sva_debug_timestamps",
+    "sva_host_buffer_device_accessible",
     "sva_catalog_encode",
     "sva_catalog_encode_tc",
     "sva_assign_centroids",
@@ -185,6 +186,7 @@ def load() -> ctypes.CDLL:
         sigs = {
             "sva_profile_events": ([c_vp, c_i32], ctypes.c_int),
             "sva_debug_timestamps": ([c_vp], ctypes.c_int),
+            "sva_host_buffer_device_accessible": ([c_vp], ctypes.c_int),
             "sva_catalog_encode": ([c_vp, c_i32, c_i64, c_i64, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_i32, c_i32,
                                     c_i64, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp], ctypes.c_int),
             "sva_catalog_encode_tc": ([c_vp, c_i32, c_i64, c_i64, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_i32,

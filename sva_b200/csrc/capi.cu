@@ -84,6 +84,16 @@ extern "C" int sva_profile_events(void* const* events, int32_t n) {
   return SVA_OK;
 }
 
+extern "C" int sva_host_buffer_device_accessible(const void* p) {
+  if (!p) return 0;
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return (attr.type == cudaMemoryTypeHost && attr.devicePointer == p) ? 1 : 0;
+}
+
 extern "C" const char* sva_version(void) { return "sva_b200 0.1.0 (sm_100a)"; }
 
 extern "C" const char* sva_last_error(void) { return sva::g_last_error.c_str(); }

@@ -35,6 +35,25 @@ def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+_host_ok: dict[int, bool] = {}
+
+
+def _cuda_or_host(t: torch.Tensor, name: str) -> None:
+    """A CUDA tensor, or a page-locked host tensor that device code can address (checked once
+    per allocation through sva_host_buffer_device_accessible)."""
+    if t.is_cuda:
+        return
+    if t.device.type == "cpu" and t.is_pinned():
+        base = t.untyped_storage().data_ptr()
+        ok = _host_ok.get(base)
+        if ok is None:
+            ok = bool(_lib.load().sva_host_buffer_device_accessible(ctypes.c_void_p(base)))
+            _host_ok[base] = ok
+        if ok:
+            return
+    raise ValueError(f"{name} must be a CUDA tensor or a pinned host tensor that the GPU can address")
+
+
 def _stream(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
@@ -141,9 +160,12 @@ def decode_args(q: torch.Tensor, q_proj: torch.Tensor, scale: torch.Tensor, code
                 lut_override: torch.Tensor | None = None, out: torch.Tensor | None = None,
                 stats: torch.Tensor | None = None) -> tuple[_lib.DecodeArgs, torch.Tensor]:
     """Validated sva_decode_args for the tensors of a decode call, and the output tensor."""
-    for name, t in (("q", q), ("codes", codes), ("k_low", k_low), ("keys", keys), ("values", values)):
+    for name, t in (("codes", codes), ("k_low", k_low), ("keys", keys), ("values", values)):
         _cuda(t, name)
-    dev = q.device
+    dev = codes.device
+    _cuda_or_host(q, "q")
+    if out is not None:
+        _cuda_or_host(out, "out")
     n_heads, n_q, head_dim = q.shape
     n_kv = int(keys.shape[0])
     key_len = int(codes.shape[1])
@@ -194,10 +216,13 @@ def decode(q: torch.Tensor, q_proj: torch.Tensor, scale: torch.Tensor, codebooks
     q [H, T, D]; codes [H, L, S] uint8 (rows contiguous); k_low [H, L, R] fp32 (rows
     contiguous); keys/values [Hkv, L, D].  Returns out [H, T, D] (and the shortlist / final
     index tensors when requested, [H, T, shortlist] / [H, T, budget] int32, ascending, -1 padded).
+    q and out may be pinned host tensors: the kernels then read q from and write out to host
+    memory directly, so a host caller needs no separate copies for them.  A new output is
+    allocated on the device of the catalog.
     """
     a, out = decode_args(q, q_proj, scale, codebooks, codes, k_low, keys, values, shortlist, budget, softmax_scale,
                          logits_mode, allowed_len, allowed_mask, lut_override, out, stats)
-    dev = q.device
+    dev = codes.device
     n_heads, n_q, _ = q.shape
     sl_out = fin_out = None
     if want_shortlist:

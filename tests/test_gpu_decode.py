@@ -195,3 +195,35 @@ def test_cpu_tensors_are_rejected():
     with pytest.raises(RuntimeError, match="CUDA"):
         kernels.decode(case.q[0], case.q_proj, case.logit_scale, case.codebooks, torch.zeros(9, 8, 2, dtype=torch.uint8),
                        torch.zeros(9, 8, 64), case.keys[0], case.values[0], 4, 2)
+
+
+def _decode_with(case, k_low, codes, q, out=None):
+    from sva_b200 import kernels
+
+    dev = codes.device
+    return kernels.decode(q, case.q_proj.to(dev), kernels.sva_scale(case.logit_scale).to(dev), case.codebooks.to(dev),
+                          codes, k_low, case.keys[0].to(dev), case.values[0].to(dev), case.shortlist, case.budget,
+                          softmax_scale=float(case.q.shape[-1]) ** -0.5, logits_mode=1, out=out)
+
+
+@pytest.mark.parametrize("name", ["cfg1", "cfg2s_4x64"])
+def test_pinned_host_query_and_output(name):
+    """q and out in pinned host memory: the kernels read and write them over PCIe; the output
+    equals the one computed with device buffers bit for bit, on both schedules."""
+    case, _ = cached_case(name)
+    k_low, codes = gpu_catalog(case)
+    out_dev = _decode_with(case, k_low, codes, case.q[0].cuda())
+    q_host = case.q[0].clone().pin_memory()
+    out_host = torch.full(tuple(out_dev.shape), float("nan"), dtype=out_dev.dtype).pin_memory()
+    for _ in range(2):  # two calls in a row on the same host buffers
+        got = _decode_with(case, k_low, codes, q_host, out=out_host)
+        torch.cuda.synchronize()
+        assert got.data_ptr() == out_host.data_ptr()
+        np.testing.assert_array_equal(to_np(out_host), to_np(out_dev))
+
+
+def test_unpinned_host_query_is_rejected():
+    case, _ = cached_case("cfg1")
+    k_low, codes = gpu_catalog(case)
+    with pytest.raises(ValueError, match="pinned host tensor"):
+        _decode_with(case, k_low, codes, case.q[0].clone())
