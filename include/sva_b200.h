@@ -71,7 +71,7 @@ int sva_host_buffer_device_accessible(const void* p);
 
 /* Phase-timestamp hook (no reference counterpart; measurement only).  When set on the calling
  * thread, the million-key schedule of sva_decode writes %globaltimer nanoseconds at its phase
- * boundaries into device_buffer[problem * 16 + slot] (slots 0..9).  Pass NULL to clear. */
+ * boundaries into device_buffer[problem * 16 + slot] (slots 0..15).  Pass NULL to clear. */
 int sva_debug_timestamps(void* device_buffer);
 
 /* ---------------------------------------------------------------------------------------
