@@ -104,6 +104,7 @@ struct DecodeParams {
   int vec_codes;  // codes aligned for 4-key vector loads
   int prep_rep;   // the prep kernel's sample lookups use a bank-replicated LUT
   int kv_stage;   // the finish kernel stages the shortlist's K and V rows in shared memory
+  int q_host;     // the query is in page-locked host memory (not written by the kernels before)
   DecodeSmem lay;
   float* ws_qlow;
   float* ws_lut;
@@ -562,10 +563,15 @@ __global__ void __launch_bounds__(kThreads) decode_prep_kernel(const DecodeParam
   const float* lo = p.a.lut_override ? p.a.lut_override + ((size_t)h * p.a.n_queries + t) * SC : nullptr;
   stage_floats(stage, p.a.q_proj + (size_t)h * D * R, D * R);
   if (!lo) stage_floats(cbs, p.a.codebooks + (size_t)h * C * R, C * R);
-  pdl_wait();
   {
+    // a query in host memory is the caller's input, not a result of the kernels before, so its
+    // PCIe round trip overlaps the wait; a device query may be the previous kernel's output
     const T* q = reinterpret_cast<const T*>(p.a.query) + h * p.a.q_head_stride + t * p.a.q_row_stride;
-    for (int d = tid; d < D; d += blockDim.x) qf[d] = to_f32<T>(q[d]);
+    if (p.q_host)
+      for (int d = tid; d < D; d += blockDim.x) qf[d] = to_f32<T>(q[d]);
+    pdl_wait();
+    if (!p.q_host)
+      for (int d = tid; d < D; d += blockDim.x) qf[d] = to_f32<T>(q[d]);
   }
   __syncthreads();
   if (tid < R) {
@@ -1321,6 +1327,11 @@ static int plan_decode(const sva_decode_args* a, DecodePlan* plan, bool force_gr
   p.sqrt_r_pow2 = pow2_float(static_cast<double>(p.sqrt_r)) ? 1 : 0;
   p.inv_sqrt_r = 1.0f / p.sqrt_r;
   p.sl_cap = static_cast<int>(std::min<int64_t>(a->shortlist, a->key_len));
+  {
+    cudaPointerAttributes attr;
+    if (cudaPointerGetAttributes(&attr, a->query) == cudaSuccess) p.q_host = attr.type == cudaMemoryTypeHost ? 1 : 0;
+    else cudaGetLastError();
+  }
   p.b_cap = std::min(a->budget, p.sl_cap);
   const int S = a->subspaces;
   const bool vec_s = (S == 1 || S == 2 || S == 4 || S == 8);
