@@ -61,6 +61,8 @@ def parse_args():
     ap.add_argument("--throughput-heads", type=int, default=64,
                     help="heads per launch of the throughput-mode measurement (0: skip)")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-inverted", dest="inverted", action="store_false",
+                    help="skip the static inverted-index summon measurement")
     return ap.parse_args()
 
 
@@ -316,6 +318,44 @@ def build_sets(args, device, rank: int, world: int):
     return sets, write, (hi - lo)
 
 
+def inverted_measure(args, sets, device) -> dict:
+    """The static inverted-index summon (reference sva/llama.py:427-576) on the same catalogs: the
+    posting lists of every set are built once (not timed), then decode_inverted runs one query
+    token per head with the serving defaults (8 cells per subspace, budget = min = mid budget),
+    eager calls over the rotating sets, device-timed after 3 warm-ups."""
+    import torch
+
+    from sva_b200 import kernels
+
+    post = [kernels.postings_build(st["codes"], int(st["cb"].shape[2])) for st in sets]
+    outs = [torch.empty(st["q"].shape[0], st["q"].shape[2], dtype=st["q"].dtype, device=device) for st in sets]
+    stats = torch.zeros(8, dtype=torch.int64, device=device)
+    cells = 8
+
+    def one(i, st_stats=None):
+        k = i % len(sets)
+        st = sets[k]
+        kernels.decode_inverted(st["q"][:, 0, :], st["q_proj"], st["scale"], st["cb"], st["codes"], post[k],
+                                st["k_low"], st["keys"], st["values"], args.budget, cells, args.budget, args.budget,
+                                dynamic=False, softmax_scale=0.125, out=outs[k], stats=st_stats)
+
+    for i in range(3):
+        one(i)
+    torch.cuda.synchronize()
+    n = 32
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(n):
+        one(i, stats)
+    e.record()
+    torch.cuda.synchronize()
+    st = stats.cpu().tolist()
+    return {"summon": "inverted_static", "us_per_query": round(1000.0 * s.elapsed_time(e) / n, 2),
+            "cells_per_subspace": cells, "budget": args.budget, "queries": n,
+            "cell_visits_per_query": round(st[5] / n, 1), "verified_per_query": round(st[4] / n, 1),
+            "timing": "eager calls over the rotating catalog sets, device clock"}
+
+
 def throughput_measure(args, device, peak: float) -> dict:
     """Throughput mode (one GPU): many independent (head, query) problems per launch, here
     ``--throughput-heads`` heads of 2^20 keys decoded by one call, so that the per-problem latency
@@ -551,6 +591,8 @@ def gpu_arm(args):
     line["gpu_launches"] = launches_per_query * qps * args.steps
     if world == 1 and args.throughput_heads > 0:
         line["throughput"] = throughput_measure(args, device, peak)
+    if world == 1 and args.inverted:
+        line["inverted_static"] = inverted_measure(args, sets, device)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         times, threads = run_cpu_decoder(args, 1000, 1, args.cpu_seconds)
         cpu_us = 1e6 * sum(times) / len(times)
