@@ -55,3 +55,12 @@ def test_errors_map_to_exceptions_without_a_gpu():
         assert "n_heads" in str(exc)
     else:
         raise AssertionError("expected ValueError")
+
+
+def test_host_buffer_check_rejects_memory_the_gpu_cannot_address():
+    """Pageable host memory and NULL are never reported as device-addressable (on a machine
+    without a GPU every pointer is rejected), so decode never hands the kernels such a pointer."""
+    lib = _lib.load()
+    buf = ctypes.create_string_buffer(256)
+    assert lib.sva_host_buffer_device_accessible(ctypes.cast(buf, ctypes.c_void_p)) == 0
+    assert lib.sva_host_buffer_device_accessible(None) == 0
