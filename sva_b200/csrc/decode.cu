@@ -582,7 +582,14 @@ __global__ void __launch_bounds__(kThreads) decode_prep_kernel(const DecodeParam
     ql[tid] = __fmul_rn(acc, sc_h);
   }
   __syncthreads();
-  query_lut<true>(R, S2, C, cbs, lo, ql, lut);
+  // the LUT's dot products with the subspace width known at compile time for the common widths
+  const int sub = R / S2;
+  const bool fixed = !lo && (reinterpret_cast<uintptr_t>(cbs) & 15u) == 0;
+  if (fixed && sub == 16) query_lut_fixed<16>(S2, C, cbs, ql, lut);
+  else if (fixed && sub == 32) query_lut_fixed<32>(S2, C, cbs, ql, lut);
+  else if (fixed && sub == 64) query_lut_fixed<64>(S2, C, cbs, ql, lut);
+  else if (fixed && sub == 8) query_lut_fixed<8>(S2, C, cbs, ql, lut);
+  else query_lut<true>(R, S2, C, cbs, lo, ql, lut);
   if (part == 0 && tid == 0) stamp(p, prob, 9);
   if (part == 0) {
     float* gl = p.ws_lut + (size_t)prob * kMaxLut;

@@ -78,6 +78,32 @@ __device__ void query_lut(int R, int S, int C, const float* codebooks_h, const f
   __syncthreads();
 }
 
+// query_lut for a compile-time subspace width SUB (a multiple of 4) with the codebook in shared
+// memory: the row is SUB / 4 vector loads and the chain is fully unrolled.  Same order and
+// result as query_lut.  Ends with a barrier.
+template <int SUB>
+__device__ void query_lut_fixed(int S, int C, const float* codebooks_h, const float* ql, float* lut) {
+  const int SC = S * C;
+  for (int e = threadIdx.x; e < SC; e += blockDim.x) {
+    const int s = e / C;
+    const float4* cb = reinterpret_cast<const float4*>(codebooks_h + (size_t)e * SUB);
+    const float* qs = ql + s * SUB;
+    float4 row[SUB / 4];
+#pragma unroll
+    for (int j = 0; j < SUB / 4; ++j) row[j] = cb[j];
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < SUB / 4; ++j) {
+      acc = mac(acc, qs[4 * j + 0], row[j].x);
+      acc = mac(acc, qs[4 * j + 1], row[j].y);
+      acc = mac(acc, qs[4 * j + 2], row[j].z);
+      acc = mac(acc, qs[4 * j + 3], row[j].w);
+    }
+    lut[e] = acc;
+  }
+  __syncthreads();
+}
+
 template <typename T>
 __device__ void build_query_lut(const T* q, int D, int R, int S, int C, const float* q_proj_h, float scale_h,
                                 const float* codebooks_h, const float* lut_override, float* qf, float* ql, float* lut,
