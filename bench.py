@@ -39,7 +39,8 @@ sys.path.insert(0, ROOT)
 
 METRIC = "SVA decode us/query @1M keys (summon+verify)"
 UNIT = "us/query"
-PUBLISHED_US = {"4x64": 1028.0, "1x256": 649.0}  # reference, H100, 9 heads
+# reference, H100, 9 heads: docs/snapshots/compact_summon_frontier_snapshot_2026-05-14.md:41,45
+PUBLISHED_US = {"4x64": 1028.0, "1x256": 649.0}
 
 
 def parse_args():
@@ -63,6 +64,12 @@ def parse_args():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-inverted", dest="inverted", action="store_false",
                     help="skip the static inverted-index summon measurement")
+    ap.add_argument("--no-ragged", dest="ragged", action="store_false",
+                    help="skip the config-5 ragged paged batch measurement")
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg3", "cfg4"],
+                    help="cfg2: million-key decode (default); cfg3 / cfg4: model-level decode tokens/s")
+    ap.add_argument("--model-prefill", type=int, default=None, help="prompt tokens (cfg3: 8192, cfg4: 32768)")
+    ap.add_argument("--model-decode", type=int, default=None, help="decode steps (cfg3: 256, cfg4: 64)")
     return ap.parse_args()
 
 
@@ -406,6 +413,144 @@ def throughput_measure(args, device, peak: float) -> dict:
             "frac": round(gbs / peak, 4), "keys": args.keys, "pq": args.pq}
 
 
+def ragged_paged_set(device, n_seqs: int = 64, page_keys: int = 256, seed: int = 3, heads: int = 9, kv_heads: int = 3,
+                     lo: int = 4096, hi: int = 131072):
+    """n_seqs sequences with cached lengths drawn log-uniform in [lo, hi]
+    (seed 3), 9 query / 3 KV heads, head_dim 64, bf16 K/V ~ N(0,1), 4x64 codes, in page pools of
+    page_keys keys handed out in a shuffled order (page tables [n_seqs, max_pages]).  Pools are
+    head-major ([heads, pages * page_keys, ...]) so that the write path encodes them in one call;
+    the decode sees them through [pages, heads, page_keys, ...] views."""
+    import torch
+
+    from sva_b200 import kernels
+
+    gen = torch.Generator().manual_seed(seed)
+    u = torch.rand(n_seqs, generator=gen, dtype=torch.float64)
+    lengths = torch.exp(math.log(lo) + u * (math.log(hi) - math.log(lo))).floor().long().clamp(lo, hi)
+    pages_per = (lengths + page_keys - 1) // page_keys
+    total_pages = int(pages_per.sum())
+    perm = torch.randperm(total_pages, generator=gen).to(torch.int32)
+    table = torch.zeros(n_seqs, int(pages_per.max()), dtype=torch.int32)
+    k = 0
+    for b in range(n_seqs):
+        n = int(pages_per[b])
+        table[b, :n] = perm[k:k + n]
+        k += n
+    d, r, s, c = 64, 64, 4, 64
+    q = torch.randn(n_seqs, heads, 1, d, generator=gen).to(torch.bfloat16)
+    q_proj = (torch.randn(heads, d, r, generator=gen) * 0.125).to(torch.bfloat16).float()
+    k_proj = (torch.randn(heads, d, r, generator=gen) * 0.125).to(torch.bfloat16).float()
+    cb = torch.randn(heads, s, c, r // s, generator=gen).to(torch.bfloat16).float()
+    rows = total_pages * page_keys
+    dgen = torch.Generator(device=device).manual_seed(seed + 11)
+    keys = torch.randn(kv_heads, rows, d, generator=dgen, device=device).to(torch.bfloat16)
+    values = torch.randn(kv_heads, rows, d, generator=dgen, device=device).to(torch.bfloat16)
+    k_low = torch.empty(heads, rows, r, dtype=torch.float32, device=device)
+    codes = torch.empty(heads, rows, s, dtype=torch.uint8, device=device)
+    q_proj, k_proj, cb = q_proj.to(device), k_proj.to(device), cb.to(device)
+    kernels.catalog_encode(keys, k_proj, cb, 0, rows, k_low, codes)
+
+    def pages_view(t):
+        return t.view(t.shape[0], total_pages, page_keys, t.shape[-1]).permute(1, 0, 2, 3)
+
+    return dict(q=q.to(device), q_proj=q_proj, scale=torch.ones(heads, device=device), cb=cb,
+                codes=pages_view(codes), k_low=pages_view(k_low), keys=pages_view(keys), values=pages_view(values),
+                table=table.to(device), lengths=lengths.tolist(), seq_lens=lengths.to(device),
+                flat=dict(codes=codes, k_low=k_low, keys=keys, values=values), page_keys=page_keys,
+                total_pages=total_pages)
+
+
+def ragged_measure(args, device, peak: float) -> dict:
+    """Config 5 on one GPU: one step decodes one query token of each of the 64 sequences (all 9
+    heads) in a single sva_decode_batched call over the paged catalog; device-timed CUDA-graph
+    replays after 3 warm-ups.  Before timing, two sequences are checked against the
+    single-sequence decode of their own rows (identical shortlists, final sets and outputs)."""
+    import torch
+
+    from sva_b200 import _lib, kernels
+
+    st = ragged_paged_set(device)
+    n_seqs, heads = st["q"].shape[0], st["q"].shape[1]
+    lmax = max(st["lengths"])
+    out = torch.empty(n_seqs, heads, 1, 64, dtype=torch.bfloat16, device=device)
+
+    def call(**kw):
+        return kernels.decode_batched(st["q"], st["q_proj"], st["scale"], st["cb"], st["codes"], st["k_low"],
+                                      st["keys"], st["values"], args.shortlist, args.budget, seq_lens=st["seq_lens"],
+                                      page_table=st["table"], max_len=lmax, softmax_scale=0.125, logits_mode=1,
+                                      **kw)
+
+    # consistency with single-sequence decodes (gathered rows of the sequence's pages)
+    _, sl, fin = call(out=out, want_shortlist=True, want_final=True)
+    torch.cuda.synchronize()
+    parity = "ok"
+    pk = st["page_keys"]
+    for b in (0, n_seqs - 1):
+        n = st["lengths"][b]
+        pages = st["table"][b, : (n + pk - 1) // pk].long()
+        idx = (pages[:, None] * pk + torch.arange(pk, device=device)[None, :]).reshape(-1)[:n]
+        f = st["flat"]
+        o1, s1, f1 = kernels.decode(st["q"][b], st["q_proj"], st["scale"], st["cb"], f["codes"][:, idx].contiguous(),
+                                    f["k_low"][:, idx].contiguous(), f["keys"][:, idx].contiguous(),
+                                    f["values"][:, idx].contiguous(), args.shortlist, args.budget, softmax_scale=0.125,
+                                    logits_mode=1, want_shortlist=True, want_final=True)
+        torch.cuda.synchronize()
+        if not (torch.equal(s1, sl[b]) and torch.equal(f1, fin[b]) and torch.equal(o1, out[b])):
+            parity = f"mismatch in sequence {b}"
+    calls = 8
+    prof = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(4)]
+    for e in prof:
+        e.record()
+    torch.cuda.synchronize()
+    handles = ctypes_voidp_array([e.cuda_event for e in prof[1:]])
+    graph = torch.cuda.CUDAGraph()
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        call(out=out)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(calls):
+                if i == 0:
+                    prof[0].record()
+                    _lib.load().sva_profile_events(handles, 3)
+                try:
+                    call(out=out)
+                finally:
+                    if i == 0:
+                        _lib.load().sva_profile_events(None, 0)
+    torch.cuda.synchronize()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    reps = 5
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    kern = []
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = 1000.0 * e0.elapsed_time(e1) / (reps * calls)
+    graph.replay()
+    torch.cuda.synchronize()
+    kern = [round(1000.0 * prof[j].elapsed_time(prof[j + 1]), 2) for j in range(3)]
+    total_keys = sum(st["lengths"])
+    sl_eff = sum(min(args.shortlist, n) for n in st["lengths"])
+    b_eff = sum(min(args.budget, args.shortlist, n) for n in st["lengths"])
+    nbytes = heads * (total_keys * 4 + sl_eff * 64 * 4 + b_eff * 64 * 2 * 2) + heads * (64 * 64 * 4 + 64 * 64 * 4)
+    gbs = nbytes / (us * 1e-6) / 1e9
+    del graph
+    return {"workload": f"cfg5 ragged paged decode: {n_seqs} sequences, lengths log-uniform in [4096, 131072] "
+                        f"(total {total_keys} keys), 9 query / 3 KV heads, 4x64 codes, {pk}-key pages, "
+                        f"shortlist {args.shortlist}, budget {args.budget}, one token per sequence per step",
+            "us_per_step": round(us, 2), "tokens_per_s": round(n_seqs / (us * 1e-6), 1),
+            "us_per_token": round(us / n_seqs, 3), "algorithmic_bytes_per_step": int(nbytes),
+            "achieved_gbs": round(gbs, 1), "peak_gbs": peak, "frac": round(gbs / peak, 4),
+            "kernel_us_first_call": dict(zip(["prep", "scan", "finish"], kern)), "gpu_launches_per_step": 3,
+            "parity": parity, "total_keys": total_keys, "pages": st["total_pages"],
+            "timing": "CUDA graph of 8 steps, 5 replays after 3 warm-ups, device clock"}
+
+
 def write_path_summary(args, write: dict, local_keys: int, peak: float) -> dict:
     """The catalog write of one set (all heads): keys/s, projection TFLOP/s and the fraction of
     the measured HBM peak its algorithmic bytes reach (K read as bf16, k_low fp32 written, codes)."""
@@ -593,6 +738,8 @@ def gpu_arm(args):
         line["throughput"] = throughput_measure(args, device, peak)
     if world == 1 and args.inverted:
         line["inverted_static"] = inverted_measure(args, sets, device)
+    if world == 1 and args.ragged:
+        line["ragged_paged"] = ragged_measure(args, device, peak)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         times, threads = run_cpu_decoder(args, 1000, 1, args.cpu_seconds)
         cpu_us = 1e6 * sum(times) / len(times)
@@ -605,6 +752,176 @@ def gpu_arm(args):
         del graph
         torch.distributed.barrier(group)
         torch.distributed.destroy_process_group()
+    return 0
+
+
+# ---------------------------------------------------------------------------------------------
+# model-level decode (BASELINE configs 3 and 4): tokens/s through patch_llama_attention
+# ---------------------------------------------------------------------------------------------
+
+def smollm2_model(device, layers: int = 30):
+    """Random-init Llama with the SmolLM2-135M shape (seed 0), bf16, SDPA attention for the
+    unpatched layers."""
+    import torch
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    cfg = LlamaConfig(vocab_size=49152, hidden_size=576, intermediate_size=1536, num_hidden_layers=layers,
+                      num_attention_heads=9, num_key_value_heads=3, head_dim=64, max_position_embeddings=65536,
+                      rope_theta=100000.0, rms_norm_eps=1e-5, tie_word_embeddings=True, attn_implementation="sdpa")
+    torch.manual_seed(0)
+    return LlamaForCausalLM(cfg).eval().to(torch.bfloat16).to(device)
+
+
+def random_bundle(n_layers: int, shortlist: int, budget: int, seed: int = 7):
+    """Frozen random-init 2x256 artifacts for every layer (bf16 values, as real bundles store)."""
+    import torch
+
+    from sva_b200 import SVAArtifactBundle, SVALayerArtifacts
+
+    gen = torch.Generator().manual_seed(seed)
+    layers = {}
+    for i in range(n_layers):
+        layers[i] = SVALayerArtifacts((torch.randn(9, 64, 64, generator=gen) * 0.125).to(torch.bfloat16),
+                                      (torch.randn(9, 64, 64, generator=gen) * 0.125).to(torch.bfloat16),
+                                      torch.zeros(9), torch.randn(9, 2, 256, 32, generator=gen).to(torch.bfloat16),
+                                      0.0, 0.0, "qk")
+    manifest = {"schema_version": 1, "artifact_type": "summon_verify_attention", "rank_dim": 64,
+                "coarse_subspaces": 2, "coarse_codewords": 256, "default_shortlist": shortlist,
+                "default_budget": budget, "layer_count": n_layers, "layers": list(range(n_layers))}
+    return SVAArtifactBundle(manifest=manifest, layers=layers)
+
+
+def passkey_prompt(batch: int, context: int, seed: int = 2, digit_ids=tuple(range(48, 58))):
+    """config 4 prompts: uniform random ids, a random 5-digit string of digit-token ids (ids 48-57
+    stand for the digits of the random-init vocabulary) inserted at a seeded position and repeated
+    at the end; ``context`` tokens in total."""
+    import torch
+
+    gen = torch.Generator().manual_seed(seed)
+    ids = torch.randint(0, 49152, (batch, context), generator=gen)
+    for b in range(batch):
+        digits = torch.tensor([digit_ids[int(d)] for d in torch.randint(0, 10, (5,), generator=gen)])
+        pos = int(torch.randint(0, context - 10, (1,), generator=gen))
+        ids[b, pos:pos + 5] = digits
+        ids[b, -5:] = digits
+    return ids
+
+
+def greedy_decode(model, prompt, steps: int, device):
+    """Prefill the prompt, then `steps` greedy tokens through the model (HF DynamicCache).
+    Returns (prefill_ms, decode_ms, decode_e2e_ms, tokens): decode_ms is the device time of the
+    decode loop; decode_e2e_ms the same loop where every step also moves its tokens device ->
+    pinned host -> device (a host-driven generation loop)."""
+    import torch
+    from transformers import DynamicCache
+
+    def prefill():
+        cache = DynamicCache(config=model.config)
+        out = model(input_ids=prompt.to(device), use_cache=True, past_key_values=cache, logits_to_keep=1)
+        return out.past_key_values, out.logits[:, -1].argmax(-1, keepdim=True)
+
+    with torch.no_grad():
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        cache, tok = prefill()
+        e1.record()
+        torch.cuda.synchronize()
+        prefill_ms = e0.elapsed_time(e1)
+        toks = [tok]
+        e0.record()
+        for _ in range(steps - 1):
+            out = model(input_ids=tok, use_cache=True, past_key_values=cache, logits_to_keep=1)
+            cache = out.past_key_values
+            tok = out.logits[:, -1].argmax(-1, keepdim=True)
+            toks.append(tok)
+        e1.record()
+        torch.cuda.synchronize()
+        decode_ms = e0.elapsed_time(e1)
+        # end to end: the same decode with the token ids crossing to the host and back every step
+        if hasattr(model, "_sva_handle"):
+            model._sva_handle.reset_catalogs()
+        cache, tok = prefill()
+        host = torch.empty_like(tok, device="cpu").pin_memory()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(steps - 1):
+            out = model(input_ids=tok, use_cache=True, past_key_values=cache, logits_to_keep=1)
+            cache = out.past_key_values
+            host.copy_(out.logits[:, -1].argmax(-1, keepdim=True), non_blocking=True)
+            tok = host.to(device, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1)
+    return prefill_ms, decode_ms, e2e_ms, torch.cat(toks, 1)
+
+
+def model_arm(args):
+    """--workload cfg3 / cfg4: decode tokens/s of the patched random-init SmolLM2-shaped model."""
+    import torch
+
+    from sva_b200 import patch_llama_attention
+    from sva_b200.adapter import wrap_socket_layers_with_adapters
+
+    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(device)
+    model = smollm2_model(device)
+    peak, peak_kind = measured_peaks()
+    runs = []
+    if args.workload == "cfg3":
+        gen = torch.Generator().manual_seed(1)
+        prompt = torch.randint(0, 49152, (1, args.model_prefill), generator=gen)
+        settings = [(2048, 512, list(range(30)), False)]
+        steps, batch = args.model_decode, 1
+    else:
+        prompt = passkey_prompt(8, args.model_prefill)
+        settings = [(8192, 2048, [26, 27, 28, 29], True), (512, 128, [26, 27, 28, 29], True)]
+        steps, batch = args.model_decode, 8
+    # the unpatched model (full attention everywhere) for context
+    pf, dm, em, _ = greedy_decode(model, prompt, steps, device)
+    full = {"prefill_ms": round(pf, 1), "decode_ms_per_step": round(dm / (steps - 1), 3),
+            "tokens_per_s": round(batch * (steps - 1) / (dm * 1e-3), 1)}
+    clocks = None
+    for shortlist, budget, layers, adapter in settings:
+        handle = patch_llama_attention(model, random_bundle(30, shortlist, budget), layers=layers,
+                                       allow_batch=batch > 1)
+        model._sva_handle = handle
+        if adapter:
+            wrap_socket_layers_with_adapters(model, layers, rank=16, scale=1.0)
+            gen = torch.Generator().manual_seed(4)
+            with torch.no_grad():
+                for i in layers:
+                    a = model.model.layers[i].self_attn
+                    a.down.weight.copy_(torch.randn(a.down.weight.shape, generator=gen) * 0.02)
+                    a.up.weight.copy_(torch.randn(a.up.weight.shape, generator=gen) * 0.02)
+        sampler = ClockSampler(None)
+        sampler.start()
+        pf, dm, em, toks = greedy_decode(model, prompt, steps, device)
+        clocks = sampler.stop()
+        summary = handle.stats.summary()
+        handle.unpatch()
+        del model._sva_handle
+        n_tok = batch * (steps - 1)
+        runs.append({"shortlist": shortlist, "budget": budget, "patched_layers": len(layers), "adapter": adapter,
+                     "prefill_ms": round(pf, 1), "decode_ms_per_step": round(dm / (steps - 1), 3),
+                     "tokens_per_s": round(n_tok / (dm * 1e-3), 1),
+                     "e2e_tokens_per_s": round(n_tok / (em * 1e-3), 1),
+                     "avg_summoned": summary.get("avg_summoned"), "avg_verified": summary.get("avg_verified")})
+    head = runs[0]
+    line = {
+        "metric": "decode tok/s" + (" @32k" if args.workload == "cfg4" else " @8k"), "value": head["tokens_per_s"],
+        "unit": "tokens/s", "n_gpus": 1, "steps": steps - 1, "warmup": 1,
+        "ms_per_step": head["decode_ms_per_step"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (random-init SmolLM2-135M-shaped model and artifacts, random token ids)",
+        "config": {"workload": (f"cfg3: 30-layer SmolLM2-135M shape, all layers SVA 2x256 (2048/512), prefill "
+                                f"{args.model_prefill}, greedy decode {steps}, batch 1") if args.workload == "cfg3" else
+                   (f"cfg4: late4 socket (layers 26-29 SVA + rank-16 residual adapters), context "
+                    f"{args.model_prefill}, batch 8, greedy decode {steps}; shortlist/budget 8192/2048 and 512/128"),
+                   "path": "HF LlamaForCausalLM patched by sva_b200.patch_llama_attention, eager decode loop"},
+        "e2e": {"value": head["e2e_tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": 8 * batch,
+                "d2h_bytes_per_step": 8 * batch},
+        "runs": runs, "full_attention": full, "clocks": clocks, "gpu_launches": None,
+    }
+    emit(line)
     return 0
 
 
@@ -684,6 +1001,12 @@ def main():
     os.dup2(2, 1)
     if args.impl == "reference":
         return reference_arm(args)
+    if args.workload in ("cfg3", "cfg4"):
+        if args.model_prefill is None:
+            args.model_prefill = 8192 if args.workload == "cfg3" else 32768
+        if args.model_decode is None:
+            args.model_decode = 256 if args.workload == "cfg3" else 64
+        return model_arm(args)
     return gpu_arm(args)
 
 

@@ -13,10 +13,12 @@
  *   sva_assign_centroids    sva/ops.py:10-21 (assign_to_centroids)
  *   sva_pq_scores           sva/ops.py:50-71 (product_quantized_scores)
  *   sva_decode              sva/llama.py:171-328 (SVALlamaAttention.sva_attention, scan summon path)
+ *   sva_decode_batched      sva/llama.py:171-328 over the sequences of a batch (the reference takes batch 1)
  *   sva_postings_build      sva/llama.py:626-657 (_rebuild_postings)
  *   sva_decode_inverted     sva/llama.py:427-576 (_inverted_static_decode_attention) and
  *                           sva/llama.py:330-425 (_inverted_decode_attention)
  *   sva_top_unique          sva/llama.py:83-116 (_top_unique_candidates)
+ *   sva_adapter_forward     experiments/sva_late4_logit_distill.py:37-51 (SVAResidualOutputAdapter) + o_proj
  */
 #ifndef SVA_B200_H_
 #define SVA_B200_H_
@@ -171,6 +173,42 @@ size_t sva_decode_workspace_size(const sva_decode_args* args);
 int sva_decode(const sva_decode_args* args, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------------------
+ * Batched, ragged and paged scan decode: the decode of sva_decode for n_seqs sequences in one
+ * call, each with its own cache length and (optionally) a paged catalog.  The reference decodes
+ * one sequence per call (sva/llama.py:182-183 rejects batch != 1); this replaces a loop of its
+ * sva/llama.py:171-328 over the sequences of a batch.
+ *
+ * Problems are (sequence b, head h, token t).  args describes one sequence as for sva_decode;
+ * args->key_len is the largest sequence length (the workspace is sized for it).  Sequence b:
+ *   keys           seq_lens[b] (NULL: args->key_len for every sequence);
+ *   query / out    args->query + b * q_seq_stride (out_seq_stride), then the head / token strides;
+ *   allowed_len    [n_seqs][T] (NULL: seq_lens[b] - T + t + 1); allowed_mask rows b * T + t;
+ *   shortlist_out / final_out  [n_seqs][H][T][...].
+ * Key l of sequence b, head h (kvh = h / (H / Hkv) for K and V):
+ *   unpaged (page_table == NULL): codes + h * codes_head_stride + b * codes_page_stride + l * S,
+ *     and the same with k_low_page_stride, k_page_stride, v_page_stride (per-sequence strides);
+ *   paged: page = page_table[b * page_table_stride + l / page_keys], row = l % page_keys:
+ *     codes + h * codes_head_stride + page * codes_page_stride + row * S, and the same for k_low
+ *     (row * R), K (row * k_row_stride) and V (row * v_row_stride).
+ * page_keys is a power of two in 64..32768.  Over 32768 keys, n_seqs * H * T <= 65535 per call.
+ * Every problem's shortlist, final set and output equal sva_decode's for that sequence alone.
+ * ------------------------------------------------------------------------------------- */
+typedef struct sva_batch_layout {
+  int32_t n_seqs;
+  int32_t page_keys;
+  const int64_t* seq_lens;    /* [n_seqs] device, or NULL */
+  const int32_t* page_table;  /* [n_seqs][page_table_stride] device, or NULL */
+  int64_t page_table_stride;
+  int64_t q_seq_stride, out_seq_stride;          /* elements */
+  int64_t codes_page_stride, k_low_page_stride;  /* elements per page (paged) or sequence */
+  int64_t k_page_stride, v_page_stride;
+} sva_batch_layout;
+
+size_t sva_decode_batched_workspace_size(const sva_decode_args* args, const sva_batch_layout* layout);
+int sva_decode_batched(const sva_decode_args* args, const sva_batch_layout* layout, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------------
  * Key-range shards: the scan decode of one token per head with the catalog split by key range
  * across ranks, one process per GPU.  Replaces the single-device sva/llama.py:171-328 when the
  * cache does not live on one GPU (the reference itself is single-device).
@@ -229,6 +267,9 @@ int sva_postings_build(const uint8_t* codes, int64_t codes_head_stride, int32_t 
  * streams, or from host threads without ordering between them) race and corrupt each other's
  * lists, so issue them on one stream.  The first call on each device looks up the buffer's
  * address, which may load the library's device module: make it before any stream capture.
+ * The address is kept per device together with the id of the context it belongs to, and looked
+ * up again when a call comes from another context (after cudaDeviceReset, or under a context
+ * the caller created with the driver API); such a first call is also a set-up call.
  * Nothing is claimed about CUDA graph capture of this entry point.
  * ------------------------------------------------------------------------------------- */
 #define SVA_POSTINGS_NOALLOC_SCRATCH_BYTES (8u << 20)
@@ -311,6 +352,21 @@ int sva_decode_inverted(const sva_inverted_args* args, void* workspace, size_t w
 int sva_top_unique(const int64_t* idx, const float* scores, const uint8_t* valid, int32_t rows, int32_t width,
                    int32_t budget, int32_t refill_factor, int64_t* sel_idx, float* sel_scores, uint8_t* sel_valid,
                    int32_t* refill_out, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Residual output adapter fused with o_proj, for decode-sized row counts.  Replaces the late-layer
+ * socket's SVAResidualOutputAdapter.forward (experiments/sva_late4_logit_distill.py:37-51) plus
+ * the wrapped attention's o_proj (sva/llama.py:169):
+ *   o   = attn . o_weight^T (+ o_bias), rounded to dtype     attn [N][in_dim], o_weight [hidden][in_dim]
+ *   c   = up . gelu(down . [float(hidden), float(o)]) * scale  (fp32; down [rank][2 hidden], up [hidden][rank])
+ *   out = round(o + round(c))                               [N][hidden]
+ * hidden / attn / o_weight / o_bias / out share `dtype` (sva_dtype); down and up are fp32.
+ * hidden_dim <= 4096 with 16 * (2 hidden_dim + rank) + small slices fitting shared memory.
+ * ------------------------------------------------------------------------------------- */
+int sva_adapter_forward(const void* hidden, int64_t hidden_row_stride, const void* attn, int64_t attn_row_stride,
+                        int32_t dtype, const void* o_weight, const void* o_bias, const float* down, const float* up,
+                        float scale, int32_t n_rows, int32_t hidden_dim, int32_t in_dim, int32_t rank, void* out,
+                        int64_t out_row_stride, void* stream);
 
 #ifdef __cplusplus
 }

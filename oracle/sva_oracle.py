@@ -335,6 +335,41 @@ def scan_decode(q_f32: np.ndarray, q_proj: np.ndarray, logit_scale: np.ndarray, 
     return DecodeResult(out, ql, lut, sl_all, fin_all, rs_all, n_summoned, n_verified)
 
 
+def scan_decode_rows(q_f32: np.ndarray, q_proj: np.ndarray, logit_scale: np.ndarray, codebooks: np.ndarray,
+                     codes: np.ndarray, k_low_rows, kv_rows, shortlist: int, budget: int, scaling: float,
+                     dtype: str = "f32", logits_mode: int = 0, key_len: np.ndarray | None = None) -> DecodeResult:
+    """scan_decode for one query token per head on catalogs too large to copy to the host whole.
+
+    The same steps as scan_decode (reference sva/llama.py:171-328), with the rows a step needs
+    fetched on demand: ``k_low_rows(h, idx) -> [n, R]`` float32 and ``kv_rows(h, idx) -> (K, V)``
+    [n, D] float32 (the query head's KV head rows).  q_f32 [H, D]; codes [H, L, S].  ``key_len``
+    [H] (optional) limits head h to keys [0, key_len[h]) (ragged batches).
+    """
+    n_heads, head_dim = q_f32.shape
+    rank = q_proj.shape[-1]
+    ql = query_low(q_f32[:, None, :], q_proj, logit_scale)
+    lut = build_lut(ql, codebooks)
+    out = np.zeros((n_heads, 1, head_dim), dtype=np.float32)
+    sl_all, fin_all, rs_all = [], [], []
+    n_summoned = n_verified = 0
+    for h in range(n_heads):
+        length = codes.shape[1] if key_len is None else int(key_len[h])
+        scores = adc_scores(lut[h : h + 1], codes[h : h + 1, :length], rank)[0, 0]
+        sl_cap = min(shortlist, length)
+        sl = topk_canonical(scores, sl_cap)
+        rank_scores = tree_dot(k_low_rows(h, sl), ql[h, 0][None, :]) / np.float32(math.sqrt(rank))
+        keep = topk_canonical(rank_scores, min(budget, sl_cap))
+        fin = sl[keep]
+        k_sel, v_sel = kv_rows(h, fin)
+        out[h, 0] = verify_one(q_f32[h], k_sel, v_sel, np.arange(fin.shape[0]), scaling, dtype, logits_mode)
+        n_summoned += sl.shape[0]
+        n_verified += fin.shape[0]
+        sl_all.append([np.sort(sl)])
+        fin_all.append([fin])
+        rs_all.append([rank_scores[keep]])
+    return DecodeResult(out, ql, lut, sl_all, fin_all, rs_all, n_summoned, n_verified)
+
+
 # ----------------------------------------------------------------------------------------
 # static inverted index (reference sva/llama.py:83-116, 427-576, 626-657)
 # ----------------------------------------------------------------------------------------

@@ -48,6 +48,8 @@ EXPORTED = (
     "sva_pq_scores",
     "sva_decode_workspace_size",
     "sva_decode",
+    "sva_decode_batched_workspace_size",
+    "sva_decode_batched",
     "sva_shard_workspace_size",
     "sva_shard_summon",
     "sva_shard_rescore",
@@ -59,6 +61,7 @@ EXPORTED = (
     "sva_inverted_workspace_size",
     "sva_decode_inverted",
     "sva_top_unique",
+    "sva_adapter_forward",
 )
 
 c_i32 = ctypes.c_int32
@@ -111,6 +114,24 @@ class DecodeArgs(ctypes.Structure):
         ("shortlist_out", c_vp),
         ("final_out", c_vp),
         ("stats", c_vp),
+    ]
+
+
+class BatchLayout(ctypes.Structure):
+    """Mirror of ``sva_batch_layout``."""
+
+    _fields_ = [
+        ("n_seqs", c_i32),
+        ("page_keys", c_i32),
+        ("seq_lens", c_vp),
+        ("page_table", c_vp),
+        ("page_table_stride", c_i64),
+        ("q_seq_stride", c_i64),
+        ("out_seq_stride", c_i64),
+        ("codes_page_stride", c_i64),
+        ("k_low_page_stride", c_i64),
+        ("k_page_stride", c_i64),
+        ("v_page_stride", c_i64),
     ]
 
 
@@ -195,6 +216,9 @@ def load() -> ctypes.CDLL:
             "sva_pq_scores": ([c_vp, c_i32, c_i32, c_i32, c_vp, c_i32, c_i32, c_vp, c_i64, c_vp, c_vp], ctypes.c_int),
             "sva_decode_workspace_size": ([ctypes.POINTER(DecodeArgs)], c_sz),
             "sva_decode": ([ctypes.POINTER(DecodeArgs), c_vp, c_sz, c_vp], ctypes.c_int),
+            "sva_decode_batched_workspace_size": ([ctypes.POINTER(DecodeArgs), ctypes.POINTER(BatchLayout)], c_sz),
+            "sva_decode_batched": ([ctypes.POINTER(DecodeArgs), ctypes.POINTER(BatchLayout), c_vp, c_sz, c_vp],
+                                   ctypes.c_int),
             "sva_shard_workspace_size": ([ctypes.POINTER(DecodeArgs)], c_sz),
             "sva_shard_summon": ([ctypes.POINTER(DecodeArgs), c_i64, c_vp, c_vp, c_sz, c_vp], ctypes.c_int),
             "sva_shard_rescore": ([ctypes.POINTER(DecodeArgs), c_i64, c_i32, c_i32, c_vp, c_vp, c_vp, c_sz, c_vp],
@@ -210,6 +234,8 @@ def load() -> ctypes.CDLL:
             "sva_decode_inverted": ([ctypes.POINTER(InvertedArgs), c_vp, c_sz, c_vp], ctypes.c_int),
             "sva_top_unique": ([c_vp, c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp,
                                 ctypes.POINTER(ctypes.c_int32), c_vp], ctypes.c_int),
+            "sva_adapter_forward": ([c_vp, c_i64, c_vp, c_i64, c_i32, c_vp, c_vp, c_vp, c_vp, c_f32, c_i32, c_i32,
+                                     c_i32, c_i32, c_vp, c_i64, c_vp], ctypes.c_int),
         }
         for name, (argtypes, restype) in sigs.items():
             fn = getattr(lib, name, None)

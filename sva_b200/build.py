@@ -15,7 +15,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 OUT = HERE / "libsva_b200.so"
-SOURCES = ["capi.cu", "catalog.cu", "decode.cu", "postings.cu", "inverted.cu"]
+SOURCES = ["capi.cu", "catalog.cu", "decode.cu", "postings.cu", "inverted.cu", "adapter.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -46,16 +46,34 @@ def needs_build() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
+    """Compile every source to an object in parallel (one nvcc per file), then link the library."""
     if not force and not needs_build():
         return OUT
+    from concurrent.futures import ThreadPoolExecutor
+
+    objdir = HERE / "_build"
+    objdir.mkdir(exist_ok=True)
+    nvcc = nvcc_path()
+    compile_flags = [f for f in NVCC_FLAGS if f != "--shared"]
+
+    def compile_one(src: Path) -> tuple[Path, subprocess.CompletedProcess]:
+        obj = objdir / (src.stem + ".o")
+        cmd = [nvcc, *compile_flags, "-I", str(HERE.parent / "include"), "-c", str(src), "-o", str(obj)]
+        if verbose:
+            print(" ".join(cmd), file=sys.stderr)
+        return obj, subprocess.run(cmd, capture_output=True, text=True)
+
+    with ThreadPoolExecutor(max_workers=len(sources())) as pool:
+        results = list(pool.map(compile_one, sources()))
+    for obj, res in results:
+        if res.returncode != 0:
+            raise RuntimeError(f"nvcc failed on {obj.stem}.cu ({res.returncode}):\n{res.stdout}\n{res.stderr}")
     tmp = OUT.with_suffix(".so.tmp")
-    cmd = [nvcc_path(), *NVCC_FLAGS, "-I", str(HERE.parent / "include"), *map(str, sources()), "-o", str(tmp),
-           "-lcudart"]
-    if verbose:
-        print(" ".join(cmd), file=sys.stderr)
+    cmd = [nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "--shared", "-Xcompiler", "-fPIC",
+           *[str(o) for o, _ in results], "-o", str(tmp), "-lcudart"]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
-        raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
+        raise RuntimeError(f"nvcc link failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
     os.replace(tmp, OUT)
     return OUT
 

@@ -54,6 +54,7 @@ constexpr int kPrepSmemLimit = 200 * 1024;  // dynamic shared memory of the prep
 constexpr int kCluster = 8;
 constexpr int kScanLocalCands = 1024;
 constexpr int kRepEntries = 256;  // largest S * C of the bank-replicated scan LUT
+constexpr int kMinPageKeys = 64;  // smallest page of a paged catalog (a power of two)
 
 // Control words per problem: the candidate count, the largest candidate key, and one threshold
 // per prep CTA (the scan's threshold T0 is their minimum).
@@ -105,6 +106,21 @@ struct DecodeParams {
   int prep_rep;   // the prep kernel's sample lookups use a bank-replicated LUT
   int kv_stage;   // the finish kernel stages the shortlist's K and V rows in shared memory
   int q_host;     // the query is in page-locked host memory (not written by the kernels before)
+  // batch layout (sva_decode_batched; sva_decode is one unpaged sequence).  Problem prob is
+  // (sequence b, head h, token t) with prob = (b * H + h) * T + t.  Key l of sequence b lives on
+  // "page" page_of(b, l), row l & page_mask of it: with a page table, page_table[b][l >> shift];
+  // without one the page is the sequence itself (shift 62), so the page strides are then the
+  // per-sequence strides.
+  int batched;                // launched through sva_decode_batched (kernels instantiated with kB)
+  int n_seqs;
+  int n_probs;                // n_seqs * n_heads * n_queries
+  const int64_t* seq_lens;    // [n_seqs] keys per sequence, or NULL (key_len each)
+  int64_t q_seq_stride, out_seq_stride;
+  const int32_t* page_table;  // [n_seqs][pt_stride] or NULL
+  int64_t pt_stride;
+  int page_shift;
+  int64_t page_mask;
+  int64_t codes_page_stride, k_low_page_stride, k_page_stride, v_page_stride;
   DecodeSmem lay;
   float* ws_qlow;
   float* ws_lut;
@@ -137,24 +153,155 @@ __device__ __forceinline__ float finish_score(float sum, const DecodeParams& p) 
   return p.sqrt_r_pow2 ? __fmul_rn(sum, p.inv_sqrt_r) : div_rn_outlined(sum, p.sqrt_r);
 }
 
-__device__ __forceinline__ int64_t allowed_length(const DecodeParams& p, int t) {
-  const int64_t L = p.a.key_len;
-  int64_t n = p.a.allowed_len ? p.a.allowed_len[t] : (L - p.a.n_queries + t + 1);
+// (sequence, head, token) of problem `prob`.
+struct ProbIdx {
+  int b, h, t;
+};
+
+// Layout helpers.  kB (batch layout) is a compile-time flag of the kernels: the single-sequence
+// instantiations (sva_decode, the shards) compile none of the batch / page arithmetic; the
+// batched ones (sva_decode_batched) follow the layout described at DecodeParams.
+template <bool kB>
+__device__ __forceinline__ ProbIdx prob_index(const DecodeParams& p, int prob) {
+  const int T = p.a.n_queries;
+  ProbIdx r;
+  if constexpr (kB) {
+    const int HT = p.a.n_heads * T;
+    r.b = prob / HT;
+    const int rem = prob - r.b * HT;
+    r.h = rem / T;
+    r.t = rem - r.h * T;
+  } else {
+    r.b = 0;
+    r.h = prob / T;
+    r.t = prob - r.h * T;
+  }
+  return r;
+}
+
+// Keys of sequence b.
+template <bool kB>
+__device__ __forceinline__ int64_t seq_keys(const DecodeParams& p, int b) {
+  if (!kB || !p.seq_lens) return p.a.key_len;
+  const int64_t n = __ldg(p.seq_lens + b);
+  return n < 0 ? 0 : (n > p.a.key_len ? p.a.key_len : n);
+}
+
+template <bool kB>
+__device__ __forceinline__ int64_t allowed_length(const DecodeParams& p, int b, int t) {
+  const int64_t L = seq_keys<kB>(p, b);
+  const int64_t row = kB ? (int64_t)b * p.a.n_queries + t : t;
+  int64_t n = p.a.allowed_len ? p.a.allowed_len[row] : (L - p.a.n_queries + t + 1);
   return n < 0 ? 0 : (n > L ? L : n);
 }
 
-__device__ __forceinline__ bool key_allowed(const DecodeParams& p, int t, int64_t i, int64_t len_t) {
+template <bool kB>
+__device__ __forceinline__ bool key_allowed(const DecodeParams& p, int b, int t, int64_t i, int64_t len_t) {
   if (i >= len_t) return false;
-  if (p.a.allowed_mask) return p.a.allowed_mask[t * p.a.mask_row_stride + i] != 0;
+  const int64_t row = kB ? (int64_t)b * p.a.n_queries + t : t;
+  if (p.a.allowed_mask) return p.a.allowed_mask[row * p.a.mask_row_stride + i] != 0;
   return true;
 }
 
-// Ordered ADC key of key i (0 when not allowed), scalar code loads.
+// Page of key l of sequence b (the sequence itself when there is no page table).
+__device__ __forceinline__ int64_t page_of(const DecodeParams& p, int b, int64_t l) {
+  return p.page_table ? static_cast<int64_t>(__ldg(p.page_table + b * p.pt_stride + (l >> p.page_shift))) : b;
+}
+
+// Base addresses of head h of sequence b: with a page table the pool's head base (pages are
+// added per key); without one the sequence's own rows.
+template <bool kB>
+__device__ __forceinline__ const uint8_t* codes_base(const DecodeParams& p, int b, int h) {
+  const uint8_t* base = p.a.codes + h * p.a.codes_head_stride;
+  if constexpr (kB) base += p.page_table ? 0 : b * p.codes_page_stride;
+  return base;
+}
+template <bool kB>
+__device__ __forceinline__ const float* k_low_base(const DecodeParams& p, int b, int h) {
+  const float* base = p.a.k_low + h * p.a.k_low_head_stride;
+  if constexpr (kB) base += p.page_table ? 0 : b * p.k_low_page_stride;
+  return base;
+}
+template <typename T, bool kB>
+__device__ __forceinline__ const T* keys_base(const DecodeParams& p, int b, int kvh) {
+  const T* base = reinterpret_cast<const T*>(p.a.keys) + kvh * p.a.k_head_stride;
+  if constexpr (kB) base += p.page_table ? 0 : b * p.k_page_stride;
+  return base;
+}
+template <typename T, bool kB>
+__device__ __forceinline__ const T* values_base(const DecodeParams& p, int b, int kvh) {
+  const T* base = reinterpret_cast<const T*>(p.a.values) + kvh * p.a.v_head_stride;
+  if constexpr (kB) base += p.page_table ? 0 : b * p.v_page_stride;
+  return base;
+}
+
+// Row addresses of key l from those bases.
+template <bool kB>
+__device__ __forceinline__ const uint8_t* key_codes(const DecodeParams& p, const uint8_t* base, int b, int64_t l) {
+  if constexpr (kB) {
+    if (p.page_table) return base + page_of(p, b, l) * p.codes_page_stride + (l & p.page_mask) * p.a.subspaces;
+  }
+  return base + l * p.a.subspaces;
+}
+template <bool kB>
+__device__ __forceinline__ const float* key_k_low(const DecodeParams& p, const float* base, int b, int64_t l) {
+  if constexpr (kB) {
+    if (p.page_table) return base + page_of(p, b, l) * p.k_low_page_stride + (l & p.page_mask) * p.a.rank_dim;
+  }
+  return base + l * p.a.rank_dim;
+}
+template <typename T, bool kB>
+__device__ __forceinline__ const T* key_row(const DecodeParams& p, const T* base, int b, int64_t l, int64_t page_stride,
+                                            int64_t row_stride) {
+  if constexpr (kB) {
+    if (p.page_table) return base + page_of(p, b, l) * page_stride + (l & p.page_mask) * row_stride;
+  }
+  return base + l * row_stride;
+}
+
+// K (or V) row functors of the verify functions over key indices rows[j] of sequence b.
+template <typename T, bool kB>
+struct KeyRows {
+  const DecodeParams* p;
+  const T* base;
+  const int32_t* rows;
+  int b;
+  int64_t page_stride, row_stride;
+  __device__ __forceinline__ const T* operator()(int j) const {
+    return key_row<T, kB>(*p, base, b, rows[j], page_stride, row_stride);
+  }
+};
+
+template <typename T, bool kB>
+__device__ __forceinline__ KeyRows<T, kB> k_rows(const DecodeParams& p, int b, int kvh, const int32_t* rows) {
+  return KeyRows<T, kB>{&p, keys_base<T, kB>(p, b, kvh), rows, b, p.k_page_stride, p.a.k_row_stride};
+}
+template <typename T, bool kB>
+__device__ __forceinline__ KeyRows<T, kB> v_rows(const DecodeParams& p, int b, int kvh, const int32_t* rows) {
+  return KeyRows<T, kB>{&p, values_base<T, kB>(p, b, kvh), rows, b, p.v_page_stride, p.a.v_row_stride};
+}
+
+// Query and output rows of problem (b, h, t).
+template <typename T, bool kB>
+__device__ __forceinline__ const T* query_row(const DecodeParams& p, int b, int h, int t) {
+  const T* q = reinterpret_cast<const T*>(p.a.query) + h * p.a.q_head_stride + t * p.a.q_row_stride;
+  if constexpr (kB) q += b * p.q_seq_stride;
+  return q;
+}
+template <typename T, bool kB>
+__device__ __forceinline__ T* out_row(const DecodeParams& p, int b, int h, int t) {
+  T* o = reinterpret_cast<T*>(p.a.out) + h * p.a.out_head_stride + t * p.a.out_row_stride;
+  if constexpr (kB) o += b * p.out_seq_stride;
+  return o;
+}
+
+// Ordered ADC key of key i (0 when not allowed), scalar code loads; `codes` from codes_base.
+template <bool kB>
 __device__ __forceinline__ uint32_t adc_key(const DecodeParams& p, const uint8_t* __restrict__ codes,
-                                            const float* __restrict__ lut, int t, int64_t i, int64_t len_t) {
-  if (!key_allowed(p, t, i, len_t)) return 0u;
+                                            const float* __restrict__ lut, int b, int t, int64_t i, int64_t len_t) {
+  if (!key_allowed<kB>(p, b, t, i, len_t)) return 0u;
   const int S = p.a.subspaces, C = p.a.codewords;
-  const uint8_t* row = codes + i * S;
+  const uint8_t* row = key_codes<kB>(p, codes, b, i);
   float sum = 0.f;
   for (int s = 0; s < S; ++s) sum = __fadd_rn(sum, lut[s * C + __ldg(row + s)]);
   return ordered_key(finish_score(sum, p));
@@ -240,11 +387,12 @@ __device__ __forceinline__ float adc_plain(const Codes4<S>& c, int j, const floa
   return sum;
 }
 
-template <typename T>
-__device__ void build_qlut(const DecodeParams& p, int h, int t, float* qf, float* ql, float* lut, float* stage) {
+template <typename T, bool kB>
+__device__ void build_qlut(const DecodeParams& p, int prob, int b, int h, int t, float* qf, float* ql, float* lut,
+                           float* stage) {
   const int D = p.a.head_dim, R = p.a.rank_dim, S = p.a.subspaces, C = p.a.codewords;
-  const T* q = reinterpret_cast<const T*>(p.a.query) + h * p.a.q_head_stride + t * p.a.q_row_stride;
-  const float* lo = p.a.lut_override ? p.a.lut_override + ((size_t)h * p.a.n_queries + t) * S * C : nullptr;
+  const T* q = query_row<T, kB>(p, b, h, t);
+  const float* lo = p.a.lut_override ? p.a.lut_override + (size_t)prob * S * C : nullptr;
   build_query_lut<T>(q, D, R, S, C, p.a.q_proj + (size_t)h * D * R, __ldg(p.a.scale + h),
                      p.a.codebooks + (size_t)h * S * C * (R / S), lo, qf, ql, lut, stage);
 }
@@ -269,22 +417,22 @@ struct NoHook {
   __device__ void operator()() const {}
 };
 
-template <int U, class Hook = NoHook>
-__device__ void rescore_rows(const DecodeParams& p, int h, const float* ql, const int32_t* rows, int n, uint32_t* rk,
-                             const Hook& after_first_loads = Hook()) {
+template <int U, bool kB, class Hook = NoHook>
+__device__ void rescore_rows(const DecodeParams& p, int b, int h, const float* ql, const int32_t* rows, int n,
+                             uint32_t* rk, const Hook& after_first_loads = Hook()) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int half = lane >> 4, l16 = lane & 15;
   const int R = p.a.rank_dim;
   const float4 q4 = (4 * l16 < R) ? make_float4(ql[4 * l16], ql[4 * l16 + 1], ql[4 * l16 + 2], ql[4 * l16 + 3])
                                   : make_float4(0.f, 0.f, 0.f, 0.f);
-  const float* klb = p.a.k_low + h * p.a.k_low_head_stride;
+  const float* klb = k_low_base<kB>(p, b, h);
   float4 r[U];
   auto load = [&](int base) {
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int j = base + 2 * u + half;
       r[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (j < n && 4 * l16 < R) r[u] = load4<float>(klb + (int64_t)rows[j] * R, 4 * l16, R);
+      if (j < n && 4 * l16 < R) r[u] = load4<float>(key_k_low<kB>(p, klb, b, rows[j]), 4 * l16, R);
     }
   };
   int base = warp * 2 * U;
@@ -335,7 +483,7 @@ __device__ void write_sorted(const int32_t* src, int n, int width, int32_t* dst,
   __syncthreads();
 }
 
-template <typename T>
+template <typename T, bool kB>
 __global__ void __launch_bounds__(kThreads) decode_fused_kernel(const DecodeParams p) {
   extern __shared__ __align__(16) unsigned char smem[];
   float* qf = reinterpret_cast<float*>(smem + p.lay.qf);
@@ -351,18 +499,18 @@ __global__ void __launch_bounds__(kThreads) decode_fused_kernel(const DecodePara
   uint32_t* cache = reinterpret_cast<uint32_t*>(smem + p.lay.cache);
 
   const int prob = blockIdx.x;
-  const int h = prob / p.a.n_queries;
-  const int t = prob - h * p.a.n_queries;
+  const ProbIdx pi = prob_index<kB>(p, prob);
+  const int b = pi.b, h = pi.h, t = pi.t;
   const int kvh = h / p.groups;
-  const int64_t L = p.a.key_len;
-  const int64_t len_t = allowed_length(p, t);
-  const uint8_t* codes = p.a.codes + h * p.a.codes_head_stride;
+  const int64_t L = seq_keys<kB>(p, b);
+  const int64_t len_t = allowed_length<kB>(p, b, t);
+  const uint8_t* codes = codes_base<kB>(p, b, h);
   const int tid = threadIdx.x;
 
-  build_qlut<T>(p, h, t, qf, ql, lut, reinterpret_cast<float*>(cache));
+  build_qlut<T, kB>(p, prob, b, h, t, qf, ql, lut, reinterpret_cast<float*>(cache));
   int nv = 0;
   for (int64_t i = tid; i < L; i += blockDim.x) {
-    const uint32_t key = adc_key(p, codes, lut, t, i, len_t);
+    const uint32_t key = adc_key<kB>(p, codes, lut, b, t, i, len_t);
     cache[i] = key;
     nv += (key != 0u);
   }
@@ -377,17 +525,16 @@ __global__ void __launch_bounds__(kThreads) decode_fused_kernel(const DecodePara
     n_sl = cta_compact(item, static_cast<int>(L), thr, [&](int pos, int i, unsigned long long) { sl[pos] = i; },
                        scratch);
   }
-  rescore_rows<16>(p, h, ql, sl, n_sl, rk);
-  const int b = min(p.b_cap, n_sl);
+  rescore_rows<16, kB>(p, b, h, ql, sl, n_sl, rk);
+  const int nb = min(p.b_cap, n_sl);
   int n_fin;
   {
     auto item = [&](int j) -> unsigned long long { return composite(rk[j], static_cast<uint32_t>(sl[j])); };
-    const SelectThreshold thr = cta_radix_select(item, n_sl, b, sc);
+    const SelectThreshold thr = cta_radix_select(item, n_sl, nb, sc);
     n_fin = cta_compact(item, n_sl, thr, [&](int pos, int j, unsigned long long) { fin[pos] = sl[j]; }, scratch);
   }
-  verify_rows<T>(p.a.keys, p.a.k_head_stride, p.a.k_row_stride, p.a.values, p.a.v_head_stride, p.a.v_row_stride, kvh,
-                 qf, p.a.head_dim, fin, n_fin, p.a.softmax_scale, p.a.logits_mode, lg, acc, scratch,
-                 reinterpret_cast<T*>(p.a.out) + h * p.a.out_head_stride + t * p.a.out_row_stride);
+  verify_rows_fn<T>(k_rows<T, kB>(p, b, kvh, fin), v_rows<T, kB>(p, b, kvh, fin), qf, p.a.head_dim, n_fin,
+                    p.a.softmax_scale, p.a.logits_mode, lg, acc, scratch, out_row<T, kB>(p, b, h, t));
   unsigned long long* tmp = reinterpret_cast<unsigned long long*>(cache);
   if (p.a.shortlist_out) write_sorted(sl, n_sl, p.a.shortlist, p.a.shortlist_out + (size_t)prob * p.a.shortlist, tmp);
   if (p.a.final_out) write_sorted(fin, n_fin, p.a.budget, p.a.final_out + (size_t)prob * p.a.budget, tmp);
@@ -407,20 +554,21 @@ __global__ void __launch_bounds__(kThreads) decode_fused_kernel(const DecodePara
 // thread handles groups of four consecutive keys, kGroupsInFlight vector loads at a time.
 // Iteration is warp-uniform: every lane calls f the same number of times (slots past the end
 // come with i == i1 and key 0), so f may use warp collectives.
-template <int S, class F>
-__device__ __forceinline__ void scan_segment(const DecodeParams& p, const uint8_t* codes, const float* lut, int t,
+// `codes` is codes_base(p, b, h); i0 is a multiple of four.
+template <int S, bool kB, class F>
+__device__ __forceinline__ void scan_segment(const DecodeParams& p, const uint8_t* codes, const float* lut, int b, int t,
                                              int64_t len_t, int64_t i0, int64_t i1, const F& f) {
   const int lane = threadIdx.x & 31;
   if constexpr (S > 0) {
     const int ngroups = static_cast<int>((i1 - i0 + 3) >> 2);
     const bool dense = (p.a.allowed_mask == nullptr) && (i1 <= len_t);
-    const uint8_t* cbase = codes + i0 * S;
     for (int gb = (threadIdx.x & ~31); gb < ngroups; gb += blockDim.x * kGroupsInFlight) {
       Codes4<S> c[kGroupsInFlight];
 #pragma unroll
       for (int u = 0; u < kGroupsInFlight; ++u) {
         const int g = gb + lane + u * blockDim.x;
-        if (g < ngroups && i0 + 4 * g + 3 < i1) c[u] = load_codes4<S>(cbase, 4 * g);
+        // a group of four keys never straddles a page (pages hold a multiple of four keys)
+        if (g < ngroups && i0 + 4 * g + 3 < i1) c[u] = load_codes4<S>(key_codes<kB>(p, codes, b, i0 + 4 * g), 0);
       }
 #pragma unroll
       for (int u = 0; u < kGroupsInFlight; ++u) {
@@ -433,9 +581,9 @@ __device__ __forceinline__ void scan_segment(const DecodeParams& p, const uint8_
           const bool live = g < ngroups && i < i1;
           uint32_t key = 0u;
           if (full) {
-            key = (dense || key_allowed(p, t, i, len_t)) ? adc_key4<S>(p, c[u], j, lut) : 0u;
+            key = (dense || key_allowed<kB>(p, b, t, i, len_t)) ? adc_key4<S>(p, c[u], j, lut) : 0u;
           } else if (live) {
-            key = adc_key(p, codes, lut, t, i, len_t);
+            key = adc_key<kB>(p, codes, lut, b, t, i, len_t);
           }
           f(live ? i : i1, key);
         }
@@ -444,7 +592,7 @@ __device__ __forceinline__ void scan_segment(const DecodeParams& p, const uint8_
   } else {
     for (int64_t wb = i0 + (threadIdx.x & ~31); wb < i1; wb += blockDim.x) {
       const int64_t i = wb + lane;
-      const uint32_t key = (i < i1) ? adc_key(p, codes, lut, t, i, len_t) : 0u;
+      const uint32_t key = (i < i1) ? adc_key<kB>(p, codes, lut, b, t, i, len_t) : 0u;
       f(i < i1 ? i : i1, key);
     }
   }
@@ -529,7 +677,7 @@ __device__ __forceinline__ void stage_floats(float* dst, const float* src, int n
 // part's sampled score range (one counting pass, no exact select).  Every part computes q_low
 // and the LUT (part 0 publishes them).  Inputs that are weights (q_proj, codebooks, the sampled
 // codes) are staged before waiting for the predecessor; q and every workspace write come after.
-template <typename T, int S>
+template <typename T, int S, bool kB>
 __global__ void __launch_bounds__(kThreads) decode_prep_kernel(const DecodeParams p, const PrepSmem lay) {
   extern __shared__ __align__(16) unsigned char dyn[];
   __shared__ float qf[kMaxHeadDim];
@@ -542,31 +690,34 @@ __global__ void __launch_bounds__(kThreads) decode_prep_kernel(const DecodeParam
   float* lut_rep = reinterpret_cast<float*>(dyn + lay.rep);
   uint32_t* skeys = reinterpret_cast<uint32_t*>(dyn + lay.stage);  // after q_low: the sampled keys
   const int prob = blockIdx.x / kPrepCtas, part = blockIdx.x - prob * kPrepCtas;
-  const int h = prob / p.a.n_queries, t = prob - h * p.a.n_queries;
+  const ProbIdx pi = prob_index<kB>(p, prob);
+  const int b = pi.b, h = pi.h, t = pi.t;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int D = p.a.head_dim, R = p.a.rank_dim, S2 = p.a.subspaces, C = p.a.codewords;
   const int SC = S2 * C;
   pdl_launch_dependents();  // the scan may be scheduled now; it waits for this grid's results
   if (part == 0 && tid == 0) stamp(p, prob, 0);
-  const int64_t len_t = allowed_length(p, t);
-  const uint8_t* codes = p.a.codes + h * p.a.codes_head_stride;
+  // lengths, page tables and codes are the caller's inputs (like the weights), staged before the
+  // wait; the query and the workspace come after it
+  const int64_t len_t = allowed_length<kB>(p, b, t);
+  const uint8_t* codes = codes_base<kB>(p, b, h);
   const int g_first = part * kThreads * kPrepGroups;
   if constexpr (S > 0) {
 #pragma unroll
     for (int u = 0; u < kPrepGroups; ++u) {
       const int gl = tid + u * kThreads;
       const int64_t g0 = sample_group_start(len_t, g_first + gl);
-      if (g0 + 3 < len_t) copy_group_async<S>(sample + gl * 4 * S, codes + g0 * S);
+      if (g0 + 3 < len_t) copy_group_async<S>(sample + gl * 4 * S, key_codes<kB>(p, codes, b, g0));
     }
     asm volatile("cp.async.commit_group;\n" ::: "memory");
   }
-  const float* lo = p.a.lut_override ? p.a.lut_override + ((size_t)h * p.a.n_queries + t) * SC : nullptr;
+  const float* lo = p.a.lut_override ? p.a.lut_override + (size_t)prob * SC : nullptr;
   stage_floats(stage, p.a.q_proj + (size_t)h * D * R, D * R);
   if (!lo) stage_floats(cbs, p.a.codebooks + (size_t)h * C * R, C * R);
   {
     // a query in host memory is the caller's input, not a result of the kernels before, so its
     // PCIe round trip overlaps the wait; a device query may be the previous kernel's output
-    const T* q = reinterpret_cast<const T*>(p.a.query) + h * p.a.q_head_stride + t * p.a.q_row_stride;
+    const T* q = query_row<T, kB>(p, b, h, t);
     if (p.q_host)
       for (int d = tid; d < D; d += blockDim.x) qf[d] = to_f32<T>(q[d]);
     pdl_wait();
@@ -627,11 +778,11 @@ __global__ void __launch_bounds__(kThreads) decode_prep_kernel(const DecodeParam
       for (int j = 0; j < 4; ++j) {
         const float sum = rep ? adc_rep_rt<(S > 0 ? S : 1)>(c, j, rep_lane, C)
                               : adc_plain<(S > 0 ? S : 1), 0>(c, j, lut, C);
-        k4[j] = key_allowed(p, t, g0 + j, len_t) ? ordered_key(finish_score(sum, p)) : 0u;
+        k4[j] = key_allowed<kB>(p, b, t, g0 + j, len_t) ? ordered_key(finish_score(sum, p)) : 0u;
       }
     } else {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) k4[j] = adc_key(p, codes, lut, t, g0 + j, len_t);
+      for (int j = 0; j < 4; ++j) k4[j] = adc_key<kB>(p, codes, lut, b, t, g0 + j, len_t);
     }
     *reinterpret_cast<uint4*>(skeys + 4 * gl) = make_uint4(k4[0], k4[1], k4[2], k4[3]);
 #pragma unroll
@@ -767,7 +918,7 @@ __device__ __forceinline__ float adc_rep(const Codes4<S>& c, int j, uint32_t lan
 // conflicts; the score of every key is the canonical sequential fp32 sum.  Candidates are rare
 // (about 2x the shortlist among all keys), so each one takes a shared atomic of its own and the
 // CTA publishes its list with one global atomic.
-template <int S, int C, bool POW2>
+template <int S, int C, bool POW2, bool PAGED>
 __global__ void __launch_bounds__(kScanThreads, 2) decode_scan_kernel(const DecodeParams p) {
   constexpr bool kRep = (S > 0) && (C > 0) && (S * C <= kRepEntries);
   constexpr int kInFlight = S == 8 ? 2 : kGroupsInFlight;  // 4-key groups loaded ahead per thread
@@ -778,8 +929,10 @@ __global__ void __launch_bounds__(kScanThreads, 2) decode_scan_kernel(const Deco
   __shared__ uint32_t n_local;
   __shared__ uint32_t flush_base;
   __shared__ uint32_t max_key;
+  __shared__ uint32_t seg_pages[PAGED ? kScanKeys / kMinPageKeys : 1];  // page table of this segment
   const int prob = blockIdx.y, seg = blockIdx.x;
-  const int h = prob / p.a.n_queries, t = prob - h * p.a.n_queries;
+  const ProbIdx pi = prob_index<true>(p, prob);
+  const int b = pi.b, h = pi.h, t = pi.t;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr uint32_t kLutAlign = kRep ? static_cast<uint32_t>(C > 0 ? C : 1) * 128u : 16u;
   const uint32_t dyn_base = static_cast<uint32_t>(__cvta_generic_to_shared(scan_dyn));
@@ -790,10 +943,16 @@ __global__ void __launch_bounds__(kScanThreads, 2) decode_scan_kernel(const Deco
   const uint32_t t0 = read_t0(ctrl);
   const int SC = p.a.subspaces * p.a.codewords;
   const float* glut = p.ws_lut + (size_t)prob * kMaxLut;
-  const int64_t len_t = allowed_length(p, t);
+  const int64_t len_t = allowed_length<true>(p, b, t);
   const int64_t i0 = (int64_t)seg * kScanKeys;
   const int64_t i1 = min(len_t, i0 + kScanKeys);
   if (i0 >= i1) return;  // uniform over the block
+  if constexpr (PAGED) {
+    // segments start on a page boundary (kScanKeys is a multiple of the page size)
+    const int np = static_cast<int>(((i1 - i0) + p.page_mask) >> p.page_shift);
+    const int32_t* pt = p.page_table + b * p.pt_stride + (i0 >> p.page_shift);
+    for (int e = tid; e < np; e += blockDim.x) seg_pages[e] = static_cast<uint32_t>(__ldg(pt + e));
+  }
   const bool fast = (S > 0) && p.a.allowed_mask == nullptr && ((i1 - i0) & 3) == 0;
   if (kRep && fast) {
     // warp w fills entries w*32 .. w*32+31 (+ multiples of blockDim.x); lane l writes copy l
@@ -813,7 +972,7 @@ __global__ void __launch_bounds__(kScanThreads, 2) decode_scan_kernel(const Deco
     max_key = 0u;
   }
   __syncthreads();
-  const uint8_t* codes = p.a.codes + h * p.a.codes_head_stride;
+  const uint8_t* codes = codes_base<true>(p, b, h);
   uint2* cand = p.ws_cand + (size_t)prob * p.a.key_len;
   uint32_t my_max = 0u;  // largest key this thread took
   auto take = [&](uint32_t key, int64_t i) {
@@ -832,6 +991,17 @@ __global__ void __launch_bounds__(kScanThreads, 2) decode_scan_kernel(const Deco
       const float scale = p.inv_sqrt_r;
       const int ngroups = static_cast<int>((i1 - i0) >> 2);
       const uint8_t* cbase = codes + i0 * S;
+      // codes of the 4-key group g of the segment (groups never straddle a page)
+      auto group_codes = [&](int g) -> Codes4<S> {
+        if constexpr (PAGED) {
+          const int k = 4 * g;
+          return load_codes4<S>(codes + static_cast<int64_t>(seg_pages[k >> p.page_shift]) * p.codes_page_stride +
+                                    static_cast<int64_t>(k & static_cast<int>(p.page_mask)) * S,
+                                0);
+        } else {
+          return load_codes4<S>(cbase, 4 * g);
+        }
+      };
       const uint32_t lut_base = static_cast<uint32_t>(__cvta_generic_to_shared(lut));
       const uint32_t lane_base = lut_base + static_cast<uint32_t>(lane) * 4u;
       // the and-or offset needs a table address with no bit in the code field or below it
@@ -857,7 +1027,7 @@ __global__ void __launch_bounds__(kScanThreads, 2) decode_scan_kernel(const Deco
         for (int gb = tid; gb < nfull; gb += tile) {
           Codes4<S> c[kInFlight];
 #pragma unroll
-          for (int u = 0; u < kInFlight; ++u) c[u] = load_codes4<S>(cbase, 4 * (gb + u * kScanThreads));
+          for (int u = 0; u < kInFlight; ++u) c[u] = group_codes(gb + u * kScanThreads);
 #pragma unroll
           for (int u = 0; u < kInFlight; ++u) {
             float sc[4];
@@ -875,7 +1045,7 @@ __global__ void __launch_bounds__(kScanThreads, 2) decode_scan_kernel(const Deco
       if (or_ok) main_loop(std::true_type{});
       else main_loop(std::false_type{});
       for (int g = nfull + tid; g < ngroups; g += kScanThreads) {
-        const Codes4<S> c = load_codes4<S>(cbase, 4 * g);
+        const Codes4<S> c = group_codes(g);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const float sc = score(c, j);
@@ -886,7 +1056,7 @@ __global__ void __launch_bounds__(kScanThreads, 2) decode_scan_kernel(const Deco
   }
   if (!fast) {
     // masked or ragged segments: generic per-key path over the plain LUT layout
-    scan_segment<S>(p, codes, lut, t, len_t, i0, i1, [&](int64_t i, uint32_t key) {
+    scan_segment<S, true>(p, codes, lut, b, t, len_t, i0, i1, [&](int64_t i, uint32_t key) {
       if (key != 0u && key >= t0) take(key, i);
     });
   }
@@ -918,15 +1088,16 @@ static __device__ __forceinline__ int shortlist_from_l2(const uint2* gc, int n_c
 
 // Shortlist select over every allowed key (the sampled threshold was above the k-th best key).
 // Writes out_idx[pos] = key index and, when out_c is set, out_c[pos] = its composite.
-static __device__ __forceinline__ int shortlist_from_all(const DecodeParams& p, int prob, int h, int t, int64_t len_t,
-                                                        int k, float* lut, SelectScratch* sc, int* scratch,
-                                                        int32_t* out_idx, unsigned long long* out_c) {
+template <bool kB>
+static __device__ __forceinline__ int shortlist_from_all(const DecodeParams& p, int prob, int b, int h, int t,
+                                                        int64_t len_t, int k, float* lut, SelectScratch* sc,
+                                                        int* scratch, int32_t* out_idx, unsigned long long* out_c) {
   for (int e = threadIdx.x; e < p.a.subspaces * p.a.codewords; e += blockDim.x)
     lut[e] = __ldcg(p.ws_lut + (size_t)prob * kMaxLut + e);
   __syncthreads();
-  const uint8_t* codes = p.a.codes + h * p.a.codes_head_stride;
+  const uint8_t* codes = codes_base<kB>(p, b, h);
   auto item = [&](int i) -> unsigned long long {
-    const uint32_t key = adc_key(p, codes, lut, t, i, len_t);
+    const uint32_t key = adc_key<kB>(p, codes, lut, b, t, i, len_t);
     return key ? composite(key, static_cast<uint32_t>(i)) : 0ull;
   };
   const SelectThreshold thr = cta_radix_select(item, static_cast<int>(len_t), k, sc);
@@ -945,10 +1116,12 @@ static __device__ __forceinline__ int shortlist_from_all(const DecodeParams& p, 
 // `lut`) and a fallback is counted when count_fallback is set.  Writes the selected keys'
 // indices to out_idx[0, n) (and their composites to out_c when it is set) in a deterministic
 // order; returns n.  Ends with a barrier.
-static __device__ __forceinline__ int select_shortlist(const DecodeParams& p, int prob, int h, int t, int64_t len_t,
+template <bool kB>
+static __device__ __forceinline__ int select_shortlist(const DecodeParams& p, int prob, int b, int h, int t,
+                                                      int64_t len_t,
                                                       uint2* cand, float* lut, SelectScratch* sc, int* scratch,
                                                       int32_t* out_idx, unsigned long long* out_c,
-                                                      bool count_fallback) {
+                                                      bool count_fallback, int cand_cap = kCandSmem) {
   const int tid = threadIdx.x;
   const int64_t L = p.a.key_len;
   const uint32_t* ctrl = p.ws_ctrl + (size_t)prob * CTRL_WORDS;
@@ -961,7 +1134,9 @@ static __device__ __forceinline__ int select_shortlist(const DecodeParams& p, in
       n_allowed = len_t;
     } else {
       int c = 0;
-      for (int64_t i = tid; i < len_t; i += blockDim.x) c += p.a.allowed_mask[t * p.a.mask_row_stride + i] != 0;
+      const int64_t mr = kB ? (int64_t)b * p.a.n_queries + t : t;
+      const uint8_t* mrow = p.a.allowed_mask + mr * p.a.mask_row_stride;
+      for (int64_t i = tid; i < len_t; i += blockDim.x) c += mrow[i] != 0;
       n_allowed = block_sum_int(c, scratch);
     }
   }
@@ -973,7 +1148,7 @@ static __device__ __forceinline__ int select_shortlist(const DecodeParams& p, in
   const float hi = kmax != 0u ? key_to_float(kmax) : INFINITY;
   int n_sl = 0;
   if (n_cand >= k) {
-    if (n_cand <= kCandSmem) {
+    if (n_cand <= cand_cap) {
       unsigned long long* c64 = reinterpret_cast<unsigned long long*>(cand);
       copy_batched(c64, gc, n_cand);
       if (tid == 0) stamp(p, prob, 12);
@@ -993,7 +1168,7 @@ static __device__ __forceinline__ int select_shortlist(const DecodeParams& p, in
       }
     }
   } else {
-    n_sl = shortlist_from_all(p, prob, h, t, len_t, k, lut, sc, scratch, out_idx, out_c);
+    n_sl = shortlist_from_all<kB>(p, prob, b, h, t, len_t, k, lut, sc, scratch, out_idx, out_c);
     if (count_fallback && p.a.stats && tid == 0) atomicAdd(p.a.stats + SVA_STAT_SELECT_FALLBACKS, 1ull);
   }
   __syncthreads();
@@ -1064,7 +1239,7 @@ __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.w
 //      max and fp64 denominator over the final logits;
 //   4. each CTA forms the rounded weights of its own final keys and their fp64 weighted V sum;
 //   5. CTA 0 adds the kCluster partial sums in CTA order and writes the output.
-template <typename T>
+template <typename T, bool kB>
 __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
     decode_finish_kernel(const DecodeParams p, const FinishSmem lay) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -1089,18 +1264,23 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
   cg::cluster_group cluster = cg::this_cluster();
   const int crank = static_cast<int>(cluster.block_rank());
   const int prob = blockIdx.x / kCluster;
-  const int h = prob / p.a.n_queries;
-  const int t = prob - h * p.a.n_queries;
+  const ProbIdx pi = prob_index<kB>(p, prob);
+  const int b = pi.b, h = pi.h, t = pi.t;
   const int kvh = h / p.groups;
-  const int64_t len_t = allowed_length(p, t);
+  const int64_t len_t = allowed_length<kB>(p, b, t);
   const int D = p.a.head_dim;
   const int tid = threadIdx.x;
 
   {
-    const T* q = reinterpret_cast<const T*>(p.a.query) + h * p.a.q_head_stride + t * p.a.q_row_stride;
+    const T* q = query_row<T, kB>(p, b, h, t);
     pdl_launch_dependents();  // a following decode's prep may start prefetching its inputs
-    for (int d = tid; d < D; d += blockDim.x) qf[d] = to_f32<T>(q[d]);
+    // as in prep: a host-resident query is the caller's input and may be read before the wait;
+    // a device query may be the output of the decode before this one
+    if (p.q_host)
+      for (int d = tid; d < D; d += blockDim.x) qf[d] = to_f32<T>(q[d]);
     pdl_wait();  // the scan's candidates (and prep's q_low)
+    if (!p.q_host)
+      for (int d = tid; d < D; d += blockDim.x) qf[d] = to_f32<T>(q[d]);
     for (int r = tid; r < p.a.rank_dim; r += blockDim.x) ql[r] = __ldcg(p.ws_qlow + (size_t)prob * kMaxRank + r);
     if (tid == 0) {
       misc[3] = 0;
@@ -1112,7 +1292,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
 
   // ---- phase 1 (every CTA): the exact shortlist ---------------------------------------------
   if (crank == 0 && tid == 0) stamp(p, prob, 2);
-  const int n_sl = select_shortlist(p, prob, h, t, len_t, cand, lut, sc, scratch, sl, nullptr, crank == 0);
+  const int n_sl = select_shortlist<kB>(p, prob, b, h, t, len_t, cand, lut, sc, scratch, sl, nullptr, crank == 0);
   if (crank == 0 && tid == 0) stamp(p, prob, 3);
   // CTA 0's candidate area and rank keys are written by the other CTAs below: arrive now, wait
   // before writing
@@ -1127,8 +1307,8 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
   const bool staged = p.kv_stage != 0;
   T* kst = reinterpret_cast<T*>(smem + lay.kv);  // [kv_rows][D]
   T* vst = kst + (size_t)lay.kv_rows * D;
-  const T* kb = reinterpret_cast<const T*>(p.a.keys) + kvh * p.a.k_head_stride;
-  const T* vb = reinterpret_cast<const T*>(p.a.values) + kvh * p.a.v_head_stride;
+  const T* kb = keys_base<T, kB>(p, b, kvh);
+  const T* vb = values_base<T, kB>(p, b, kvh);
   // the K/V gathers of the slice, issued while the k_low rows of the rescore are in flight
   auto gather_kv = [&]() {
     if (staged) {
@@ -1138,15 +1318,15 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
         const int q = tid % cpr, step = blockDim.x / cpr;
         for (int jj = tid / cpr; jj < nj; jj += step) {
           const int64_t key = mine[jj];
-          cp_async16(kst + jj * D + q * kPer, kb + key * p.a.k_row_stride + q * kPer);
-          cp_async16(vst + jj * D + q * kPer, vb + key * p.a.v_row_stride + q * kPer);
+          cp_async16(kst + jj * D + q * kPer, key_row<T, kB>(p, kb, b, key, p.k_page_stride, p.a.k_row_stride) + q * kPer);
+          cp_async16(vst + jj * D + q * kPer, key_row<T, kB>(p, vb, b, key, p.v_page_stride, p.a.v_row_stride) + q * kPer);
         }
       } else {
         for (int e = tid; e < nj * cpr; e += blockDim.x) {
           const int jj = e / cpr, q = e - jj * cpr;
           const int64_t key = mine[jj];
-          cp_async16(kst + jj * D + q * kPer, kb + key * p.a.k_row_stride + q * kPer);
-          cp_async16(vst + jj * D + q * kPer, vb + key * p.a.v_row_stride + q * kPer);
+          cp_async16(kst + jj * D + q * kPer, key_row<T, kB>(p, kb, b, key, p.k_page_stride, p.a.k_row_stride) + q * kPer);
+          cp_async16(vst + jj * D + q * kPer, key_row<T, kB>(p, vb, b, key, p.v_page_stride, p.a.v_row_stride) + q * kPer);
         }
       }
       asm volatile("cp.async.commit_group;\n" ::: "memory");
@@ -1156,13 +1336,15 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
       for (int e = tid; e < nj * lines; e += blockDim.x) {
         const int j = e / lines, o = (e - j * lines) * 128;
         const int64_t key = mine[j];
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(kb + key * p.a.k_row_stride) + o));
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(vb + key * p.a.v_row_stride) + o));
+        const T* kr = key_row<T, kB>(p, kb, b, key, p.k_page_stride, p.a.k_row_stride);
+        const T* vr = key_row<T, kB>(p, vb, b, key, p.v_page_stride, p.a.v_row_stride);
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(kr) + o));
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(vr) + o));
       }
     }
   };
   for (int jj = tid; jj < nj; jj += blockDim.x) fmark[jj] = 0;  // set by CTA 0 in phase 3
-  rescore_rows<8>(p, h, ql, mine, nj, rk, gather_kv);
+  rescore_rows<8, kB>(p, b, h, ql, mine, nj, rk, gather_kv);
   uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
   for (int jj = tid; jj < nj; jj += blockDim.x) {
     kmin = min(kmin, rk[jj]);
@@ -1175,8 +1357,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
     __syncthreads();
     verify_logits<T, true>(kst, 0, D, 0, qf, D, nullptr, nj, p.a.softmax_scale, p.a.logits_mode, olg);
   } else {
-    verify_logits<T>(p.a.keys, p.a.k_head_stride, p.a.k_row_stride, kvh, qf, D, mine, nj, p.a.softmax_scale,
-                     p.a.logits_mode, olg);
+    verify_logits_fn<T>(k_rows<T, kB>(p, b, kvh, mine), qf, D, nj, p.a.softmax_scale, p.a.logits_mode, olg);
   }
   cluster_wait();
   {
@@ -1197,12 +1378,12 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
 
   // ---- phase 3 (CTA 0): budget select, final marks, softmax statistics ----------------------
   if (crank == 0) {
-    const int b = min(p.b_cap, n_sl);
+    const int nb = min(p.b_cap, n_sl);
     unsigned long long* c64 = reinterpret_cast<unsigned long long*>(cand);
     const float* lgs = reinterpret_cast<const float*>(c64 + n_sl);
     for (int j = tid; j < n_sl; j += blockDim.x) c64[j] = composite(rk[j], static_cast<uint32_t>(sl[j]));
     __syncthreads();
-    const SelectThreshold thr = select_u64(c64, n_sl, b, key_to_float(static_cast<uint32_t>(misc[6])),
+    const SelectThreshold thr = select_u64(c64, n_sl, nb, key_to_float(static_cast<uint32_t>(misc[6])),
                                            key_to_float(static_cast<uint32_t>(misc[7])), sc);
     const int n_fin = compact_u64(c64, n_sl, thr, fin, scratch);  // fin[pos] = shortlist position
     for (int pos = tid; pos < n_fin; pos += blockDim.x) {
@@ -1243,7 +1424,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
     if (staged)
       accumulate_rows<T, true>(vst, 0, D, 0, D, orow, wt, n_my, acc, sums);
     else
-      accumulate_rows<T>(p.a.values, p.a.v_head_stride, p.a.v_row_stride, kvh, D, orow, wt, n_my, acc, sums);
+      accumulate_rows_fn<T>(v_rows<T, kB>(p, b, kvh, orow), D, wt, n_my, acc, sums);
     double* parts0 = cluster.map_shared_rank(parts, 0);
     for (int d = tid; d < D; d += blockDim.x) parts0[crank * D + d] = sums[d];
     if (crank == 0 && tid == 0) stamp(p, prob, 6);
@@ -1252,7 +1433,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
 
     // ---- phase 5 (CTA 0): merge, outputs, counters ------------------------------------------
     if (crank == 0) {
-      T* out = reinterpret_cast<T*>(p.a.out) + h * p.a.out_head_stride + t * p.a.out_row_stride;
+      T* out = out_row<T, kB>(p, b, h, t);
       for (int d = tid; d < D; d += blockDim.x) {
         double tot = 0.0;
         for (int c = 0; c < kCluster; ++c) tot += parts[c * D + d];
@@ -1269,6 +1450,128 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
       }
       if (tid == 0) stamp(p, prob, 8);
     }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// wide finish: one CTA per problem, for launches with many problems
+// ---------------------------------------------------------------------------------------
+// The cluster finish above spreads one problem over kCluster CTAs of kThreads threads, which
+// minimises the latency of a single decode; with hundreds of problems per launch (batches of
+// sequences, throughput mode) it keeps a few problems resident at a time.  Here one CTA of
+// kWideThreads threads does the whole finish of its problem with a small shared-memory
+// footprint, so several problems share each SM and the gathers of many problems overlap:
+// shortlist select, rank rescore, budget select, verify -- the same steps, selections and
+// arithmetic as the cluster finish (and as the fused kernel).
+constexpr int kWideThreads = 256;
+constexpr int kWideCands = 4096;  // candidates selected in shared memory (more are streamed from L2)
+constexpr int kWideMinProblems = 64;  // problems per launch from which the wide finish is used
+
+struct WideSmem {
+  int qf, ql, sc, scratch, sl, rk, fin, lg, acc, cand, total;
+};
+
+__host__ __device__ inline WideSmem wide_smem_layout(int head_dim, int sl_cap, int b_cap, int dbg_cap) {
+  WideSmem s;
+  int o = 0;
+  // the candidate area also holds the LUT of the exact fallback (kMaxLut floats), the budget
+  // select's composites (8 bytes per shortlist key) and the debug outputs' sort buffer
+  int cand = kWideCands;
+  if (cand * 2 < kMaxLut) cand = kMaxLut / 2;
+  if (cand < sl_cap) cand = sl_cap;
+  if (cand < dbg_cap) cand = dbg_cap;
+  s.qf = o;      o = align16(o + 4 * head_dim);
+  s.ql = o;      o = align16(o + 4 * kMaxRank);
+  s.sc = o;      o = align16(o + (int)sizeof(SelectScratch));
+  s.scratch = o; o = align16(o + 4 * 64);
+  s.sl = o;      o = align16(o + 4 * sl_cap);
+  s.rk = o;      o = align16(o + 4 * sl_cap);
+  s.fin = o;     o = align16(o + 4 * b_cap);
+  s.lg = o;      o = align16(o + 4 * b_cap);
+  s.acc = o;     o = align16(o + 8 * ((kWideThreads / 32) * 64 + kMaxHeadDim));
+  s.cand = o;    o = align16(o + 8 * cand);
+  s.total = o;
+  return s;
+}
+
+template <typename T, bool kB>
+__global__ void __launch_bounds__(kWideThreads, 3) decode_finish_wide_kernel(const DecodeParams p, const WideSmem lay) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  float* qf = reinterpret_cast<float*>(smem + lay.qf);
+  float* ql = reinterpret_cast<float*>(smem + lay.ql);
+  SelectScratch* sc = reinterpret_cast<SelectScratch*>(smem + lay.sc);
+  int* scratch = reinterpret_cast<int*>(smem + lay.scratch);
+  int32_t* sl = reinterpret_cast<int32_t*>(smem + lay.sl);
+  uint32_t* rk = reinterpret_cast<uint32_t*>(smem + lay.rk);
+  int32_t* fin = reinterpret_cast<int32_t*>(smem + lay.fin);
+  float* lg = reinterpret_cast<float*>(smem + lay.lg);
+  double* acc = reinterpret_cast<double*>(smem + lay.acc);
+  uint2* cand = reinterpret_cast<uint2*>(smem + lay.cand);
+  float* lut = reinterpret_cast<float*>(smem + lay.cand);  // only for the exact fallback
+
+  const int prob = blockIdx.x;
+  const ProbIdx pi = prob_index<kB>(p, prob);
+  const int b = pi.b, h = pi.h, t = pi.t;
+  const int kvh = h / p.groups;
+  const int64_t len_t = allowed_length<kB>(p, b, t);
+  const int D = p.a.head_dim;
+  const int tid = threadIdx.x;
+  {
+    const T* q = query_row<T, kB>(p, b, h, t);
+    pdl_launch_dependents();
+    if (p.q_host)
+      for (int d = tid; d < D; d += blockDim.x) qf[d] = to_f32<T>(q[d]);
+    pdl_wait();  // the scan's candidates (and prep's q_low)
+    if (!p.q_host)
+      for (int d = tid; d < D; d += blockDim.x) qf[d] = to_f32<T>(q[d]);
+    for (int r = tid; r < p.a.rank_dim; r += blockDim.x) ql[r] = __ldcg(p.ws_qlow + (size_t)prob * kMaxRank + r);
+  }
+  __syncthreads();
+  const int n_sl =
+      select_shortlist<kB>(p, prob, b, h, t, len_t, cand, lut, sc, scratch, sl, nullptr, true, kWideCands);
+  rescore_rows<8, kB>(p, b, h, ql, sl, n_sl, rk);
+  // budget select over (rank key, key index) composites with the known rank-key range
+  uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
+  unsigned long long* c64 = reinterpret_cast<unsigned long long*>(cand);
+  for (int j = tid; j < n_sl; j += blockDim.x) {
+    kmin = min(kmin, rk[j]);
+    kmax = max(kmax, rk[j]);
+    c64[j] = composite(rk[j], static_cast<uint32_t>(sl[j]));
+  }
+  kmin = __reduce_min_sync(0xFFFFFFFFu, kmin);
+  kmax = __reduce_max_sync(0xFFFFFFFFu, kmax);
+  if ((tid & 31) == 0) {
+    sc->lo_part[tid >> 5] = kmin;
+    sc->hi_part[tid >> 5] = kmax;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    uint32_t a = 0xFFFFFFFFu, c = 0u;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+      a = min(a, static_cast<uint32_t>(sc->lo_part[w]));
+      c = max(c, static_cast<uint32_t>(sc->hi_part[w]));
+    }
+    scratch[0] = static_cast<int>(a);
+    scratch[1] = static_cast<int>(c);
+  }
+  __syncthreads();
+  const float lo = key_to_float(static_cast<uint32_t>(scratch[0])), hi = key_to_float(static_cast<uint32_t>(scratch[1]));
+  __syncthreads();
+  const int nb = min(p.b_cap, n_sl);
+  const SelectThreshold thr = select_u64(c64, n_sl, nb, lo, hi, sc);
+  const int n_fin = compact_u64(c64, n_sl, thr, fin, scratch);  // shortlist positions
+  for (int pos = tid; pos < n_fin; pos += blockDim.x) fin[pos] = sl[fin[pos]];
+  __syncthreads();
+  verify_rows_fn<T>(k_rows<T, kB>(p, b, kvh, fin), v_rows<T, kB>(p, b, kvh, fin), qf, D, n_fin, p.a.softmax_scale,
+                    p.a.logits_mode, lg, acc, scratch, out_row<T, kB>(p, b, h, t));
+  unsigned long long* tmp = reinterpret_cast<unsigned long long*>(cand);
+  if (p.a.shortlist_out) write_sorted(sl, n_sl, p.a.shortlist, p.a.shortlist_out + (size_t)prob * p.a.shortlist, tmp);
+  if (p.a.final_out) write_sorted(fin, n_fin, p.a.budget, p.a.final_out + (size_t)prob * p.a.budget, tmp);
+  if (p.a.stats && tid == 0) {
+    atomicAdd(p.a.stats + SVA_STAT_QUERIES, 1ull);
+    atomicAdd(p.a.stats + SVA_STAT_SUMMONED, static_cast<unsigned long long>(n_sl));
+    atomicAdd(p.a.stats + SVA_STAT_EXACT_SCORED, static_cast<unsigned long long>(n_fin));
+    atomicAdd(p.a.stats + SVA_STAT_VERIFIED, static_cast<unsigned long long>(n_fin));
   }
 }
 
@@ -1302,11 +1605,14 @@ static bool pow2_float(double x) {
 struct DecodePlan {
   DecodeParams p;
   FinishSmem fin_lay;
+  WideSmem wide_lay;
+  bool wide;  // one-CTA-per-problem finish (many problems per launch)
   size_t ws_bytes;
   size_t smem_bytes;
 };
 
-static int plan_decode(const sva_decode_args* a, DecodePlan* plan, bool force_grid = false) {
+static int plan_decode(const sva_decode_args* a, DecodePlan* plan, bool force_grid = false,
+                       const sva_batch_layout* layout = nullptr) {
   if (!a) return set_error(SVA_ERR_SHAPE, "null args");
   if (a->n_heads <= 0 || a->n_kv_heads <= 0 || a->n_heads % a->n_kv_heads != 0)
     return set_error(SVA_ERR_SHAPE, "n_heads must be a positive multiple of n_kv_heads");
@@ -1334,21 +1640,69 @@ static int plan_decode(const sva_decode_args* a, DecodePlan* plan, bool force_gr
   p.sqrt_r_pow2 = pow2_float(static_cast<double>(p.sqrt_r)) ? 1 : 0;
   p.inv_sqrt_r = 1.0f / p.sqrt_r;
   p.sl_cap = static_cast<int>(std::min<int64_t>(a->shortlist, a->key_len));
+  // batch layout: one unpaged sequence unless a layout is given
+  p.n_seqs = 1;
+  p.page_shift = 62;
+  p.page_mask = (int64_t{1} << 62) - 1;
+  if (layout) {
+    if (layout->n_seqs <= 0) return set_error(SVA_ERR_SHAPE, "n_seqs must be positive");
+    p.batched = 1;
+    p.n_seqs = layout->n_seqs;
+    p.seq_lens = layout->seq_lens;
+    p.q_seq_stride = layout->q_seq_stride;
+    p.out_seq_stride = layout->out_seq_stride;
+    p.codes_page_stride = layout->codes_page_stride;
+    p.k_low_page_stride = layout->k_low_page_stride;
+    p.k_page_stride = layout->k_page_stride;
+    p.v_page_stride = layout->v_page_stride;
+    if (layout->page_table) {
+      const int pk = layout->page_keys;
+      if (pk < kMinPageKeys || pk > kScanKeys || (pk & (pk - 1)) != 0)
+        return set_error(SVA_ERR_SHAPE, "page_keys must be a power of two in 64..32768");
+      if (layout->page_table_stride < (a->key_len + pk - 1) / pk)
+        return set_error(SVA_ERR_SHAPE, "page_table_stride must cover key_len / page_keys pages");
+      p.page_table = layout->page_table;
+      p.pt_stride = layout->page_table_stride;
+      p.page_shift = 0;
+      while ((1 << p.page_shift) < pk) ++p.page_shift;
+      p.page_mask = pk - 1;
+    }
+  }
   {
+    const int64_t np = static_cast<int64_t>(p.n_seqs) * a->n_heads * a->n_queries;
+    if (np > 0x7FFFFFF) return set_error(SVA_ERR_SHAPE, "n_seqs * n_heads * n_queries is too large");
+    p.n_probs = static_cast<int>(np);
+  }
+  {
+    // page-locked host buffers are read / written in place only where the device address of
+    // the mapping is the host address itself (sva_host_buffer_device_accessible)
     cudaPointerAttributes attr;
-    if (cudaPointerGetAttributes(&attr, a->query) == cudaSuccess) p.q_host = attr.type == cudaMemoryTypeHost ? 1 : 0;
-    else cudaGetLastError();
+    if (cudaPointerGetAttributes(&attr, a->query) == cudaSuccess) {
+      if (attr.type == cudaMemoryTypeHost && attr.devicePointer != a->query)
+        return set_error(SVA_ERR_SHAPE, "query is host memory that the device cannot address at the same pointer");
+      p.q_host = attr.type == cudaMemoryTypeHost ? 1 : 0;
+    } else {
+      cudaGetLastError();
+    }
+    if (cudaPointerGetAttributes(&attr, a->out) == cudaSuccess) {
+      if (attr.type == cudaMemoryTypeHost && attr.devicePointer != a->out)
+        return set_error(SVA_ERR_SHAPE, "out is host memory that the device cannot address at the same pointer");
+    } else {
+      cudaGetLastError();
+    }
   }
   p.b_cap = std::min(a->budget, p.sl_cap);
   const int S = a->subspaces;
   const bool vec_s = (S == 1 || S == 2 || S == 4 || S == 8);
   const uintptr_t align = static_cast<uintptr_t>(4 * S);
   p.vec_codes = (vec_s && (reinterpret_cast<uintptr_t>(a->codes) % align == 0) &&
-                 (a->codes_head_stride % (4 * S)) == 0)
+                 (a->codes_head_stride % (4 * S)) == 0 && (p.codes_page_stride % (4 * S)) == 0)
                     ? 1
                     : 0;
-  const int64_t P = static_cast<int64_t>(a->n_heads) * a->n_queries;
+  const int64_t P = p.n_probs;
   p.grid_mode = (force_grid || a->key_len > kFusedMaxKeys) ? 1 : 0;
+  if (p.grid_mode && P > 65535)
+    return set_error(SVA_ERR_SHAPE, "over 32768 keys, n_seqs * n_heads * n_queries must be <= 65535 per call");
   p.nseg = static_cast<int>((a->key_len + kScanKeys - 1) / kScanKeys);
   int dbg_cap = 1;
   if (a->shortlist_out || a->final_out)
@@ -1367,13 +1721,18 @@ static int plan_decode(const sva_decode_args* a, DecodePlan* plan, bool force_gr
     const int row_bytes = a->head_dim * esz;
     const bool aligned = (row_bytes % 16 == 0) && ((a->k_row_stride * esz) % 16 == 0) &&
                          ((a->v_row_stride * esz) % 16 == 0) && ((a->k_head_stride * esz) % 16 == 0) &&
-                         ((a->v_head_stride * esz) % 16 == 0) && (reinterpret_cast<uintptr_t>(a->keys) % 16 == 0) &&
+                         ((a->v_head_stride * esz) % 16 == 0) && ((p.k_page_stride * esz) % 16 == 0) &&
+                         ((p.v_page_stride * esz) % 16 == 0) && (reinterpret_cast<uintptr_t>(a->keys) % 16 == 0) &&
                          (reinterpret_cast<uintptr_t>(a->values) % 16 == 0);
     plan->fin_lay = finish_smem_layout(a->head_dim, p.sl_cap, p.b_cap, cand_entries, aligned ? row_bytes : 0);
     if (plan->fin_lay.total > kMaxDynSmem - 1024)
       plan->fin_lay = finish_smem_layout(a->head_dim, p.sl_cap, p.b_cap, cand_entries, 0);
     p.kv_stage = plan->fin_lay.kv_rows > 0 ? 1 : 0;
     plan->smem_bytes = static_cast<size_t>(plan->fin_lay.total);
+    // with many problems per launch, one CTA per problem keeps more problems in flight than
+    // one cluster per problem
+    plan->wide_lay = wide_smem_layout(a->head_dim, p.sl_cap, p.b_cap, dbg_cap);
+    plan->wide = P >= kWideMinProblems && plan->wide_lay.total <= kMaxDynSmem;
     auto take = [&](size_t bytes) {
       size_t o = ws;
       ws = (ws + bytes + 255) & ~static_cast<size_t>(255);
@@ -1398,7 +1757,8 @@ constexpr int scan_lut_bytes() {
 template <int S, int C>
 static int launch_scan(const DecodeParams& p, int P, cudaStream_t stream) {
   constexpr int smem = scan_lut_bytes<S, C>();
-  auto k = p.sqrt_r_pow2 ? decode_scan_kernel<S, C, true> : decode_scan_kernel<S, C, false>;
+  auto k = p.page_table ? (p.sqrt_r_pow2 ? decode_scan_kernel<S, C, true, true> : decode_scan_kernel<S, C, false, true>)
+                        : (p.sqrt_r_pow2 ? decode_scan_kernel<S, C, true, false> : decode_scan_kernel<S, C, false, false>);
   const int rc = ensure_smem_attr(reinterpret_cast<const void*>(k), smem);
   if (rc != SVA_OK) return rc;
   const cudaError_t e = launch_dependent(k, dim3(p.nseg, P), dim3(kScanThreads), smem, stream, p);
@@ -1407,10 +1767,10 @@ static int launch_scan(const DecodeParams& p, int P, cudaStream_t stream) {
 
 template <typename T, int S>
 static int launch_prep(const DecodeParams& p, int P, const PrepSmem& lay, cudaStream_t stream) {
-  int rc = ensure_smem_attr(reinterpret_cast<const void*>(decode_prep_kernel<T, S>), lay.total);
+  auto k = p.batched ? decode_prep_kernel<T, S, true> : decode_prep_kernel<T, S, false>;
+  int rc = ensure_smem_attr(reinterpret_cast<const void*>(k), lay.total);
   if (rc != SVA_OK) return rc;
-  const cudaError_t e =
-      launch_dependent(decode_prep_kernel<T, S>, dim3(P * kPrepCtas), dim3(kThreads), lay.total, stream, p, lay);
+  const cudaError_t e = launch_dependent(k, dim3(P * kPrepCtas), dim3(kThreads), lay.total, stream, p, lay);
   return e == cudaSuccess ? SVA_OK : set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
 }
 
@@ -1426,7 +1786,7 @@ static void bind_workspace(DecodeParams& p, void* ws) {
 // The grid schedule's prep and scan launches (q_low, LUT, threshold, candidates).
 template <typename T>
 static int launch_prep_scan(DecodeParams& p, cudaStream_t stream) {
-  const int P = p.a.n_heads * p.a.n_queries;
+  const int P = p.n_probs;
   int rc;
   const int D = p.a.head_dim, R = p.a.rank_dim, C = p.a.codewords, S = p.a.subspaces;
   const bool prep_vec = p.vec_codes && prep_smem_layout(D, R, C, S, false).total <= kPrepSmemLimit;
@@ -1457,22 +1817,31 @@ static int launch_prep_scan(DecodeParams& p, cudaStream_t stream) {
 template <typename T>
 static int launch_decode(DecodePlan& plan, void* ws, cudaStream_t stream) {
   DecodeParams& p = plan.p;
-  const int P = p.a.n_heads * p.a.n_queries;
+  const int P = p.n_probs;
   int rc;
   if (!p.grid_mode) {
-    rc = ensure_smem_attr(reinterpret_cast<const void*>(decode_fused_kernel<T>), kMaxDynSmem);
+    auto fk = p.batched ? decode_fused_kernel<T, true> : decode_fused_kernel<T, false>;
+    rc = ensure_smem_attr(reinterpret_cast<const void*>(fk), kMaxDynSmem);
     if (rc != SVA_OK) return rc;
-    decode_fused_kernel<T><<<P, kThreads, plan.smem_bytes, stream>>>(p);
+    fk<<<P, kThreads, plan.smem_bytes, stream>>>(p);
     profile_mark(0, stream);
   } else {
     bind_workspace(p, ws);
     p.dbg_ts = static_cast<unsigned long long*>(debug_timestamps());
     rc = launch_prep_scan<T>(p, stream);
     if (rc != SVA_OK) return rc;
-    rc = ensure_smem_attr(reinterpret_cast<const void*>(decode_finish_kernel<T>), static_cast<int>(plan.smem_bytes));
-    if (rc != SVA_OK) return rc;
-    cudaError_t le = launch_dependent(decode_finish_kernel<T>, dim3(P * kCluster), dim3(kThreads), plan.smem_bytes,
-                                      stream, p, plan.fin_lay);
+    cudaError_t le;
+    if (plan.wide) {
+      auto wk = p.batched ? decode_finish_wide_kernel<T, true> : decode_finish_wide_kernel<T, false>;
+      rc = ensure_smem_attr(reinterpret_cast<const void*>(wk), plan.wide_lay.total);
+      if (rc != SVA_OK) return rc;
+      le = launch_dependent(wk, dim3(P), dim3(kWideThreads), plan.wide_lay.total, stream, p, plan.wide_lay);
+    } else {
+      auto nk = p.batched ? decode_finish_kernel<T, true> : decode_finish_kernel<T, false>;
+      rc = ensure_smem_attr(reinterpret_cast<const void*>(nk), static_cast<int>(plan.smem_bytes));
+      if (rc != SVA_OK) return rc;
+      le = launch_dependent(nk, dim3(P * kCluster), dim3(kThreads), plan.smem_bytes, stream, p, plan.fin_lay);
+    }
     if (le != cudaSuccess) return set_error(SVA_ERR_CUDA, cudaGetErrorString(le));
     profile_mark(2, stream);
   }
@@ -1495,6 +1864,28 @@ extern "C" int sva_decode(const sva_decode_args* args, void* workspace, size_t w
   if (rc != SVA_OK) return rc;
   if (workspace_bytes < plan.ws_bytes || (plan.ws_bytes > 0 && workspace == nullptr))
     return sva::set_error(SVA_ERR_WORKSPACE, "workspace smaller than sva_decode_workspace_size()");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (args->qkv_dtype) {
+    case SVA_DTYPE_F32: return sva::launch_decode<float>(plan, workspace, s);
+    case SVA_DTYPE_BF16: return sva::launch_decode<__nv_bfloat16>(plan, workspace, s);
+    default: return sva::launch_decode<__half>(plan, workspace, s);
+  }
+}
+
+extern "C" size_t sva_decode_batched_workspace_size(const sva_decode_args* args, const sva_batch_layout* layout) {
+  sva::DecodePlan plan;
+  if (!layout || sva::plan_decode(args, &plan, false, layout) != SVA_OK) return 0;
+  return plan.ws_bytes;
+}
+
+extern "C" int sva_decode_batched(const sva_decode_args* args, const sva_batch_layout* layout, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  if (!layout) return sva::set_error(SVA_ERR_SHAPE, "layout is null");
+  sva::DecodePlan plan;
+  int rc = sva::plan_decode(args, &plan, false, layout);
+  if (rc != SVA_OK) return rc;
+  if (workspace_bytes < plan.ws_bytes || (plan.ws_bytes > 0 && workspace == nullptr))
+    return sva::set_error(SVA_ERR_WORKSPACE, "workspace smaller than sva_decode_batched_workspace_size()");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (args->qkv_dtype) {
     case SVA_DTYPE_F32: return sva::launch_decode<float>(plan, workspace, s);

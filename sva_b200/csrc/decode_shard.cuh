@@ -38,12 +38,12 @@ __global__ void __launch_bounds__(kThreads)
   __shared__ int scratch[64];
   const int prob = blockIdx.x;
   const int h = prob / p.a.n_queries, t = prob - h * p.a.n_queries;
-  const int64_t len_t = allowed_length(p, t);
+  const int64_t len_t = allowed_length<false>(p, 0, t);
   const int SL = p.a.shortlist;
   unsigned long long* out = top_out + (size_t)prob * SL;
   const uint32_t off = static_cast<uint32_t>(key_offset);
   int32_t* idx = reinterpret_cast<int32_t*>(smem + kCandSmem * sizeof(uint2));  // SL entries
-  const int n = select_shortlist(p, prob, h, t, len_t, cand, lut, &sc, scratch, idx, out, true);
+  const int n = select_shortlist<false>(p, prob, 0, h, t, len_t, cand, lut, &sc, scratch, idx, out, true);
   for (int j = threadIdx.x; j < SL; j += blockDim.x)
     out[j] = j < n ? composite(static_cast<uint32_t>(out[j] >> 32), static_cast<uint32_t>(idx[j]) + off) : 0ull;
 }
@@ -88,7 +88,7 @@ __global__ void __launch_bounds__(kThreads)
   const int prob = blockIdx.x;
   const int h = prob / p.a.n_queries, t = prob - h * p.a.n_queries;
   const int kvh = h / p.groups;
-  const int P = p.a.n_heads * p.a.n_queries;
+  const int P = p.n_probs;
   const int tid = threadIdx.x;
   {
     const T* q = reinterpret_cast<const T*>(p.a.query) + h * p.a.q_head_stride + t * p.a.q_row_stride;
@@ -104,7 +104,7 @@ __global__ void __launch_bounds__(kThreads)
   const SelectThreshold thr = cta_radix_select(item, N, k, &sc);
   const GatheredTop own{gathered, P, SL, prob, rank * SL};
   const int m = cta_compact(own, SL, thr, OwnShortlistEmit{rows, gidx, static_cast<uint32_t>(key_offset)}, scratch);
-  rescore_rows<8>(p, h, ql, rows, m, rk);
+  rescore_rows<8, false>(p, 0, h, ql, rows, m, rk);
   verify_logits<T>(p.a.keys, p.a.k_head_stride, p.a.k_row_stride, kvh, qf, p.a.head_dim, rows, m, p.a.softmax_scale,
                    p.a.logits_mode, lg);
   uint4* out = records + (size_t)prob * SL;
@@ -135,7 +135,7 @@ __global__ void __launch_bounds__(kThreads)
   const int prob = blockIdx.x;
   const int h = prob / p.a.n_queries, t = prob - h * p.a.n_queries;
   const int kvh = h / p.groups;
-  const int P = p.a.n_heads * p.a.n_queries;
+  const int P = p.n_probs;
   const int SL = p.a.shortlist;
   const int D = p.a.head_dim;
   const int tid = threadIdx.x;
@@ -183,7 +183,7 @@ template <typename T>
 __global__ void shard_combine_kernel(const DecodeParams p, int world, const double* __restrict__ gathered) {
   const int prob = blockIdx.x;
   const int h = prob / p.a.n_queries, t = prob - h * p.a.n_queries;
-  const int P = p.a.n_heads * p.a.n_queries;
+  const int P = p.n_probs;
   const int D = p.a.head_dim;
   T* out = reinterpret_cast<T*>(p.a.out) + h * p.a.out_head_stride + t * p.a.out_row_stride;
   for (int d = threadIdx.x; d < D; d += blockDim.x) {

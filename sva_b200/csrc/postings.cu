@@ -184,7 +184,42 @@ static __device__ __align__(256) unsigned char g_postings_scratch[SVA_POSTINGS_N
 namespace {
 constexpr int kTrackedDevices = 64;
 std::mutex g_postings_scratch_mu;
-void* g_postings_scratch_addr[kTrackedDevices] = {};
+// Per device ordinal: the buffer's device address and the id of the context it was looked up
+// in.  A device address is only valid in its own context, so the address is looked up again
+// when the calling thread's current context is another one (after cudaDeviceReset, or under a
+// context the caller created with the driver API).
+struct ScratchAddr {
+  unsigned long long ctx_id;
+  void* addr;
+};
+ScratchAddr g_postings_scratch_addr[kTrackedDevices] = {};
+
+using CtxGetCurrentFn = int (*)(void**);
+using CtxGetIdFn = int (*)(void*, unsigned long long*);
+
+// Unique id of the calling thread's current CUDA context (0 if it cannot be read).  The driver
+// entry points come through the runtime, so the library needs no link to the driver library.
+unsigned long long current_context_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(f);
+    f = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(f);
+    cudaGetLastError();
+  });
+  void* ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current && get_id && get_current(&ctx) == 0 && ctx && get_id(ctx, &id) == 0) return id;
+  return 0;
+}
 }  // namespace
 
 extern "C" int sva_postings_build_noalloc(const uint8_t* codes, int64_t codes_head_stride, int32_t n_heads,
@@ -200,15 +235,20 @@ extern "C" int sva_postings_build_noalloc(const uint8_t* codes, int64_t codes_he
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
     if (dev < 0 || dev >= kTrackedDevices) return set_error(SVA_ERR_CUDA, "device ordinal out of range");
+    // 0 before the runtime has made a context current: the address is then looked up on every
+    // call until one is (the lookup itself initialises the context and loads the module)
+    const unsigned long long ctx = current_context_id();
     std::lock_guard<std::mutex> lock(g_postings_scratch_mu);
-    if (!g_postings_scratch_addr[dev]) {
+    ScratchAddr& slot = g_postings_scratch_addr[dev];
+    if (!slot.addr || ctx == 0 || slot.ctx_id != ctx) {
       void* addr = nullptr;
-      e = cudaGetSymbolAddress(&addr, g_postings_scratch);  // resolved on the current device
+      e = cudaGetSymbolAddress(&addr, g_postings_scratch);  // resolved in the current context
       if (e != cudaSuccess || addr == nullptr)
         return set_error(SVA_ERR_CUDA, e != cudaSuccess ? cudaGetErrorString(e) : "null scratch address");
-      g_postings_scratch_addr[dev] = addr;
+      slot.addr = addr;
+      slot.ctx_id = ctx;
     }
-    scratch = g_postings_scratch_addr[dev];
+    scratch = slot.addr;
   }
   return sva_postings_build(codes, codes_head_stride, n_heads, subspaces, codewords, key_len, counts, offsets, ids,
                             ids_sub_stride, max_bucket, scratch, need, stream);

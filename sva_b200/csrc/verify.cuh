@@ -19,18 +19,36 @@ namespace sva {
 
 constexpr int kVerifyUnroll = 8;
 
-// `rows` are key indices; NULL means rows 0..n-1.  `values` (optional): the V rows of the same
-// keys are prefetched into L2 while the K rows load, so that the weighted sum that follows reads
-// them from L2.
+// Row addressing of the verify functions: row(j) is the address of the j-th selected key's K
+// (or V) row.  StridedRows covers one head of a [heads][keys][D] cache with arbitrary strides;
+// the decode kernels pass their own functors for paged and batched caches.
+template <typename T>
+struct StridedRows {
+  const T* base;        // the head's row 0
+  int64_t row_stride;   // elements
+  const int32_t* rows;  // key indices, or NULL for rows 0..n-1
+  __device__ __forceinline__ const T* operator()(int j) const { return base + (int64_t)(rows ? rows[j] : j) * row_stride; }
+};
+
+template <typename T>
+__device__ __forceinline__ StridedRows<T> strided_rows(const void* base, int64_t head_stride, int64_t row_stride,
+                                                        int kvh, const int32_t* rows) {
+  return StridedRows<T>{reinterpret_cast<const T*>(base) + kvh * head_stride, row_stride, rows};
+}
+
+struct NoPrefetch {
+  __device__ __forceinline__ const void* operator()(int) const { return nullptr; }
+};
+
+// logits of n selected keys: lg[j] = q . K[row(j)] * softmax_scale (see the file comment).
+// `vrow` (optional): the V rows of the same keys are prefetched into L2 while the K rows load,
+// so that the weighted sum that follows reads them from L2.
 // kShared: the rows live in shared memory (staged copies), read with plain loads.
-template <typename T, bool kShared = false>
-__device__ void verify_logits(const void* keys, int64_t k_head_stride, int64_t k_row_stride, int kvh, const float* qf,
-                              int D, const int32_t* rows, int n, float softmax_scale, int logits_mode, float* lg,
-                              const void* values = nullptr, int64_t v_head_stride = 0, int64_t v_row_stride = 0) {
+template <typename T, bool kShared = false, class KRow, class VRow = NoPrefetch>
+__device__ void verify_logits_fn(const KRow& krow, const float* qf, int D, int n, float softmax_scale,
+                                 int logits_mode, float* lg, const VRow& vrow = VRow(), bool prefetch_v = false) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   const int half = lane >> 4, l16 = lane & 15;
-  const T* kb = reinterpret_cast<const T*>(keys) + kvh * k_head_stride;
-  const T* vb = values ? reinterpret_cast<const T*>(values) + kvh * v_head_stride : nullptr;
   constexpr int U = kVerifyUnroll;
   for (int base = warp * 2 * U; base < n; base += nwarps * 2 * U) {
     float part[U];
@@ -43,19 +61,19 @@ __device__ void verify_logits(const void* keys, int64_t k_head_stride, int64_t k
       for (int u = 0; u < U; ++u) {
         const int j = base + 2 * u + half;
         if (j < n && e < D) {
-          const T* kr = kb + (int64_t)(rows ? rows[j] : j) * k_row_stride;
+          const T* kr = krow(j);
           k4[u] = kShared ? load4s<T>(kr, e, D) : load4<T>(kr, e, D);
         } else {
           k4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
       }
-      if (vb) {
+      if (prefetch_v) {
         // one prefetch per 128-byte line of each row's chunk: lanes l16 = 0, 8 of every half-warp
 #pragma unroll
         for (int u = 0; u < U; ++u) {
           const int j = base + 2 * u + half;
           if (j < n && e < D && ((e * static_cast<int>(sizeof(T))) & 127) == 0)
-            asm volatile("prefetch.global.L2 [%0];" ::"l"(vb + (int64_t)rows[j] * v_row_stride + e));
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const T*>(vrow(j)) + e));
         }
       }
       const float4 qv = (e < D) ? make_float4(qf[e], (e + 1 < D) ? qf[e + 1] : 0.f, (e + 2 < D) ? qf[e + 2] : 0.f,
@@ -88,6 +106,21 @@ __device__ void verify_logits(const void* keys, int64_t k_head_stride, int64_t k
     }
   }
   __syncthreads();
+}
+
+// The same over one head of a strided cache; `rows` are key indices, NULL means rows 0..n-1.
+// `values` (optional): prefetch the V rows of the same keys into L2.
+template <typename T, bool kShared = false>
+__device__ void verify_logits(const void* keys, int64_t k_head_stride, int64_t k_row_stride, int kvh, const float* qf,
+                              int D, const int32_t* rows, int n, float softmax_scale, int logits_mode, float* lg,
+                              const void* values = nullptr, int64_t v_head_stride = 0, int64_t v_row_stride = 0) {
+  const StridedRows<T> kr = strided_rows<T>(keys, k_head_stride, k_row_stride, kvh, rows);
+  if (values) {
+    const StridedRows<T> vr = strided_rows<T>(values, v_head_stride, v_row_stride, kvh, rows);
+    verify_logits_fn<T, kShared>(kr, qf, D, n, softmax_scale, logits_mode, lg, vr, true);
+  } else {
+    verify_logits_fn<T, kShared>(kr, qf, D, n, softmax_scale, logits_mode, lg);
+  }
 }
 
 // Max (fp32) and fp64 denominator of softmax over lg[0, n); every thread gets both.
@@ -132,14 +165,12 @@ __device__ void softmax_weights(float* lg, int n, float mx, float denom) {
   __syncthreads();
 }
 
-// out[d] = sum_j round_T(w[j] * V[rows[j]][d]) in fp64 for d < D (written by threads 0..63 per
+// out[d] = sum_j round_T(w[j] * V[row(j)][d]) in fp64 for d < D (written by threads 0..63 per
 // 64-wide chunk).  `acc` needs (blockDim.x / 32) * 64 doubles.
-template <typename T, bool kShared = false>
-__device__ void accumulate_rows(const void* values, int64_t v_head_stride, int64_t v_row_stride, int kvh, int D,
-                                const int32_t* rows, const float* w, int n, double* acc, double* out) {
+template <typename T, bool kShared = false, class VRow>
+__device__ void accumulate_rows_fn(const VRow& vrow, int D, const float* w, int n, double* acc, double* out) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   const int half = lane >> 4, l16 = lane & 15;
-  const T* vb = reinterpret_cast<const T*>(values) + kvh * v_head_stride;
   constexpr int U = kVerifyUnroll;
   const int nchunks = (D + 63) / 64;
   for (int c = 0; c < nchunks; ++c) {
@@ -154,7 +185,7 @@ __device__ void accumulate_rows(const void* values, int64_t v_head_stride, int64
         v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
         wu[u] = 0.f;
         if (j < n && e < D) {
-          const T* vr = vb + (int64_t)rows[j] * v_row_stride;
+          const T* vr = vrow(j);
           v[u] = kShared ? load4s<T>(vr, e, D) : load4<T>(vr, e, D);
           wu[u] = w[j];
         }
@@ -188,22 +219,37 @@ __device__ void accumulate_rows(const void* values, int64_t v_head_stride, int64
   }
 }
 
+// The same over one head of a strided cache; `rows` are key indices.
+template <typename T, bool kShared = false>
+__device__ void accumulate_rows(const void* values, int64_t v_head_stride, int64_t v_row_stride, int kvh, int D,
+                                const int32_t* rows, const float* w, int n, double* acc, double* out) {
+  accumulate_rows_fn<T, kShared>(strided_rows<T>(values, v_head_stride, v_row_stride, kvh, rows), D, w, n, acc, out);
+}
+
 // The whole verify inside one CTA.  Shared memory: lg[n_fin] floats; acc[(nwarps * 64) +
 // nwarps + 1] doubles; red[kMaxHeadDim] doubles for the output sums; scratch[64] ints.
-template <typename T>
-__device__ void verify_rows(const void* keys, int64_t k_head_stride, int64_t k_row_stride, const void* values,
-                            int64_t v_head_stride, int64_t v_row_stride, int kvh, const float* qf, int D,
-                            const int32_t* fin, int n_fin, float softmax_scale, int logits_mode, float* lg,
-                            double* acc, int* scratch, T* out) {
-  verify_logits<T>(keys, k_head_stride, k_row_stride, kvh, qf, D, fin, n_fin, softmax_scale, logits_mode, lg);
+template <typename T, class KRow, class VRow>
+__device__ void verify_rows_fn(const KRow& krow, const VRow& vrow, const float* qf, int D, int n_fin,
+                               float softmax_scale, int logits_mode, float* lg, double* acc, int* scratch, T* out) {
+  verify_logits_fn<T>(krow, qf, D, n_fin, softmax_scale, logits_mode, lg);
   float mx, denom;
   const int nwarps = blockDim.x >> 5;
   softmax_stats(lg, n_fin, scratch, acc, &mx, &denom);
   softmax_weights<T>(lg, n_fin, mx, denom);
   double* sums = acc + nwarps * 64;  // D doubles after the per-warp partials
-  accumulate_rows<T>(values, v_head_stride, v_row_stride, kvh, D, fin, lg, n_fin, acc, sums);
+  accumulate_rows_fn<T>(vrow, D, lg, n_fin, acc, sums);
   for (int d = threadIdx.x; d < D; d += blockDim.x) out[d] = from_f32<T>(n_fin > 0 ? static_cast<float>(sums[d]) : 0.f);
   __syncthreads();
+}
+
+template <typename T>
+__device__ void verify_rows(const void* keys, int64_t k_head_stride, int64_t k_row_stride, const void* values,
+                            int64_t v_head_stride, int64_t v_row_stride, int kvh, const float* qf, int D,
+                            const int32_t* fin, int n_fin, float softmax_scale, int logits_mode, float* lg,
+                            double* acc, int* scratch, T* out) {
+  verify_rows_fn<T>(strided_rows<T>(keys, k_head_stride, k_row_stride, kvh, fin),
+                    strided_rows<T>(values, v_head_stride, v_row_stride, kvh, fin), qf, D, n_fin, softmax_scale,
+                    logits_mode, lg, acc, scratch, out);
 }
 
 }  // namespace sva

@@ -241,6 +241,103 @@ def decode(q: torch.Tensor, q_proj: torch.Tensor, scale: torch.Tensor, codebooks
     return out
 
 
+def decode_batched(q: torch.Tensor, q_proj: torch.Tensor, scale: torch.Tensor, codebooks: torch.Tensor,
+                   codes: torch.Tensor, k_low: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, shortlist: int,
+                   budget: int, *, seq_lens: torch.Tensor | None = None, page_table: torch.Tensor | None = None,
+                   max_len: int | None = None, softmax_scale: float | None = None, logits_mode: int = 0,
+                   allowed_len: torch.Tensor | None = None, allowed_mask: torch.Tensor | None = None,
+                   out: torch.Tensor | None = None, want_shortlist: bool = False, want_final: bool = False,
+                   stats: torch.Tensor | None = None):
+    """Scan decode of B sequences in one call (sva_decode_batched, see include/sva_b200.h).
+
+    q [B, H, T, D]; q_proj / scale / codebooks are shared by the sequences (one layer).
+    Unpaged (``page_table`` None): codes [B, H, L, S], k_low [B, H, L, R], keys / values
+    [B, Hkv, L, D], with L the longest sequence.  Paged: codes [pages, H, page_keys, S], k_low
+    [pages, H, page_keys, R], keys / values [pages, Hkv, page_keys, D] page pools and page_table
+    [B, max_pages] int32 (page of every page_keys-key block of each sequence).  ``seq_lens`` [B]
+    int64 (device) gives each sequence's keys (None: all L, or all ``max_len``); ``max_len`` (host
+    int) bounds them (default: L, or max_pages * page_keys).  ``allowed_len`` [B, T] int64 and
+    ``allowed_mask`` [B * T, >= L] uint8 as for ``decode``.  Returns out [B, H, T, D] (and
+    shortlist / final index tensors [B, H, T, shortlist] / [B, H, T, budget] when requested).
+    """
+    for name, t in (("q", q), ("codes", codes), ("k_low", k_low), ("keys", keys), ("values", values)):
+        _cuda(t, name)
+    if q.dim() != 4 or codes.dim() != 4 or k_low.dim() != 4 or keys.dim() != 4 or values.dim() != 4:
+        raise ValueError("decode_batched takes 4-d q, codes, k_low, keys and values")
+    dev = q.device
+    n_seqs, n_heads, n_q, head_dim = q.shape
+    n_kv = int(keys.shape[1])
+    rank = int(q_proj.shape[-1])
+    if q.stride(-1) != 1 or keys.stride(-1) != 1 or values.stride(-1) != 1:
+        raise ValueError("q, keys and values must have contiguous rows")
+    if codes.dtype != torch.uint8 or codes.stride(-1) != 1 or codes.stride(-2) != codes.shape[-1]:
+        raise ValueError("codes must be uint8 with contiguous rows")
+    if k_low.dtype != torch.float32 or k_low.stride(-1) != 1 or k_low.stride(-2) != rank:
+        raise ValueError("k_low must be float32 with contiguous rows")
+    if keys.dtype != q.dtype or values.dtype != q.dtype:
+        raise TypeError("q, keys and values must share a dtype")
+    paged = page_table is not None
+    if paged:
+        _cuda(page_table, "page_table")
+        if page_table.dtype != torch.int32 or page_table.dim() != 2 or page_table.stride(-1) != 1:
+            raise ValueError("page_table must be an int32 [B, max_pages] tensor with contiguous rows")
+        page_keys = int(codes.shape[2])
+        if max_len is None:
+            max_len = int(page_table.shape[1]) * page_keys
+    else:
+        page_keys = 0
+        if max_len is None:
+            max_len = int(codes.shape[2])
+    if seq_lens is not None:
+        _cuda(seq_lens, "seq_lens")
+        if seq_lens.dtype != torch.int64 or seq_lens.numel() != n_seqs:
+            raise ValueError("seq_lens must be an int64 tensor of B entries")
+    if out is None:
+        out = torch.empty(n_seqs, n_heads, n_q, head_dim, dtype=q.dtype, device=dev)
+    a = _lib.DecodeArgs()
+    a.n_heads, a.n_kv_heads, a.n_queries, a.head_dim = n_heads, n_kv, n_q, head_dim
+    a.rank_dim, a.subspaces, a.codewords = rank, int(codebooks.shape[1]), int(codebooks.shape[2])
+    a.shortlist, a.budget = int(shortlist), int(budget)
+    a.qkv_dtype = dtype_code(q.dtype)
+    a.logits_mode = int(logits_mode)
+    a.softmax_scale = float(head_dim ** -0.5 if softmax_scale is None else softmax_scale)
+    a.key_len = int(max_len)
+    a.query, a.q_head_stride, a.q_row_stride = q.data_ptr(), q.stride(1), q.stride(2)
+    a.q_proj, a.scale, a.codebooks = q_proj.data_ptr(), scale.data_ptr(), codebooks.data_ptr()
+    a.codes, a.codes_head_stride = codes.data_ptr(), codes.stride(1)
+    a.k_low, a.k_low_head_stride = k_low.data_ptr(), k_low.stride(1)
+    a.keys, a.k_head_stride, a.k_row_stride = keys.data_ptr(), keys.stride(1), keys.stride(2)
+    a.values, a.v_head_stride, a.v_row_stride = values.data_ptr(), values.stride(1), values.stride(2)
+    a.allowed_len = _ptr(allowed_len)
+    a.allowed_mask = _ptr(allowed_mask)
+    a.mask_row_stride = 0 if allowed_mask is None else allowed_mask.stride(0)
+    a.out, a.out_head_stride, a.out_row_stride = out.data_ptr(), out.stride(1), out.stride(2)
+    a.stats = _ptr(stats)
+    lay = _lib.BatchLayout()
+    lay.n_seqs, lay.page_keys = n_seqs, page_keys
+    lay.seq_lens = _ptr(seq_lens)
+    lay.page_table = _ptr(page_table)
+    lay.page_table_stride = 0 if page_table is None else page_table.stride(0)
+    lay.q_seq_stride, lay.out_seq_stride = q.stride(0), out.stride(0)
+    lay.codes_page_stride, lay.k_low_page_stride = codes.stride(0), k_low.stride(0)
+    lay.k_page_stride, lay.v_page_stride = keys.stride(0), values.stride(0)
+    sl_out = fin_out = None
+    if want_shortlist:
+        sl_out = torch.empty(n_seqs, n_heads, n_q, int(shortlist), dtype=torch.int32, device=dev)
+        a.shortlist_out = sl_out.data_ptr()
+    if want_final:
+        fin_out = torch.empty(n_seqs, n_heads, n_q, int(budget), dtype=torch.int32, device=dev)
+        a.final_out = fin_out.data_ptr()
+    lib = _lib.load()
+    ws_bytes = int(lib.sva_decode_batched_workspace_size(ctypes.byref(a), ctypes.byref(lay)))
+    ws = _decode_ws.get(dev, ws_bytes)
+    rc = lib.sva_decode_batched(ctypes.byref(a), ctypes.byref(lay), _ptr(ws), ws_bytes, _stream(dev))
+    _lib.check(rc)
+    if want_shortlist or want_final:
+        return out, sl_out, fin_out
+    return out
+
+
 def sva_scale(logit_scale: torch.Tensor) -> torch.Tensor:
     """clamp(exp(logit_scale), 0.01, 100) computed as the reference does (sva/llama.py:69-73)."""
     return logit_scale.detach().float().exp().clamp(0.01, 100.0)

@@ -49,10 +49,15 @@ class SVALlamaServingConfig:
     adaptive_high_margin: float = 0.70
     profile_components: bool = False
     static_tail_rebuild_interval: int = 64
-    # Not in the reference: "auto" projects keys on the tensor cores (tcgen05) when the keys are
-    # bf16 and the key projection holds bf16 values, else exactly on CUDA cores; "exact" always
-    # uses the CUDA-core projection in the canonical fp32 order.
-    write_path: str = "auto"
+    # Not in the reference: "exact" (the default) projects keys on CUDA cores in the canonical fp32
+    # order, so k_low and the codes are bit-exact; "auto" projects them on the tensor cores
+    # (tcgen05) when the keys are bf16 and the key projection holds bf16 values, which changes the
+    # fp32 summation order, so k_low may differ by a few ulp and codes may flip at near ties.
+    write_path: str = "exact"
+    # Not in the reference, which raises on batch != 1 (sva/llama.py:182-183): with allow_batch the
+    # scan summon decodes every sequence of a batch in one sva_decode_batched call, each
+    # sequence exactly as a batch-1 call would.  Off by default, keeping the reference's error.
+    allow_batch: bool = False
 
 
 class SVALlamaAttention(nn.Module):
@@ -97,6 +102,12 @@ class SVALlamaAttention(nn.Module):
         self._cached_signature: tuple | None = None
         self._tc_write_key: tuple | None = None
         self._tc_write = False
+        # batched catalog (allow_batch): [B, H, cap, R] fp32 / [B, H, cap, S] uint8
+        self._bk_low: torch.Tensor | None = None
+        self._bcodes: torch.Tensor | None = None
+        self._bkey_len = 0
+        self._bsignature: tuple | None = None
+        self._brep: tuple | None = None
 
     @property
     def _cached_k_low(self) -> torch.Tensor | None:
@@ -128,6 +139,16 @@ class SVALlamaAttention(nn.Module):
     def forward(self, hidden_states: torch.Tensor, position_embeddings: tuple[torch.Tensor, torch.Tensor] | None = None,
                 attention_mask: torch.Tensor | None = None, past_key_values: Cache | None = None,
                 **kwargs: Any) -> tuple[torch.Tensor, None]:
+        attn_output, weights = self.forward_attention(hidden_states, position_embeddings, attention_mask,
+                                                      past_key_values, **kwargs)
+        return self.o_proj(attn_output), weights
+
+    def forward_attention(self, hidden_states: torch.Tensor,
+                          position_embeddings: tuple[torch.Tensor, torch.Tensor] | None = None,
+                          attention_mask: torch.Tensor | None = None, past_key_values: Cache | None = None,
+                          **kwargs: Any) -> tuple[torch.Tensor, None]:
+        """forward without the final o_proj: the attention output [B, q, H * D] (the residual
+        adapter fuses o_proj into its own kernel)."""
         if self.training:
             raise RuntimeError("SVA Llama adapter is inference-only. Call model.eval() before running it.")
         if kwargs.get("output_attentions"):
@@ -145,7 +166,7 @@ class SVALlamaAttention(nn.Module):
             key_states, value_states = past_key_values.update(key_states, value_states, self.layer_idx)
         attn_output = self.sva_attention(query_states, key_states, value_states, attention_mask)
         attn_output = attn_output.transpose(1, 2).contiguous().reshape(*input_shape, -1)
-        return self.o_proj(attn_output), None
+        return attn_output, None
 
     # ------------------------------------------------------------------------------------
     def sva_attention(self, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
@@ -154,7 +175,9 @@ class SVALlamaAttention(nn.Module):
         batch, n_heads, q_len, head_dim = query.shape
         k_len = int(key.shape[2])
         if batch != 1:
-            raise ValueError("SVA Llama adapter currently expects batch size 1.")
+            if not self.serving.allow_batch:
+                raise ValueError("SVA Llama adapter currently expects batch size 1.")
+            return self._sva_attention_batched(query, key, value, attention_mask)
         if query.device.type != "cuda":
             raise RuntimeError("The B200 SVA adapter runs on CUDA devices only; move the model to a GPU.")
         mode = self.serving.summon_mode
@@ -227,6 +250,87 @@ class SVALlamaAttention(nn.Module):
                            allowed_mask=None if allowed_mask is None else allowed_mask[t0:t1],
                            out=out[:, t0:t1], stats=counters)
         return out.unsqueeze(0)
+
+    # ------------------------------------------------------------------------------------
+    def _sva_attention_batched(self, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                               attention_mask: torch.Tensor | None) -> torch.Tensor:
+        """query [B, H, q, D]; key/value [B, Hkv, L, D] -> [B, H, q, D]: the scan summon of every
+        sequence in one call (allow_batch).  Each sequence gets exactly what a batch-1 call of the
+        reference would compute for it (sva/llama.py:171-328)."""
+        batch, n_heads, q_len, head_dim = query.shape
+        k_len = int(key.shape[2])
+        if query.device.type != "cuda":
+            raise RuntimeError("The B200 SVA adapter runs on CUDA devices only; move the model to a GPU.")
+        mode = self.serving.summon_mode
+        if mode not in {"scan", "inverted", "inverted_static"}:
+            raise ValueError(f"Unknown SVA summon_mode: {mode!r}")
+        if mode != "scan":
+            raise ValueError("Batched SVA decode supports summon_mode='scan' only; run inverted modes at batch 1.")
+        dev = query.device
+        if key.stride(-1) != 1:
+            key = key.contiguous()
+        if value.stride(-1) != 1:
+            value = value.contiguous()
+        self._key_catalog_batched(key, q_len)
+        allowed_mask = None
+        if attention_mask is not None:
+            m = attention_mask[..., :q_len, :k_len] > -1e4
+            allowed_mask = m.expand(batch, 1, q_len, k_len).reshape(batch * q_len, k_len).to(torch.uint8).contiguous()
+        counters = None if self.stats is None else self.stats.device_counters(int(self.layer_idx or 0), dev)
+        out = torch.empty(batch, n_heads, q_len, head_dim, dtype=query.dtype, device=dev)
+        chunk = q_len
+        if k_len > _FUSED_MAX_KEYS:
+            chunk = max(1, min(q_len, _GRID_WORKSPACE_BUDGET // max(1, batch * n_heads * k_len * 8),
+                               65535 // (batch * n_heads)))
+        if self.serving.query_chunk_size:
+            chunk = min(chunk, int(self.serving.query_chunk_size))
+        for t0 in range(0, q_len, chunk):
+            t1 = min(q_len, t0 + chunk)
+            if allowed_mask is None:
+                lens = torch.arange(k_len - q_len + t0 + 1, k_len - q_len + t1 + 1, device=dev, dtype=torch.int64)
+                allowed_len = lens.expand(batch, t1 - t0).contiguous()
+                mask = None
+            else:
+                allowed_len = torch.full((batch, t1 - t0), k_len, device=dev, dtype=torch.int64)
+                mask = allowed_mask.view(batch, q_len, k_len)[:, t0:t1].reshape(batch * (t1 - t0), k_len)
+            kernels.decode_batched(query[:, :, t0:t1], self.sva_q_proj, self.sva_scale, self.sva_coarse_codebooks,
+                                   self._bcodes, self._bk_low, key, value, self.serving.coarse_shortlist,
+                                   self.serving.budget, max_len=k_len, softmax_scale=self.scaling, logits_mode=1,
+                                   allowed_len=allowed_len, allowed_mask=mask, out=out[:, :, t0:t1], stats=counters)
+        return out
+
+    def _key_catalog_batched(self, keys: torch.Tensor, q_len: int) -> None:
+        """The batched catalog [B, H, cap, ...]: new keys of every sequence are projected and coded
+        in place (one catalog_encode call over the B * H flattened heads)."""
+        batch, n_kv, k_len, head_dim = keys.shape
+        n_heads = int(self.sva_q_proj.shape[0])
+        signature = (keys.device, keys.dtype, batch, n_heads, head_dim)
+        can_append = (self._bsignature == signature and self._bk_low is not None and self._bkey_len > 0
+                      and k_len > self._bkey_len and k_len - self._bkey_len <= max(q_len, 1) and q_len < k_len)
+        start = self._bkey_len if can_append else 0
+        cap = 0 if self._bk_low is None else int(self._bk_low.shape[2])
+        rank = self.serving.rank_dim
+        subspaces = int(self.sva_coarse_codebooks.shape[1])
+        if self._bsignature != signature or cap < k_len:
+            new_cap = (max(k_len, 2 * cap if self._bsignature == signature else 0, 256) + 255) // 256 * 256
+            k_low = torch.empty(batch, n_heads, new_cap, rank, dtype=torch.float32, device=keys.device)
+            codes = torch.zeros(batch, n_heads, new_cap, subspaces, dtype=torch.uint8, device=keys.device)
+            if can_append:
+                k_low[:, :, :start] = self._bk_low[:, :, :start]
+                codes[:, :, :start] = self._bcodes[:, :, :start]
+            self._bk_low, self._bcodes = k_low, codes
+        if self._brep is None or self._brep[0] != batch or self._brep[1].device != keys.device:
+            self._brep = (batch, self.sva_k_proj.to(keys.device).repeat(batch, 1, 1).contiguous(),
+                          self.sva_coarse_codebooks.to(keys.device).repeat(batch, 1, 1, 1).contiguous())
+        flat_keys = keys.reshape(batch * n_kv, k_len, head_dim) if keys.is_contiguous() else keys.contiguous().view(
+            batch * n_kv, k_len, head_dim)
+        cap = int(self._bk_low.shape[2])
+        kernels.catalog_encode(flat_keys, self._brep[1], self._brep[2], start, k_len - start,
+                               self._bk_low.view(batch * n_heads, cap, rank),
+                               self._bcodes.view(batch * n_heads, cap, subspaces), n_heads=batch * n_heads,
+                               tensor_cores=self._tensor_core_write(flat_keys))
+        self._bkey_len = k_len
+        self._bsignature = signature
 
     # ------------------------------------------------------------------------------------
     def _ensure_capacity(self, n_heads: int, needed: int, device: torch.device) -> None:
@@ -368,7 +472,7 @@ class SVALlamaPatcher:
                  adaptive_min_budget: int | None = None, adaptive_mid_budget: int | None = None,
                  adaptive_low_margin: float = 0.35, adaptive_high_margin: float = 0.70,
                  profile_components: bool = False, static_tail_rebuild_interval: int = 64,
-                 layers: list[int] | None = None, write_path: str = "auto") -> None:
+                 layers: list[int] | None = None, write_path: str = "exact", allow_batch: bool = False) -> None:
         self.model = model
         self.bundle = bundle
         self.stats = SVAStats()
@@ -389,6 +493,7 @@ class SVALlamaPatcher:
             profile_components=profile_components,
             static_tail_rebuild_interval=static_tail_rebuild_interval,
             write_path=write_path,
+            allow_batch=allow_batch,
         )
 
     def patch(self) -> "SVALlamaPatcher":
@@ -466,12 +571,14 @@ def patch_llama_attention(model: nn.Module, artifact_dir_or_bundle: str | Path |
                           adaptive_mid_budget: int | None = None, adaptive_low_margin: float = 0.35,
                           adaptive_high_margin: float = 0.70, profile_components: bool = False,
                           static_tail_rebuild_interval: int = 64, layers: list[int] | None = None,
-                          write_path: str = "auto") -> SVALlamaPatcher:
+                          write_path: str = "exact", allow_batch: bool = False) -> SVALlamaPatcher:
     """Patch a Llama-family model with SVA attention and return a reversible handle (reference sva/llama.py:808-848).
 
-    ``write_path`` (not in the reference) selects the key projection: "auto" (tcgen05 tensor cores
-    when the keys are bf16 and the projection holds bf16 values) or "exact" (CUDA cores, canonical
-    fp32 order).
+    ``write_path`` (not in the reference) selects the key projection: "exact" (default; CUDA cores,
+    canonical fp32 order, bit-exact codes) or "auto" (tcgen05 tensor cores when the keys are bf16
+    and the projection holds bf16 values; codes may flip at near ties).  ``allow_batch`` (not in the
+    reference, which raises on batch != 1) decodes batches of sequences in one call per layer in
+    scan mode, each sequence exactly as at batch 1.
     """
     bundle = (artifact_dir_or_bundle if isinstance(artifact_dir_or_bundle, SVAArtifactBundle)
               else load_sva_artifact_bundle(artifact_dir_or_bundle))
@@ -482,4 +589,5 @@ def patch_llama_attention(model: nn.Module, artifact_dir_or_bundle: str | Path |
         adaptive_mid_budget=adaptive_mid_budget, adaptive_low_margin=adaptive_low_margin,
         adaptive_high_margin=adaptive_high_margin, profile_components=profile_components,
         static_tail_rebuild_interval=static_tail_rebuild_interval, layers=layers, write_path=write_path,
+        allow_batch=allow_batch,
     ).patch()

@@ -174,11 +174,12 @@ def main() -> None:
     ap.add_argument("--reference", default=None, help="path of the reference checkout (contains sva/)")
     ap.add_argument("--out", default=str(HERE / "golden_v1.npz"))
     ap.add_argument("--models", action="store_true", help="write the model-level fixtures instead")
+    ap.add_argument("--models-bf16", action="store_true", help="write the bf16 model-level fixtures instead")
     args = ap.parse_args()
     if args.reference:
         sys.path.insert(0, args.reference)
     torch.set_num_threads(8)
-    if args.models:
+    if args.models or args.models_bf16:
         return
     res = {}
     res.update(scan_case(config1(), "cfg1"))
@@ -204,20 +205,55 @@ def canonical_topk(self, k, dim=-1, largest=True, sorted=True):
     return torch.return_types.topk((vals.narrow(dim, 0, k), idx.narrow(dim, 0, k)))
 
 
-def model_cases(out_path: str) -> None:
+def model_cases(out_path: str, bf16: bool = False) -> None:
     """Model-level fixtures: the reference's patch_llama_attention on seeded random Llama models,
-    with torch.Tensor.topk replaced by canonical_topk for the duration of each run."""
+    with torch.Tensor.topk replaced by canonical_topk for the duration of each run.  ``bf16``
+    selects the bf16 SmolLM2-shaped cases (model_cases.BF16_CASES)."""
     from sva import SVAArtifactBundle, SVALayerArtifacts, patch_llama_attention
     from tests.golden import model_cases as mc
 
+    from sva.llama import SVALlamaAttention
+
     res = {}
     original = torch.Tensor.topk
+    original_attention = SVALlamaAttention.sva_attention
+    calls: list = []
+
+    def recording_attention(self, query, key, value, attention_mask):
+        # the inputs and output of every SVA attention call of layer 1 (bf16 cases): the GPU test
+        # feeds the same tensors to the B200 module, so the comparison does not depend on how the
+        # rest of the model rounds on each device
+        out = original_attention(self, query, key, value, attention_mask)
+        if self.layer_idx == 1:
+            allowed = None if attention_mask is None else (attention_mask[..., : query.shape[2], : key.shape[2]] > -1e4)
+            calls.append((query.detach().clone(), key.detach().clone(), value.detach().clone(),
+                          None if allowed is None else allowed.detach().clone(), out.detach().clone()))
+        return out
+
+    def bits(t: torch.Tensor) -> np.ndarray:
+        return t.contiguous().view(torch.int16).numpy().view(np.uint16) if t.dtype == torch.bfloat16 else t.numpy()
+
     try:
         torch.Tensor.topk = canonical_topk
-        for name in mc.CASES:
+        if bf16:
+            SVALlamaAttention.sva_attention = recording_attention
+        for name in (mc.BF16_CASES if bf16 else mc.CASES):
+            calls.clear()
             model, bundle, steps, case = mc.build(name, SVAArtifactBundle, SVALayerArtifacts)
             res[f"{name}_model_checksum"] = np.asarray(sum(float(p.double().sum()) for p in model.parameters()))
             outs, summary, state = mc.run(model, patch_llama_attention, bundle, steps, case)
+            if bf16:
+                # layer 1's calls: queries and outputs of every step, the final K / V (each step's
+                # cache is a prefix of it), and the mask of the calls that had one
+                res[f"{name}_l1_calls"] = np.asarray(len(calls))
+                res[f"{name}_l1_key"] = bits(calls[-1][1])
+                res[f"{name}_l1_value"] = bits(calls[-1][2])
+                for i, (q, k, v, allowed, out) in enumerate(calls):
+                    res[f"{name}_l1_q_{i}"] = bits(q)
+                    res[f"{name}_l1_klen_{i}"] = np.asarray(k.shape[2])
+                    res[f"{name}_l1_out_{i}"] = bits(out)
+                    if allowed is not None:
+                        res[f"{name}_l1_allowed_{i}"] = allowed[0, 0].numpy()
             for i, o in enumerate(outs):
                 res[f"{name}_logits_{i}"] = o.numpy()
             for k, v in summary.items():
@@ -226,9 +262,12 @@ def model_cases(out_path: str) -> None:
                 res[f"{name}_state_{k}"] = np.asarray(v)
     finally:
         torch.Tensor.topk = original
+        SVALlamaAttention.sva_attention = original_attention
     np.savez_compressed(out_path, **res)
     print("wrote", out_path, len(res), "arrays")
 
 
 if __name__ == "__main__" and "--models" in sys.argv:
     model_cases(str(HERE / "golden_models_v1.npz"))
+if __name__ == "__main__" and "--models-bf16" in sys.argv:
+    model_cases(str(HERE / "golden_models_bf16_v1.npz"), bf16=True)

@@ -27,6 +27,16 @@ CASES = {
                                  static_tail_rebuild_interval=3), steps="small"),
 }
 
+# The same SmolLM2-shaped attention in bf16 (model weights, activations and KV cache), with
+# artifacts holding bf16 values as real bundles do; the adapter runs with its default write path.
+# Their fixtures live in golden_models_bf16_v1.npz and are compared within the bf16 tolerance.
+BF16_CASES = {
+    "small_bf16_scan": dict(model="small_bf16", mode="scan", kw=dict(shortlist=96, budget=24), steps="small"),
+    "small_bf16_static": dict(model="small_bf16", mode="inverted_static",
+                              kw=dict(shortlist=96, budget=24, inverted_cells_per_subspace=8,
+                                      static_tail_rebuild_interval=3), steps="small"),
+}
+
 
 def tiny_model() -> LlamaForCausalLM:
     torch.manual_seed(1234)
@@ -70,10 +80,14 @@ def small_steps():
 def build(name: str, bundle_cls, layer_cls):
     """Model, bundle (constructed with the given SVAArtifactBundle / SVALayerArtifacts classes)
     and token steps of a case."""
-    case = CASES[name]
+    case = CASES[name] if name in CASES else BF16_CASES[name]
     if case["model"] == "tiny":
         model = tiny_model()
         tensors, manifest = tiny_bundle_tensors(), tiny_manifest()
+    elif case["model"] == "small_bf16":
+        model = small_model().to(torch.bfloat16)
+        tensors, manifest = small_bundle_tensors()
+        tensors = {i: {k: v.to(torch.bfloat16) for k, v in t.items()} for i, t in tensors.items()}
     else:
         model = small_model()
         tensors, manifest = small_bundle_tensors()

@@ -227,3 +227,34 @@ def test_unpinned_host_query_is_rejected():
     k_low, codes = gpu_catalog(case)
     with pytest.raises(ValueError, match="pinned host tensor"):
         _decode_with(case, k_low, codes, case.q[0].clone())
+
+
+def test_chained_decodes_query_aliases_previous_output():
+    """Two back-to-back decodes on one stream where the second call's query is the first call's
+    output buffer: the dependent launches of the second call must read the query only after the
+    first call has written it.  Compared with the same two calls separated by a synchronize."""
+    case, _ = cached_case("cfg2s_4x64")  # 2^16 keys: the grid schedule
+    k_low, codes = gpu_catalog(case)
+    q0 = case.q[0].cuda()
+
+    def run(q, out):
+        from sva_b200 import kernels
+
+        return kernels.decode(q, case.q_proj.cuda(), kernels.sva_scale(case.logit_scale).cuda(), case.codebooks.cuda(),
+                              codes, k_low, case.keys[0].cuda(), case.values[0].cuda(), 2048, 512,
+                              softmax_scale=0.125, logits_mode=1, out=out)
+
+    for _ in range(3):
+        out1 = torch.empty_like(q0)
+        out2 = torch.empty_like(q0)
+        run(q0, out1)
+        run(out1, out2)  # no synchronisation between the calls
+        torch.cuda.synchronize()
+        ref1 = torch.empty_like(q0)
+        run(q0, ref1)
+        torch.cuda.synchronize()
+        ref2 = torch.empty_like(q0)
+        run(ref1.clone(), ref2)
+        torch.cuda.synchronize()
+        assert torch.equal(out1, ref1)
+        assert torch.equal(out2, ref2)
