@@ -807,51 +807,65 @@ def passkey_prompt(batch: int, context: int, seed: int = 2, digit_ids=tuple(rang
     return ids
 
 
-def greedy_decode(model, prompt, steps: int, device):
-    """Prefill the prompt, then `steps` greedy tokens through the model (HF DynamicCache).
-    Returns (prefill_ms, decode_ms, decode_e2e_ms, tokens): decode_ms is the device time of the
-    decode loop; decode_e2e_ms the same loop where every step also moves its tokens device ->
-    pinned host -> device (a host-driven generation loop)."""
+def eager_decode(model, prompt, steps: int, device):
+    """Prefill the prompt, then `steps` greedy tokens through the model's eager forward over HF's
+    DynamicCache (the reference's way).  Returns (prefill_ms, decode_ms): device time of each."""
     import torch
     from transformers import DynamicCache
 
-    def prefill():
-        cache = DynamicCache(config=model.config)
-        out = model(input_ids=prompt.to(device), use_cache=True, past_key_values=cache, logits_to_keep=1)
-        return out.past_key_values, out.logits[:, -1].argmax(-1, keepdim=True)
+    with torch.no_grad():
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record()
+        out = model(input_ids=prompt.to(device), use_cache=True, past_key_values=DynamicCache(config=model.config),
+                    logits_to_keep=1)
+        tok = out.logits[:, -1].argmax(-1, keepdim=True)
+        e1.record()
+        cache = out.past_key_values
+        for _ in range(steps - 1):
+            out = model(input_ids=tok, use_cache=True, past_key_values=cache, logits_to_keep=1)
+            tok = out.logits[:, -1].argmax(-1, keepdim=True)
+        e2.record()
+        torch.cuda.synchronize()
+    return e0.elapsed_time(e1), e1.elapsed_time(e2)
 
+
+def graphed_decode(model, prompt, steps: int, device):
+    """The same greedy decode with the per-token step captured in a CUDA graph over a StaticCache
+    (sva_b200.serving.GraphedGreedyDecoder).  Returns (prefill_ms, decode_ms, e2e_ms, tokens):
+    decode_ms is the device time of `steps` graph replays; e2e_ms the same replays where every
+    step also moves its tokens device -> pinned host -> device (a host-driven generation loop)."""
+    import torch
+
+    from sva_b200.serving import GraphedGreedyDecoder
+
+    batch = prompt.shape[0]
+    dec = GraphedGreedyDecoder(model, batch, prompt.shape[1] + 2 * steps + 4)
     with torch.no_grad():
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        cache, tok = prefill()
+        first = dec.prefill(prompt)
         e1.record()
         torch.cuda.synchronize()
         prefill_ms = e0.elapsed_time(e1)
-        toks = [tok]
+        dec.capture()
+        toks = [first, dec.warm_token]
         e0.record()
-        for _ in range(steps - 1):
-            out = model(input_ids=tok, use_cache=True, past_key_values=cache, logits_to_keep=1)
-            cache = out.past_key_values
-            tok = out.logits[:, -1].argmax(-1, keepdim=True)
-            toks.append(tok)
+        for _ in range(steps):
+            dec.step()
         e1.record()
         torch.cuda.synchronize()
         decode_ms = e0.elapsed_time(e1)
-        # end to end: the same decode with the token ids crossing to the host and back every step
-        if hasattr(model, "_sva_handle"):
-            model._sva_handle.reset_catalogs()
-        cache, tok = prefill()
-        host = torch.empty_like(tok, device="cpu").pin_memory()
-        torch.cuda.synchronize()
+        toks.append(dec.tok.clone())
+        host = torch.empty_like(dec.tok, device="cpu").pin_memory()
         e0.record()
-        for _ in range(steps - 1):
-            out = model(input_ids=tok, use_cache=True, past_key_values=cache, logits_to_keep=1)
-            cache = out.past_key_values
-            host.copy_(out.logits[:, -1].argmax(-1, keepdim=True), non_blocking=True)
-            tok = host.to(device, non_blocking=True)
+        for _ in range(steps):
+            nxt = dec.step()
+            host.copy_(nxt, non_blocking=True)
+            dec.tok.copy_(host, non_blocking=True)
         e1.record()
         torch.cuda.synchronize()
         e2e_ms = e0.elapsed_time(e1)
+    dec.release()
     return prefill_ms, decode_ms, e2e_ms, torch.cat(toks, 1)
 
 
@@ -865,8 +879,6 @@ def model_arm(args):
     device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
     torch.cuda.set_device(device)
     model = smollm2_model(device)
-    peak, peak_kind = measured_peaks()
-    runs = []
     if args.workload == "cfg3":
         gen = torch.Generator().manual_seed(1)
         prompt = torch.randint(0, 49152, (1, args.model_prefill), generator=gen)
@@ -876,15 +888,17 @@ def model_arm(args):
         prompt = passkey_prompt(8, args.model_prefill)
         settings = [(8192, 2048, [26, 27, 28, 29], True), (512, 128, [26, 27, 28, 29], True)]
         steps, batch = args.model_decode, 8
-    # the unpatched model (full attention everywhere) for context
-    pf, dm, em, _ = greedy_decode(model, prompt, steps, device)
-    full = {"prefill_ms": round(pf, 1), "decode_ms_per_step": round(dm / (steps - 1), 3),
-            "tokens_per_s": round(batch * (steps - 1) / (dm * 1e-3), 1)}
+    # warm-up (kernel loading, library heuristics) on a short prompt, then the unpatched model
+    eager_decode(model, prompt[:, :256], 4, device)
+    pf, _, _, _ = graphed_decode(model, prompt, steps, device)
+    _, dm, _, _ = graphed_decode(model, prompt, steps, device)
+    full = {"prefill_ms": round(pf, 1), "decode_ms_per_step": round(dm / steps, 3),
+            "tokens_per_s": round(batch * steps / (dm * 1e-3), 1), "path": "full attention, graphed step"}
+    runs = []
     clocks = None
     for shortlist, budget, layers, adapter in settings:
         handle = patch_llama_attention(model, random_bundle(30, shortlist, budget), layers=layers,
                                        allow_batch=batch > 1)
-        model._sva_handle = handle
         if adapter:
             wrap_socket_layers_with_adapters(model, layers, rank=16, scale=1.0)
             gen = torch.Generator().manual_seed(4)
@@ -893,30 +907,35 @@ def model_arm(args):
                     a = model.model.layers[i].self_attn
                     a.down.weight.copy_(torch.randn(a.down.weight.shape, generator=gen) * 0.02)
                     a.up.weight.copy_(torch.randn(a.up.weight.shape, generator=gen) * 0.02)
+        eager_steps = min(steps, 16)
+        epf, edm = eager_decode(model, prompt, eager_steps, device)
+        handle.reset_catalogs()
         sampler = ClockSampler(None)
         sampler.start()
-        pf, dm, em, toks = greedy_decode(model, prompt, steps, device)
+        pf, dm, em, toks = graphed_decode(model, prompt, steps, device)
         clocks = sampler.stop()
         summary = handle.stats.summary()
         handle.unpatch()
-        del model._sva_handle
-        n_tok = batch * (steps - 1)
+        n_tok = batch * steps
         runs.append({"shortlist": shortlist, "budget": budget, "patched_layers": len(layers), "adapter": adapter,
-                     "prefill_ms": round(pf, 1), "decode_ms_per_step": round(dm / (steps - 1), 3),
-                     "tokens_per_s": round(n_tok / (dm * 1e-3), 1),
-                     "e2e_tokens_per_s": round(n_tok / (em * 1e-3), 1),
+                     "prefill_ms": round(pf, 1), "decode_ms_per_step": round(dm / steps, 3),
+                     "tokens_per_s": round(n_tok / (dm * 1e-3), 1), "e2e_tokens_per_s": round(n_tok / (em * 1e-3), 1),
+                     "eager_prefill_ms": round(epf, 1), "eager_decode_ms_per_step": round(edm / (eager_steps - 1), 3),
+                     "eager_tokens_per_s": round(batch * (eager_steps - 1) / (edm * 1e-3), 1),
                      "avg_summoned": summary.get("avg_summoned"), "avg_verified": summary.get("avg_verified")})
     head = runs[0]
     line = {
         "metric": "decode tok/s" + (" @32k" if args.workload == "cfg4" else " @8k"), "value": head["tokens_per_s"],
-        "unit": "tokens/s", "n_gpus": 1, "steps": steps - 1, "warmup": 1,
+        "unit": "tokens/s", "n_gpus": 1, "steps": steps, "warmup": 1,
         "ms_per_step": head["decode_ms_per_step"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic (random-init SmolLM2-135M-shaped model and artifacts, random token ids)",
         "config": {"workload": (f"cfg3: 30-layer SmolLM2-135M shape, all layers SVA 2x256 (2048/512), prefill "
                                 f"{args.model_prefill}, greedy decode {steps}, batch 1") if args.workload == "cfg3" else
                    (f"cfg4: late4 socket (layers 26-29 SVA + rank-16 residual adapters), context "
                     f"{args.model_prefill}, batch 8, greedy decode {steps}; shortlist/budget 8192/2048 and 512/128"),
-                   "path": "HF LlamaForCausalLM patched by sva_b200.patch_llama_attention, eager decode loop"},
+                   "path": "HF LlamaForCausalLM patched by sva_b200.patch_llama_attention; per-token step in one CUDA "
+                           "graph over a StaticCache (sva_b200.serving.GraphedGreedyDecoder); eager DynamicCache "
+                           "loop reported beside it"},
         "e2e": {"value": head["e2e_tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": 8 * batch,
                 "d2h_bytes_per_step": 8 * batch},
         "runs": runs, "full_attention": full, "clocks": clocks, "gpu_launches": None,

@@ -92,6 +92,16 @@ int sva_catalog_encode(const void* keys, int32_t key_dtype, int64_t key_head_str
                        int64_t start, int64_t count, float* k_low, int64_t k_low_head_stride, uint8_t* codes,
                        int64_t codes_head_stride, void* stream);
 
+/* The same for rows [*start, *start + count) with the start row read from device memory, so that
+ * the call can sit in a captured CUDA graph whose replays append at a moving position; rows at or
+ * beyond `limit` (the capacity of keys, k_low and codes) are skipped.  No reference counterpart:
+ * the reference appends with torch.cat (sva/llama.py:599-613). */
+int sva_catalog_encode_at(const void* keys, int32_t key_dtype, int64_t key_head_stride, int64_t key_row_stride,
+                          int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t rank_dim,
+                          const float* k_proj, const float* codebooks, int32_t subspaces, int32_t codewords,
+                          const int64_t* start, int64_t count, int64_t limit, float* k_low,
+                          int64_t k_low_head_stride, uint8_t* codes, int64_t codes_head_stride, void* stream);
+
 /* The same on the tensor cores: k_low = K . Kproj by tcgen05 MMA (bf16 operands, fp32
  * accumulator in tensor memory), then the same nearest-codeword assignment on the fp32 rows.
  * K must be bf16 with 16-byte aligned rows; Kproj is rounded to bf16, which is exact for bf16
@@ -238,6 +248,46 @@ int sva_shard_rescore(const sva_decode_args* args, int64_t key_offset, int32_t w
 int sva_shard_verify(const sva_decode_args* args, int64_t key_offset, int32_t world, int32_t rank,
                      const uint32_t* gathered_records, double* partial_out, void* stream);
 int sva_shard_combine(const sva_decode_args* args, int32_t world, const double* gathered_partials, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Batched shards: the same four stages for a batch of sequences (sva_batch_layout) and with a
+ * narrower first exchange.  Replaces the single-device sva/llama.py:171-328 for batches whose
+ * caches are split across ranks (the reference is single-device).
+ *
+ * sva_shard_map gives each rank's local -> global key numbering (the tie rule uses global
+ * indices): key-range shards (page_world == 0) hold global keys [key_offset, key_offset + L_r)
+ * of every sequence; page-dealt shards (page_world > 0, paged layout required) hold global page
+ * g of every sequence on rank g % page_world as local page g / page_world, rows unchanged.
+ *
+ * exchange_width k1 (0 < k1 <= shortlist, 0 meaning the shortlist): each rank sends its local
+ * top-k1 per problem (top_out [P][k1] u64) and the records of its shortlist members
+ * (records_out [P][k1][4] u32); the host all-gathers them to [W][P][k1] as before.  The global
+ * shortlist is exact whenever no rank has more than k1 members; the rescore stage sets
+ * *saturated (device int32, may be NULL) when a rank sent k1 entries that are all members, in
+ * which case the host must repeat the decode with exchange_width = shortlist.  With k1 near
+ * shortlist / W the first two exchanges shrink about W-fold.  P = n_seqs * n_heads problems
+ * (n_queries == 1); partial_out and gathered partials are [P][head_dim] as before.
+ * ------------------------------------------------------------------------------------- */
+typedef struct sva_shard_map {
+  int64_t key_offset;
+  int32_t page_world;
+  int32_t page_rank;
+} sva_shard_map;
+
+size_t sva_shard_batched_workspace_size(const sva_decode_args* args, const sva_batch_layout* layout,
+                                        const sva_shard_map* map, int32_t exchange_width);
+int sva_shard_batched_summon(const sva_decode_args* args, const sva_batch_layout* layout, const sva_shard_map* map,
+                             int32_t exchange_width, uint64_t* top_out, void* workspace, size_t workspace_bytes,
+                             void* stream);
+int sva_shard_batched_rescore(const sva_decode_args* args, const sva_batch_layout* layout, const sva_shard_map* map,
+                              int32_t exchange_width, int32_t world, int32_t rank, const uint64_t* gathered_top,
+                              uint32_t* records_out, int32_t* saturated, void* workspace, size_t workspace_bytes,
+                              void* stream);
+int sva_shard_batched_verify(const sva_decode_args* args, const sva_batch_layout* layout, const sva_shard_map* map,
+                             int32_t exchange_width, int32_t world, int32_t rank, const uint32_t* gathered_records,
+                             double* partial_out, void* stream);
+int sva_shard_batched_combine(const sva_decode_args* args, const sva_batch_layout* layout, int32_t world,
+                              const double* gathered_partials, void* stream);
 
 /* ---------------------------------------------------------------------------------------
  * Posting lists of the static inverted index.  Replaces sva/llama.py:626-657.

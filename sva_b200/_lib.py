@@ -43,6 +43,7 @@ EXPORTED = (
     "sva_debug_timestamps",
     "sva_host_buffer_device_accessible",
     "sva_catalog_encode",
+    "sva_catalog_encode_at",
     "sva_catalog_encode_tc",
     "sva_assign_centroids",
     "sva_pq_scores",
@@ -55,6 +56,11 @@ EXPORTED = (
     "sva_shard_rescore",
     "sva_shard_verify",
     "sva_shard_combine",
+    "sva_shard_batched_workspace_size",
+    "sva_shard_batched_summon",
+    "sva_shard_batched_rescore",
+    "sva_shard_batched_verify",
+    "sva_shard_batched_combine",
     "sva_postings_workspace_size",
     "sva_postings_build",
     "sva_postings_build_noalloc",
@@ -135,6 +141,16 @@ class BatchLayout(ctypes.Structure):
     ]
 
 
+class ShardMap(ctypes.Structure):
+    """Mirror of ``sva_shard_map``."""
+
+    _fields_ = [
+        ("key_offset", c_i64),
+        ("page_world", c_i32),
+        ("page_rank", c_i32),
+    ]
+
+
 class InvertedArgs(ctypes.Structure):
     """Mirror of ``sva_inverted_args``."""
 
@@ -210,6 +226,8 @@ def load() -> ctypes.CDLL:
             "sva_host_buffer_device_accessible": ([c_vp], ctypes.c_int),
             "sva_catalog_encode": ([c_vp, c_i32, c_i64, c_i64, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_i32, c_i32,
                                     c_i64, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp], ctypes.c_int),
+            "sva_catalog_encode_at": ([c_vp, c_i32, c_i64, c_i64, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_i32,
+                                       c_i32, c_vp, c_i64, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp], ctypes.c_int),
             "sva_catalog_encode_tc": ([c_vp, c_i32, c_i64, c_i64, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_i32,
                                        c_i32, c_i64, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_vp], ctypes.c_int),
             "sva_assign_centroids": ([c_vp, c_i64, c_i32, c_i64, c_vp, c_i32, c_vp, c_vp], ctypes.c_int),
@@ -225,6 +243,14 @@ def load() -> ctypes.CDLL:
                                   ctypes.c_int),
             "sva_shard_verify": ([ctypes.POINTER(DecodeArgs), c_i64, c_i32, c_i32, c_vp, c_vp, c_vp], ctypes.c_int),
             "sva_shard_combine": ([ctypes.POINTER(DecodeArgs), c_i32, c_vp, c_vp], ctypes.c_int),
+            "sva_shard_batched_workspace_size": ([ctypes.POINTER(DecodeArgs), c_vp, c_vp, c_i32], c_sz),
+            "sva_shard_batched_summon": ([ctypes.POINTER(DecodeArgs), c_vp, c_vp, c_i32, c_vp, c_vp, c_sz, c_vp],
+                                         ctypes.c_int),
+            "sva_shard_batched_rescore": ([ctypes.POINTER(DecodeArgs), c_vp, c_vp, c_i32, c_i32, c_i32, c_vp, c_vp,
+                                           c_vp, c_vp, c_sz, c_vp], ctypes.c_int),
+            "sva_shard_batched_verify": ([ctypes.POINTER(DecodeArgs), c_vp, c_vp, c_i32, c_i32, c_i32, c_vp, c_vp,
+                                          c_vp], ctypes.c_int),
+            "sva_shard_batched_combine": ([ctypes.POINTER(DecodeArgs), c_vp, c_i32, c_vp, c_vp], ctypes.c_int),
             "sva_postings_workspace_size": ([c_i32, c_i32, c_i32, c_i64], c_sz),
             "sva_postings_build": ([c_vp, c_i64, c_i32, c_i32, c_i32, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp,
                                     c_sz, c_vp], ctypes.c_int),

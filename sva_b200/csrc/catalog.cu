@@ -23,6 +23,8 @@ struct CatalogParams {
   const float* k_proj;
   const float* codebooks;
   int64_t start, count;
+  const int64_t* start_dev;  // when set, rows start at *start_dev + start (read on the device) ...
+  int64_t limit;             // ... and rows >= limit are skipped
   float* k_low;
   int64_t k_low_head_stride;
   uint8_t* codes;
@@ -135,8 +137,10 @@ __global__ void __launch_bounds__(kCatKeys) catalog_encode_kernel(const CatalogP
   const int kvh = h / p.groups;
   const int tid = threadIdx.x;
   const int D = p.D, R = p.R;
-  const int64_t l0 = p.start + (int64_t)blockIdx.x * kCatKeys;
-  const int64_t l_end = p.start + p.count;
+  const int64_t start = p.start_dev ? __ldg(p.start_dev) + p.start : p.start;
+  const int64_t l0 = start + (int64_t)blockIdx.x * kCatKeys;
+  const int64_t l_end = min(start + p.count, p.limit);
+  if (l0 < 0 || l0 >= l_end) return;  // uniform over the block
   const int nrows = (l_end - l0 < kCatKeys) ? (int)(l_end - l0) : kCatKeys;
 
   const float* Pg = p.k_proj + (size_t)h * D * R;
@@ -173,6 +177,97 @@ __global__ void __launch_bounds__(kCatKeys) catalog_encode_kernel(const CatalogP
   }
   __syncthreads();
   if (p.k_low) store_k_low(p, h, l0, nrows, kl);
+}
+
+// Append path for a few keys (decode steps): one CTA per (key, head), so a one-key append is
+// spread over the threads of many CTAs instead of one thread of a 128-key tile.  Same canonical
+// arithmetic as catalog_encode_kernel: every projection output and every distance is one thread's
+// sequential fp32 dot product; the nearest codeword is the first minimum in codeword order.
+constexpr int kAppendThreads = 128;
+constexpr int kAppendMaxKeys = 8;  // appends of at most this many keys take this kernel
+
+template <typename T>
+__global__ void __launch_bounds__(kAppendThreads) catalog_append_kernel(const CatalogParams p) {
+  __shared__ float x[kMaxHeadDim];
+  __shared__ float y[kMaxRank];
+  __shared__ float bd[kAppendThreads / 32][kMaxSubspaces];
+  __shared__ int bc[kAppendThreads / 32][kMaxSubspaces];
+  const int h = blockIdx.y;
+  const int kvh = h / p.groups;
+  const int tid = threadIdx.x;
+  const int D = p.D, R = p.R, S = p.S, C = p.C, sub = p.sub;
+  const int64_t start = p.start_dev ? __ldg(p.start_dev) + p.start : p.start;
+  const int64_t l = start + blockIdx.x;
+  if (l < 0 || l >= min(start + p.count, p.limit)) return;  // uniform over the block
+  const T* kr = reinterpret_cast<const T*>(p.keys) + kvh * p.key_head_stride + l * p.key_row_stride;
+  for (int d = tid; d < D; d += blockDim.x) x[d] = to_f32<T>(kr[d]);
+  __syncthreads();
+  const float* Pg = p.k_proj + (size_t)h * D * R;
+  for (int r = tid; r < R; r += blockDim.x) {
+    float a = 0.f;
+    for (int d = 0; d < D; ++d) a = mac(a, x[d], __ldg(Pg + d * R + r));
+    y[r] = a;
+  }
+  __syncthreads();
+  if (p.k_low)
+    for (int r = tid; r < R; r += blockDim.x) p.k_low[h * p.k_low_head_stride + l * R + r] = y[r];
+  if (!p.codes) return;
+  const int lane = tid & 31, warp = tid >> 5;
+  for (int sp = 0; sp < S; ++sp) {
+    const float* xs = y + sp * sub;
+    float xn = 0.f;
+    for (int j = 0; j < sub; ++j) xn = mac(xn, xs[j], xs[j]);
+    // this thread's best codeword of the subspace: first minimum, NaN distances never win
+    float best = INFINITY;
+    int bi = C;
+    bool nan0 = false;
+    for (int c = tid; c < C; c += blockDim.x) {
+      const float* cw = p.codebooks + (((size_t)h * S + sp) * C + c) * sub;
+      float dv = 0.f, cn = 0.f;
+      for (int j = 0; j < sub; ++j) {
+        const float v = __ldg(cw + j);
+        dv = mac(dv, xs[j], v);
+        cn = mac(cn, v, v);
+      }
+      const float dist = __fadd_rn(__fsub_rn(xn, __fmul_rn(2.f, dv)), cn);
+      if (c == 0 && isnan(dist)) nan0 = true;
+      if (dist < best) {
+        best = dist;
+        bi = c;
+      }
+    }
+    // the sequential rule keeps codeword 0 when its distance is NaN
+    nan0 = __any_sync(0xFFFFFFFFu, nan0);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+      const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+      if (ob < best || (ob == best && oi < bi)) {
+        best = ob;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      bd[warp][sp] = best;
+      bc[warp][sp] = nan0 ? -1 : bi;
+    }
+  }
+  __syncthreads();
+  if (tid < S) {
+    float best = INFINITY;
+    int bi = C;
+    bool nan0 = false;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+      if (bc[w][tid] < 0) nan0 = true;
+      if (bd[w][tid] < best || (bd[w][tid] == best && bc[w][tid] < bi)) {
+        best = bd[w][tid];
+        bi = bc[w][tid];
+      }
+    }
+    // every distance NaN or infinite: the sequential scan keeps codeword 0
+    if (nan0 || bi >= C || bi < 0) bi = 0;
+    p.codes[h * p.codes_head_stride + l * S + tid] = static_cast<uint8_t>(bi);
+  }
 }
 
 __global__ void __launch_bounds__(256) assign_centroids_kernel(const float* __restrict__ x, int64_t n, int dim,
@@ -420,11 +515,11 @@ __global__ void __launch_bounds__(kTcKeys) catalog_encode_tc_kernel(const Catalo
 
 using namespace sva;
 
-extern "C" int sva_catalog_encode(const void* keys, int32_t key_dtype, int64_t key_head_stride,
-                                  int64_t key_row_stride, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
-                                  int32_t rank_dim, const float* k_proj, const float* codebooks, int32_t subspaces,
-                                  int32_t codewords, int64_t start, int64_t count, float* k_low,
-                                  int64_t k_low_head_stride, uint8_t* codes, int64_t codes_head_stride, void* stream) {
+static int catalog_encode_impl(const void* keys, int32_t key_dtype, int64_t key_head_stride, int64_t key_row_stride,
+                               int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t rank_dim,
+                               const float* k_proj, const float* codebooks, int32_t subspaces, int32_t codewords,
+                               int64_t start, const int64_t* start_dev, int64_t count, int64_t limit, float* k_low,
+                               int64_t k_low_head_stride, uint8_t* codes, int64_t codes_head_stride, void* stream) {
   if (n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads) return set_error(SVA_ERR_SHAPE, "bad head counts");
   if (head_dim <= 0 || head_dim > kMaxHeadDim) return set_error(SVA_ERR_SHAPE, "head_dim must be in 1..256");
   if (rank_dim <= 0 || rank_dim > kMaxRank || rank_dim % 4) return set_error(SVA_ERR_SHAPE, "rank_dim must be a multiple of 4 <= 64");
@@ -449,15 +544,27 @@ extern "C" int sva_catalog_encode(const void* keys, int32_t key_dtype, int64_t k
   p.codebooks = codebooks;
   p.start = start;
   p.count = count;
+  p.start_dev = start_dev;
+  p.limit = limit;
   p.k_low = k_low;
   p.k_low_head_stride = k_low_head_stride;
   p.codes = codes;
   p.codes_head_stride = codes_head_stride;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (count <= kAppendMaxKeys) {
+    dim3 agrid((unsigned)count, (unsigned)n_heads);
+    switch (key_dtype) {
+      case SVA_DTYPE_F32: catalog_append_kernel<float><<<agrid, kAppendThreads, 0, s>>>(p); break;
+      case SVA_DTYPE_BF16: catalog_append_kernel<__nv_bfloat16><<<agrid, kAppendThreads, 0, s>>>(p); break;
+      default: catalog_append_kernel<__half><<<agrid, kAppendThreads, 0, s>>>(p); break;
+    }
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? SVA_OK : set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
+  }
   catalog_layout(p);
   const size_t smem = sizeof(float) * p.total_floats;
   if (smem > (size_t)kMaxDynSmem) return set_error(SVA_ERR_SHAPE, "catalog tile exceeds shared memory");
   dim3 grid((unsigned)((count + kCatKeys - 1) / kCatKeys), (unsigned)n_heads);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   int rc;
   switch (key_dtype) {
     case SVA_DTYPE_F32:
@@ -479,6 +586,29 @@ extern "C" int sva_catalog_encode(const void* keys, int32_t key_dtype, int64_t k
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
   return SVA_OK;
+}
+
+extern "C" int sva_catalog_encode(const void* keys, int32_t key_dtype, int64_t key_head_stride,
+                                  int64_t key_row_stride, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                                  int32_t rank_dim, const float* k_proj, const float* codebooks, int32_t subspaces,
+                                  int32_t codewords, int64_t start, int64_t count, float* k_low,
+                                  int64_t k_low_head_stride, uint8_t* codes, int64_t codes_head_stride, void* stream) {
+  return catalog_encode_impl(keys, key_dtype, key_head_stride, key_row_stride, n_heads, n_kv_heads, head_dim, rank_dim,
+                             k_proj, codebooks, subspaces, codewords, start, nullptr, count, start + count, k_low,
+                             k_low_head_stride, codes, codes_head_stride, stream);
+}
+
+extern "C" int sva_catalog_encode_at(const void* keys, int32_t key_dtype, int64_t key_head_stride,
+                                     int64_t key_row_stride, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                                     int32_t rank_dim, const float* k_proj, const float* codebooks, int32_t subspaces,
+                                     int32_t codewords, const int64_t* start, int64_t count, int64_t limit,
+                                     float* k_low, int64_t k_low_head_stride, uint8_t* codes, int64_t codes_head_stride,
+                                     void* stream) {
+  if (!start) return set_error(SVA_ERR_SHAPE, "start is null");
+  if (limit < 0) return set_error(SVA_ERR_SHAPE, "negative limit");
+  return catalog_encode_impl(keys, key_dtype, key_head_stride, key_row_stride, n_heads, n_kv_heads, head_dim, rank_dim,
+                             k_proj, codebooks, subspaces, codewords, 0, start, count, limit, k_low, k_low_head_stride,
+                             codes, codes_head_stride, stream);
 }
 
 extern "C" int sva_assign_centroids(const float* x, int64_t n, int32_t dim, int64_t x_row_stride,
@@ -551,6 +681,8 @@ extern "C" int sva_catalog_encode_tc(const void* keys, int32_t key_dtype, int64_
   p.sub = rank_dim / subspaces;
   p.k_proj = k_proj;
   p.codebooks = codebooks;
+  p.start_dev = nullptr;
+  p.limit = start + count;
   p.start = start;
   p.count = count;
   p.k_low = k_low;

@@ -42,6 +42,8 @@ namespace cg = cooperative_groups;
 constexpr int kThreads = 512;
 constexpr int kScanKeys = 32768;         // keys per scan CTA
 constexpr int kFusedMaxKeys = 32768;
+constexpr int kFusedSmallMaxKeys = 4096;  // longest cache of the fused schedule below kFusedMinProblems
+constexpr int kFusedMinProblems = 148;
 constexpr int kCandSmem = 12288;         // candidates selected in shared memory
 constexpr int kScanThreads = 512;
 constexpr int kGroupsInFlight = 4;
@@ -853,6 +855,137 @@ __global__ void __launch_bounds__(kThreads) decode_prep_kernel(const DecodeParam
     p.ws_ctrl[(size_t)prob * CTRL_WORDS + CTRL_T0 + part] = t0 > 1u ? t0 : 1u;
     if (part == 0) stamp(p, prob, 1);
   }
+}
+
+// Wide prep: one CTA per problem, for launches with many problems.  The 4-CTA prep above stages
+// its inputs in ~200 KB of shared memory per CTA to minimise the latency of a single decode; with
+// hundreds of problems per launch that leaves one CTA per SM.  Here each problem's q_low and LUT
+// come out of the same canonical arithmetic with the weights read from L2, and the threshold from
+// a sample of kWideSample keys (kWideRuns evenly spaced runs), so a CTA needs ~50 KB and several
+// problems share an SM.  The threshold rule is the 4-CTA prep's with one part and one extra rank
+// of margin for the smaller sample; as there, it only sizes the candidate set.
+constexpr int kWidePrepThreads = 256;
+constexpr int kWideRuns = 64;
+constexpr int kWideRunKeys = 128;
+constexpr int kWideSample = kWideRuns * kWideRunKeys;
+
+__host__ __device__ inline int wide_prep_smem_bytes() {
+  return static_cast<int>(sizeof(SelectScratch)) + 4 * (kMaxHeadDim + kMaxRank + kMaxLut + kWideSample);
+}
+
+template <typename T, bool kB>
+__global__ void __launch_bounds__(kWidePrepThreads, 2) decode_prep_wide_kernel(const DecodeParams p) {
+  extern __shared__ __align__(16) unsigned char wdyn[];
+  SelectScratch& sel = *reinterpret_cast<SelectScratch*>(wdyn);
+  float* qf = reinterpret_cast<float*>(wdyn + sizeof(SelectScratch));
+  float* ql = qf + kMaxHeadDim;
+  float* lut = ql + kMaxRank;
+  uint32_t* skeys = reinterpret_cast<uint32_t*>(lut + kMaxLut);
+  const int prob = blockIdx.x;
+  const ProbIdx pi = prob_index<kB>(p, prob);
+  const int b = pi.b, h = pi.h, t = pi.t;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int D = p.a.head_dim, R = p.a.rank_dim, S2 = p.a.subspaces, C = p.a.codewords;
+  const int SC = S2 * C;
+  pdl_launch_dependents();
+  const int64_t len_t = allowed_length<kB>(p, b, t);
+  const uint8_t* codes = codes_base<kB>(p, b, h);
+  {
+    const T* q = query_row<T, kB>(p, b, h, t);
+    if (p.q_host)
+      for (int d = tid; d < D; d += blockDim.x) qf[d] = to_f32<T>(q[d]);
+    pdl_wait();
+    if (!p.q_host)
+      for (int d = tid; d < D; d += blockDim.x) qf[d] = to_f32<T>(q[d]);
+  }
+  __syncthreads();
+  const float* qp = p.a.q_proj + (size_t)h * D * R;
+  for (int r = tid; r < R; r += blockDim.x) {
+    float acc = 0.f;
+    for (int d = 0; d < D; ++d) acc = mac(acc, qf[d], __ldg(qp + d * R + r));
+    ql[r] = __fmul_rn(acc, __ldg(p.a.scale + h));
+  }
+  __syncthreads();
+  const float* lo = p.a.lut_override ? p.a.lut_override + (size_t)prob * SC : nullptr;
+  query_lut<false>(R, S2, C, p.a.codebooks + (size_t)h * C * R, lo, ql, lut);
+  {
+    float* gl = p.ws_lut + (size_t)prob * kMaxLut;
+    for (int e = tid; e < SC; e += blockDim.x) gl[e] = lut[e];
+    for (int r = tid; r < R; r += blockDim.x) p.ws_qlow[(size_t)prob * kMaxRank + r] = ql[r];
+    if (tid == 0) {
+      p.ws_ctrl[(size_t)prob * CTRL_WORDS + CTRL_NCAND] = 0u;
+      p.ws_ctrl[(size_t)prob * CTRL_WORDS + CTRL_MAXKEY] = 0u;
+    }
+  }
+  // sample: kWideRuns runs of kWideRunKeys keys evenly spaced over the allowed range
+  int nv = 0;
+  float smin = INFINITY, smax = -INFINITY;
+  for (int i = tid; i < kWideSample; i += blockDim.x) {
+    const int run = i / kWideRunKeys, off = i - run * kWideRunKeys;
+    const int64_t key = ((len_t * run) / kWideRuns) + off;
+    const uint32_t k = (key < len_t) ? adc_key<kB>(p, codes, lut, b, t, key, len_t) : 0u;
+    skeys[i] = k;
+    if (k != 0u) {
+      const float sc = key_to_float(k);
+      smin = fminf(smin, sc);
+      smax = fmaxf(smax, sc);
+      ++nv;
+    }
+  }
+  nv = __reduce_add_sync(0xFFFFFFFFu, nv);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    smin = fminf(smin, __shfl_xor_sync(0xFFFFFFFFu, smin, o));
+    smax = fmaxf(smax, __shfl_xor_sync(0xFFFFFFFFu, smax, o));
+  }
+  if (lane == 0) {
+    sel.warp_tot[1][warp] = nv;
+    sel.lo_part[warp] = __float_as_uint(smin);
+    sel.hi_part[warp] = __float_as_uint(smax);
+  }
+  for (int bn = tid; bn < kSelectBins; bn += blockDim.x) sel.hist[0][bn] = 0u;
+  __syncthreads();
+  {
+    const int nw = blockDim.x >> 5;
+    int c = lane < nw ? sel.warp_tot[1][lane] : 0;
+    float a = lane < nw ? __uint_as_float(static_cast<uint32_t>(sel.lo_part[lane])) : INFINITY;
+    float bb = lane < nw ? __uint_as_float(static_cast<uint32_t>(sel.hi_part[lane])) : -INFINITY;
+    c = __reduce_add_sync(0xFFFFFFFFu, c);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      a = fminf(a, __shfl_xor_sync(0xFFFFFFFFu, a, o));
+      bb = fmaxf(bb, __shfl_xor_sync(0xFFFFFFFFu, bb, o));
+    }
+    nv = c;
+    smin = a;
+    smax = bb;
+  }
+  // samples can repeat keys when the range is shorter than the sample; they only size the set
+  const int n_s = nv;
+  const int64_t k_est = imin64(p.sl_cap, len_t);
+  const int64_t r = len_t > 0 ? (2 * k_est * n_s + len_t - 1) / len_t + 1 : 0;
+  uint32_t t0 = 1u;
+  const float span = smax - smin;
+  if (n_s > 0 && r >= 1 && r < n_s && len_t > kWideSample && isfinite(span)) {
+    if (!(span > 0.f)) {
+      t0 = ordered_key(smin);
+    } else {
+      const float scale = (static_cast<float>(kSelectBins) - 0.5f) / span;
+      uint32_t* hist = sel.hist[0];
+      for (int i = tid; i < kWideSample; i += blockDim.x) {
+        const uint32_t kk = skeys[i];
+        if (kk != 0u) {
+          const float x = __fmul_rn(__fsub_rn(key_to_float(kk), smin), scale);
+          atomicAdd(&hist[x > 0.f ? static_cast<int>(fminf(x, static_cast<float>(kSelectBins - 1))) : 0], 1u);
+        }
+      }
+      __syncthreads();
+      (void)select_find_bin(hist, static_cast<int>(r), &sel, 0);
+      const int bstar = sel.digit[0];
+      t0 = ordered_key(bstar >= 1 ? __fadd_rn(smin, __fdiv_rn(static_cast<float>(bstar - 1), scale)) : smin);
+    }
+  }
+  if (tid < kPrepCtas) p.ws_ctrl[(size_t)prob * CTRL_WORDS + CTRL_T0 + tid] = t0 > 1u ? t0 : 1u;
 }
 
 // LUT lookup of key j in the bank-replicated table: entry e lives at lut[e * 32 + lane], so
@@ -1700,20 +1833,30 @@ static int plan_decode(const sva_decode_args* a, DecodePlan* plan, bool force_gr
                     ? 1
                     : 0;
   const int64_t P = p.n_probs;
-  p.grid_mode = (force_grid || a->key_len > kFusedMaxKeys) ? 1 : 0;
-  if (p.grid_mode && P > 65535)
-    return set_error(SVA_ERR_SHAPE, "over 32768 keys, n_seqs * n_heads * n_queries must be <= 65535 per call");
-  p.nseg = static_cast<int>((a->key_len + kScanKeys - 1) / kScanKeys);
+  // a few problems over a long-ish cache decode faster spread over the whole GPU (grid) than in
+  // one CTA each (fused); many problems (prefill) keep the fused schedule
+  p.grid_mode = (force_grid || a->key_len > kFusedMaxKeys ||
+                 (P < kFusedMinProblems && a->key_len > kFusedSmallMaxKeys))
+                    ? 1
+                    : 0;
   int dbg_cap = 1;
   if (a->shortlist_out || a->final_out)
     while (dbg_cap < p.sl_cap) dbg_cap <<= 1;
-  size_t ws = 0;
   if (!p.grid_mode) {
+    // one CTA per problem keeps every key's ADC key in shared memory; larger shortlists and
+    // caches than fit go to the grid schedule
     const int stage_bytes = 4 * a->head_dim * a->rank_dim;
     int cache_bytes = std::max<int>(static_cast<int>(4 * a->key_len), stage_bytes);
     cache_bytes = std::max(cache_bytes, 8 * dbg_cap);
     p.lay = decode_smem_layout(a->head_dim, p.sl_cap, p.b_cap, cache_bytes);
     plan->smem_bytes = static_cast<size_t>(p.lay.total);
+    if (p.lay.total > kMaxDynSmem) p.grid_mode = 1;
+  }
+  if (p.grid_mode && P > 65535)
+    return set_error(SVA_ERR_SHAPE, "in the grid schedule, n_seqs * n_heads * n_queries must be <= 65535 per call");
+  p.nseg = static_cast<int>((a->key_len + kScanKeys - 1) / kScanKeys);
+  size_t ws = 0;
+  if (!p.grid_mode) {
   } else {
     // the candidate area later holds the budget select's composites and the shortlist logits
     const int cand_entries = finish_cand_entries(p.sl_cap, dbg_cap);
@@ -1774,6 +1917,22 @@ static int launch_prep(const DecodeParams& p, int P, const PrepSmem& lay, cudaSt
   return e == cudaSuccess ? SVA_OK : set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
 }
 
+// The scan launch for the codes' layout (vector loads for 1, 2, 4 or 8 subspaces).
+static int launch_scan_for(const DecodeParams& p, int P, cudaStream_t stream) {
+  const int C = p.a.codewords;
+  int rc;
+  switch (p.vec_codes ? p.a.subspaces : 0) {
+    case 1: rc = C == 256 ? launch_scan<1, 256>(p, P, stream) : launch_scan<1, 0>(p, P, stream); break;
+    case 2: rc = C == 128 ? launch_scan<2, 128>(p, P, stream) : launch_scan<2, 0>(p, P, stream); break;
+    case 4: rc = C == 64 ? launch_scan<4, 64>(p, P, stream) : launch_scan<4, 0>(p, P, stream); break;
+    case 8: rc = C == 32 ? launch_scan<8, 32>(p, P, stream) : launch_scan<8, 0>(p, P, stream); break;
+    default: rc = launch_scan<0, 0>(p, P, stream); break;
+  }
+  if (rc != SVA_OK) return rc;
+  profile_mark(1, stream);
+  return SVA_OK;
+}
+
 // Points the planned workspace offsets at `ws`.
 static void bind_workspace(DecodeParams& p, void* ws) {
   char* base = static_cast<char*>(ws);
@@ -1788,6 +1947,16 @@ template <typename T>
 static int launch_prep_scan(DecodeParams& p, cudaStream_t stream) {
   const int P = p.n_probs;
   int rc;
+  if (P >= kWideMinProblems) {
+    auto k = p.batched ? decode_prep_wide_kernel<T, true> : decode_prep_wide_kernel<T, false>;
+    const int smem = wide_prep_smem_bytes();
+    rc = ensure_smem_attr(reinterpret_cast<const void*>(k), smem);
+    if (rc != SVA_OK) return rc;
+    const cudaError_t e = launch_dependent(k, dim3(P), dim3(kWidePrepThreads), smem, stream, p);
+    if (e != cudaSuccess) return set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
+    profile_mark(0, stream);
+    return launch_scan_for(p, P, stream);
+  }
   const int D = p.a.head_dim, R = p.a.rank_dim, C = p.a.codewords, S = p.a.subspaces;
   const bool prep_vec = p.vec_codes && prep_smem_layout(D, R, C, S, false).total <= kPrepSmemLimit;
   const bool want_rep = prep_vec && S * C <= kRepEntries;
@@ -1802,16 +1971,7 @@ static int launch_prep_scan(DecodeParams& p, cudaStream_t stream) {
   }
   if (rc != SVA_OK) return rc;
   profile_mark(0, stream);
-  switch (p.vec_codes ? p.a.subspaces : 0) {
-    case 1: rc = C == 256 ? launch_scan<1, 256>(p, P, stream) : launch_scan<1, 0>(p, P, stream); break;
-    case 2: rc = C == 128 ? launch_scan<2, 128>(p, P, stream) : launch_scan<2, 0>(p, P, stream); break;
-    case 4: rc = C == 64 ? launch_scan<4, 64>(p, P, stream) : launch_scan<4, 0>(p, P, stream); break;
-    case 8: rc = C == 32 ? launch_scan<8, 32>(p, P, stream) : launch_scan<8, 0>(p, P, stream); break;
-    default: rc = launch_scan<0, 0>(p, P, stream); break;
-  }
-  if (rc != SVA_OK) return rc;
-  profile_mark(1, stream);
-  return SVA_OK;
+  return launch_scan_for(p, P, stream);
 }
 
 template <typename T>

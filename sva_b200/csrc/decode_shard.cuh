@@ -27,88 +27,120 @@
 namespace sva {
 
 constexpr int kShardMaxShortlist = 8192;
+constexpr int kShardMaxWorld = 64;
 
-// Stage 1, after prep + scan: the exact local shortlist as global composites.
+// Local key index <-> global key index of one rank.  Key-range shards: global = key_offset +
+// local.  Page-dealt shards (page_world > 0): the pages of every sequence are dealt round-robin,
+// global page g to rank g % page_world, so local page lp of this rank is global page
+// lp * page_world + page_rank, and rows keep their offset inside the page.
+struct ShardMap {
+  int64_t key_offset;
+  int page_world, page_rank, page_shift;
+  __device__ __forceinline__ uint32_t to_global(int64_t l) const {
+    if (page_world <= 0) return static_cast<uint32_t>(key_offset + l);
+    const int64_t mask = (int64_t{1} << page_shift) - 1;
+    return static_cast<uint32_t>((((l >> page_shift) * page_world + page_rank) << page_shift) | (l & mask));
+  }
+  __device__ __forceinline__ int64_t to_local(uint32_t g) const {
+    if (page_world <= 0) return static_cast<int64_t>(g) - key_offset;
+    const int64_t mask = (int64_t{1} << page_shift) - 1;
+    return (((static_cast<int64_t>(g) >> page_shift) / page_world) << page_shift) | (static_cast<int64_t>(g) & mask);
+  }
+};
+
+// Stage 1, after prep + scan: this rank's exact local top-k1 (k1 = p.sl_cap) of every problem as
+// global composites, zero padded.
+template <bool kB>
 __global__ void __launch_bounds__(kThreads)
-    shard_top_kernel(const DecodeParams p, int64_t key_offset, unsigned long long* __restrict__ top_out) {
+    shard_top_kernel(const DecodeParams p, const ShardMap map, int k1, unsigned long long* __restrict__ top_out) {
   extern __shared__ __align__(16) unsigned char smem[];
   uint2* cand = reinterpret_cast<uint2*>(smem);  // kCandSmem entries
   __shared__ float lut[kMaxLut];
   __shared__ SelectScratch sc;
   __shared__ int scratch[64];
   const int prob = blockIdx.x;
-  const int h = prob / p.a.n_queries, t = prob - h * p.a.n_queries;
-  const int64_t len_t = allowed_length<false>(p, 0, t);
-  const int SL = p.a.shortlist;
-  unsigned long long* out = top_out + (size_t)prob * SL;
-  const uint32_t off = static_cast<uint32_t>(key_offset);
-  int32_t* idx = reinterpret_cast<int32_t*>(smem + kCandSmem * sizeof(uint2));  // SL entries
-  const int n = select_shortlist<false>(p, prob, 0, h, t, len_t, cand, lut, &sc, scratch, idx, out, true);
-  for (int j = threadIdx.x; j < SL; j += blockDim.x)
-    out[j] = j < n ? composite(static_cast<uint32_t>(out[j] >> 32), static_cast<uint32_t>(idx[j]) + off) : 0ull;
+  const ProbIdx pi = prob_index<kB>(p, prob);
+  const int64_t len_t = allowed_length<kB>(p, pi.b, pi.t);
+  unsigned long long* out = top_out + (size_t)prob * k1;
+  int32_t* idx = reinterpret_cast<int32_t*>(smem + kCandSmem * sizeof(uint2));  // k1 entries
+  pdl_wait();
+  const int n = select_shortlist<kB>(p, prob, pi.b, pi.h, pi.t, len_t, cand, lut, &sc, scratch, idx, out, true);
+  for (int j = threadIdx.x; j < k1; j += blockDim.x)
+    out[j] = j < n ? composite(static_cast<uint32_t>(out[j] >> 32), map.to_global(idx[j])) : 0ull;
 }
 
 // Item functors of the shard kernels (plain structs: lambdas here trip the compiler's front end).
 struct GatheredTop {
   const unsigned long long* g;
-  int P, SL, prob, base;
+  int P, K, prob, base;
   __device__ unsigned long long operator()(int i) const {
     const int ii = base + i;
-    const int r = ii / SL, j = ii - r * SL;
-    return __ldcg(g + ((size_t)r * P + prob) * SL + j);
+    const int r = ii / K, j = ii - r * K;
+    return __ldcg(g + ((size_t)r * P + prob) * K + j);
   }
 };
 
 struct OwnShortlistEmit {
   int32_t* rows;
   uint32_t* gidx;
-  uint32_t off;
+  ShardMap map;
   __device__ void operator()(int pos, int, unsigned long long c) const {
     const uint32_t g = ~static_cast<uint32_t>(c);
     gidx[pos] = g;
-    rows[pos] = static_cast<int32_t>(g - off);
+    rows[pos] = static_cast<int32_t>(map.to_local(g));
   }
 };
 
-// Stage 2: global shortlist from the gathered top lists; rescore + logits of this rank's members.
-template <typename T>
+// Stage 2: the global shortlist (top-min(SL, non-zero) of the W x k1 gathered composites); this
+// rank rescores its own members and computes their verify logits -> records [P][k1] of (rank
+// composite lo, hi, logit bits, 0).  A rank that sent k1 entries all inside the global shortlist
+// may hold more members it did not send: the problem is then flagged in *saturated and the host
+// repeats the exchange with k1 = SL.
+template <typename T, bool kB>
 __global__ void __launch_bounds__(kThreads)
-    shard_rescore_kernel(const DecodeParams p, int64_t key_offset, int world, int rank,
-                         const unsigned long long* __restrict__ gathered, uint4* __restrict__ records) {
+    shard_rescore_kernel(const DecodeParams p, const ShardMap map, int world, int rank, int k1,
+                         const unsigned long long* __restrict__ gathered, uint4* __restrict__ records,
+                         int* __restrict__ saturated) {
   extern __shared__ __align__(16) unsigned char smem[];
-  const int SL = p.a.shortlist;
   int32_t* rows = reinterpret_cast<int32_t*>(smem);
-  uint32_t* gidx = reinterpret_cast<uint32_t*>(rows + SL);
-  uint32_t* rk = gidx + SL;
-  float* lg = reinterpret_cast<float*>(rk + SL);
+  uint32_t* gidx = reinterpret_cast<uint32_t*>(rows + k1);
+  uint32_t* rk = gidx + k1;
+  float* lg = reinterpret_cast<float*>(rk + k1);
   __shared__ float qf[kMaxHeadDim];
   __shared__ float ql[kMaxRank];
   __shared__ SelectScratch sc;
   __shared__ int scratch[64];
+  __shared__ int per_rank[kShardMaxWorld];
   const int prob = blockIdx.x;
-  const int h = prob / p.a.n_queries, t = prob - h * p.a.n_queries;
+  const ProbIdx pi = prob_index<kB>(p, prob);
+  const int b = pi.b, h = pi.h, t = pi.t;
   const int kvh = h / p.groups;
   const int P = p.n_probs;
   const int tid = threadIdx.x;
   {
-    const T* q = reinterpret_cast<const T*>(p.a.query) + h * p.a.q_head_stride + t * p.a.q_row_stride;
+    const T* q = query_row<T, kB>(p, b, h, t);
     for (int d = tid; d < p.a.head_dim; d += blockDim.x) qf[d] = to_f32<T>(q[d]);
     for (int r = tid; r < p.a.rank_dim; r += blockDim.x) ql[r] = __ldcg(p.ws_qlow + (size_t)prob * kMaxRank + r);
+    for (int r = tid; r < world; r += blockDim.x) per_rank[r] = 0;
   }
-  const GatheredTop item{gathered, P, SL, prob, 0};
-  const int N = world * SL;
+  const GatheredTop item{gathered, P, k1, prob, 0};
+  const int N = world * k1;
   int nz = 0;
   for (int i = tid; i < N; i += blockDim.x) nz += item(i) != 0ull;
   nz = block_sum_int(nz, scratch);
-  const int k = min(SL, nz);
+  const int k = min(p.a.shortlist, nz);
   const SelectThreshold thr = cta_radix_select(item, N, k, &sc);
-  const GatheredTop own{gathered, P, SL, prob, rank * SL};
-  const int m = cta_compact(own, SL, thr, OwnShortlistEmit{rows, gidx, static_cast<uint32_t>(key_offset)}, scratch);
-  rescore_rows<8, false>(p, 0, h, ql, rows, m, rk);
-  verify_logits<T>(p.a.keys, p.a.k_head_stride, p.a.k_row_stride, kvh, qf, p.a.head_dim, rows, m, p.a.softmax_scale,
-                   p.a.logits_mode, lg);
-  uint4* out = records + (size_t)prob * SL;
-  for (int j = tid; j < SL; j += blockDim.x) {
+  // members per rank; a rank whose k1 sent entries are all members may hold unsent members
+  for (int i = tid; i < N; i += blockDim.x)
+    if (is_selected(thr, item(i))) atomicAdd(&per_rank[i / k1], 1);
+  __syncthreads();
+  if (tid < world && per_rank[tid] == k1 && k1 < p.a.shortlist && saturated) atomicOr(saturated, 1);
+  const GatheredTop own{gathered, P, k1, prob, rank * k1};
+  const int m = cta_compact(own, k1, thr, OwnShortlistEmit{rows, gidx, map}, scratch);
+  rescore_rows<8, kB>(p, b, h, ql, rows, m, rk);
+  verify_logits_fn<T>(k_rows<T, kB>(p, b, kvh, rows), qf, p.a.head_dim, m, p.a.softmax_scale, p.a.logits_mode, lg);
+  uint4* out = records + (size_t)prob * k1;
+  for (int j = tid; j < k1; j += blockDim.x) {
     if (j < m) {
       const unsigned long long c = composite(rk[j], gidx[j]);
       out[j] = make_uint4(static_cast<uint32_t>(c), static_cast<uint32_t>(c >> 32), __float_as_uint(lg[j]), 0u);
@@ -118,11 +150,11 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
-// Stage 3: global budget set and softmax from the gathered records; fp64 partial output of this
-// rank's final keys.
-template <typename T>
+// Stage 3: global budget set and softmax from the gathered records [W][P][k1]; fp64 partial
+// output of this rank's final keys.
+template <typename T, bool kB>
 __global__ void __launch_bounds__(kThreads)
-    shard_verify_kernel(const DecodeParams p, int64_t key_offset, int world, int rank,
+    shard_verify_kernel(const DecodeParams p, const ShardMap map, int world, int rank, int k1,
                         const uint4* __restrict__ gathered, double* __restrict__ partial_out) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int B = p.a.budget;
@@ -133,42 +165,41 @@ __global__ void __launch_bounds__(kThreads)
   __shared__ SelectScratch sc;
   __shared__ int scratch[64];
   const int prob = blockIdx.x;
-  const int h = prob / p.a.n_queries, t = prob - h * p.a.n_queries;
+  const ProbIdx pi = prob_index<kB>(p, prob);
+  const int b = pi.b, h = pi.h;
   const int kvh = h / p.groups;
   const int P = p.n_probs;
-  const int SL = p.a.shortlist;
   const int D = p.a.head_dim;
   const int tid = threadIdx.x;
   auto rec = [&](int i) -> uint4 {
-    const int r = i / SL, j = i - r * SL;
-    return __ldcg(gathered + ((size_t)r * P + prob) * SL + j);
+    const int r = i / k1, j = i - r * k1;
+    return __ldcg(gathered + ((size_t)r * P + prob) * k1 + j);
   };
   auto item = [&](int i) -> unsigned long long {
     const uint4 v = rec(i);
     return (static_cast<unsigned long long>(v.y) << 32) | v.x;
   };
-  const int N = world * SL;
+  const int N = world * k1;
   int nz = 0;
   for (int i = tid; i < N; i += blockDim.x) nz += item(i) != 0ull;
   const int n_sl = block_sum_int(nz, scratch);
-  const int b = min(B, n_sl);
-  const SelectThreshold thr = cta_radix_select(item, N, b, &sc);
+  const int nb = min(B, n_sl);
+  const SelectThreshold thr = cta_radix_select(item, N, nb, &sc);
   const int n_fin = cta_compact(item, N, thr,
                                 [&](int pos, int i, unsigned long long) { lgs[pos] = __uint_as_float(rec(i).z); },
                                 scratch);
   float mx, denom;
   softmax_stats(lgs, n_fin, scratch, acc, &mx, &denom);
-  const uint32_t off = static_cast<uint32_t>(key_offset);
-  auto own = [&](int j) -> unsigned long long { return item(rank * SL + j); };
-  const int n_own = cta_compact(own, SL, thr,
+  auto own = [&](int j) -> unsigned long long { return item(rank * k1 + j); };
+  const int n_own = cta_compact(own, k1, thr,
                                 [&](int pos, int j, unsigned long long c) {
-                                  rows[pos] = static_cast<int32_t>(~static_cast<uint32_t>(c) - off);
-                                  const float lj = __uint_as_float(rec(rank * SL + j).z);
+                                  rows[pos] = static_cast<int32_t>(map.to_local(~static_cast<uint32_t>(c)));
+                                  const float lj = __uint_as_float(rec(rank * k1 + j).z);
                                   w[pos] = round_to<T>(expf(lj - mx) / denom);
                                 },
                                 scratch);
   double* sums = acc + (kThreads / 32) * 64;
-  accumulate_rows<T>(p.a.values, p.a.v_head_stride, p.a.v_row_stride, kvh, D, rows, w, n_own, acc, sums);
+  accumulate_rows_fn<T>(v_rows<T, kB>(p, b, kvh, rows), D, w, n_own, acc, sums);
   for (int d = tid; d < D; d += blockDim.x) partial_out[(size_t)prob * D + d] = sums[d];
   if (p.a.stats && rank == 0 && tid == 0) {
     atomicAdd(p.a.stats + SVA_STAT_QUERIES, 1ull);
@@ -179,13 +210,13 @@ __global__ void __launch_bounds__(kThreads)
 }
 
 // Stage 4: the output, summing the ranks' partials in rank order.
-template <typename T>
+template <typename T, bool kB>
 __global__ void shard_combine_kernel(const DecodeParams p, int world, const double* __restrict__ gathered) {
   const int prob = blockIdx.x;
-  const int h = prob / p.a.n_queries, t = prob - h * p.a.n_queries;
+  const ProbIdx pi = prob_index<kB>(p, prob);
   const int P = p.n_probs;
   const int D = p.a.head_dim;
-  T* out = reinterpret_cast<T*>(p.a.out) + h * p.a.out_head_stride + t * p.a.out_row_stride;
+  T* out = out_row<T, kB>(p, pi.b, pi.h, pi.t);
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     double tot = 0.0;
     for (int r = 0; r < world; ++r) tot += __ldcg(gathered + ((size_t)r * P + prob) * D + d);
@@ -193,20 +224,41 @@ __global__ void shard_combine_kernel(const DecodeParams p, int world, const doub
   }
 }
 
-static int plan_shard(const sva_decode_args* a, int64_t key_offset, DecodePlan* plan) {
-  int rc = plan_decode(a, plan, /*force_grid=*/true);
+// Plans one rank's stages.  k1 = entries each rank exchanges per problem (0: the shortlist).
+static int plan_shard(const sva_decode_args* a, const sva_batch_layout* layout, const sva_shard_map* m, int k1,
+                      DecodePlan* plan, ShardMap* map) {
+  if (a && (a->shortlist > kShardMaxShortlist))
+    return set_error(SVA_ERR_SHAPE, "shards take shortlist <= 8192");
+  if (a && (k1 < 0 || k1 > a->shortlist)) return set_error(SVA_ERR_SHAPE, "exchange width must be in 0..shortlist");
+  // the local decode keeps the local top-k1, not the global shortlist
+  sva_decode_args local = a ? *a : sva_decode_args{};
+  if (a && k1 > 0) local.shortlist = k1;
+  int rc = plan_decode(a ? &local : nullptr, plan, /*force_grid=*/true, layout);
   if (rc != SVA_OK) return rc;
+  plan->p.a.shortlist = a->shortlist;  // the global shortlist, for the rescore stage
   if (a->n_queries != 1) return set_error(SVA_ERR_SHAPE, "shards decode one query token per head (n_queries == 1)");
   if (a->allowed_len || a->allowed_mask) return set_error(SVA_ERR_SHAPE, "shards take no allowed_len / allowed_mask");
   if (a->shortlist_out || a->final_out) return set_error(SVA_ERR_SHAPE, "shards write no shortlist_out / final_out");
-  if (a->shortlist > kShardMaxShortlist) return set_error(SVA_ERR_SHAPE, "shards take shortlist <= 8192");
-  if (key_offset < 0 || key_offset + a->key_len > 0x7FFFFFFFll)
+  map->key_offset = m ? m->key_offset : 0;
+  map->page_world = m ? m->page_world : 0;
+  map->page_rank = m ? m->page_rank : 0;
+  map->page_shift = plan->p.page_table ? plan->p.page_shift : 0;
+  if (map->page_world > 0) {
+    if (!plan->p.page_table) return set_error(SVA_ERR_SHAPE, "page-dealt shards need a paged layout");
+    if (map->page_rank < 0 || map->page_rank >= map->page_world)
+      return set_error(SVA_ERR_SHAPE, "need 0 <= page_rank < page_world");
+    if (((a->key_len + (int64_t{1} << map->page_shift) - 1) >> map->page_shift) * map->page_world
+            << map->page_shift > 0x7FFFFFFFll)
+      return set_error(SVA_ERR_SHAPE, "global key indices must stay below 2^31");
+  } else if (map->key_offset < 0 || map->key_offset + a->key_len > 0x7FFFFFFFll) {
     return set_error(SVA_ERR_SHAPE, "key_offset + key_len must be in 0..2^31-1");
+  }
   return SVA_OK;
 }
 
 static int shard_world_ok(int32_t world, int32_t rank) {
-  if (world < 1 || rank < 0 || rank >= world) return set_error(SVA_ERR_SHAPE, "need 0 <= rank < world");
+  if (world < 1 || world > kShardMaxWorld || rank < 0 || rank >= world)
+    return set_error(SVA_ERR_SHAPE, "need 0 <= rank < world <= 64");
   return SVA_OK;
 }
 
@@ -215,122 +267,177 @@ static int launch_status() {
   return e == cudaSuccess ? SVA_OK : set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
 }
 
+static int k1_of(const DecodePlan& plan, int k1) { return k1 > 0 ? k1 : plan.p.a.shortlist; }
+
 template <typename T>
-static int shard_summon(DecodePlan& plan, int64_t key_offset, unsigned long long* top_out, void* ws, cudaStream_t st) {
+static int shard_summon(DecodePlan& plan, const ShardMap& map, int k1, unsigned long long* top_out, void* ws,
+                        cudaStream_t st) {
   DecodeParams& p = plan.p;
   bind_workspace(p, ws);
   p.dbg_ts = nullptr;
   int rc = launch_prep_scan<T>(p, st);
   if (rc != SVA_OK) return rc;
-  const int smem = kCandSmem * static_cast<int>(sizeof(uint2)) + 4 * p.a.shortlist;
-  rc = ensure_smem_attr(reinterpret_cast<const void*>(shard_top_kernel), smem);
+  k1 = k1_of(plan, k1);
+  const int smem = kCandSmem * static_cast<int>(sizeof(uint2)) + 4 * k1;
+  auto k = p.batched ? shard_top_kernel<true> : shard_top_kernel<false>;
+  rc = ensure_smem_attr(reinterpret_cast<const void*>(k), smem);
   if (rc != SVA_OK) return rc;
-  shard_top_kernel<<<p.a.n_heads, kThreads, smem, st>>>(p, key_offset, top_out);
+  const cudaError_t e = launch_dependent(k, dim3(p.n_probs), dim3(kThreads), smem, st, p, map, k1, top_out);
+  if (e != cudaSuccess) return set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
   profile_mark(2, st);
   return launch_status();
 }
 
 template <typename T>
-static int shard_rescore(DecodePlan& plan, int64_t key_offset, int world, int rank, const unsigned long long* gathered,
-                         uint4* records, void* ws, cudaStream_t st) {
+static int shard_rescore(DecodePlan& plan, const ShardMap& map, int world, int rank, int k1,
+                         const unsigned long long* gathered, uint4* records, int* saturated, void* ws,
+                         cudaStream_t st) {
   DecodeParams& p = plan.p;
   bind_workspace(p, ws);
-  const int smem = 16 * p.a.shortlist;
-  int rc = ensure_smem_attr(reinterpret_cast<const void*>(shard_rescore_kernel<T>), smem);
+  k1 = k1_of(plan, k1);
+  const int smem = 16 * k1;
+  auto k = p.batched ? shard_rescore_kernel<T, true> : shard_rescore_kernel<T, false>;
+  int rc = ensure_smem_attr(reinterpret_cast<const void*>(k), smem);
   if (rc != SVA_OK) return rc;
-  shard_rescore_kernel<T><<<p.a.n_heads, kThreads, smem, st>>>(p, key_offset, world, rank, gathered, records);
+  k<<<p.n_probs, kThreads, smem, st>>>(p, map, world, rank, k1, gathered, records, saturated);
   return launch_status();
 }
 
 template <typename T>
-static int shard_verify(DecodePlan& plan, int64_t key_offset, int world, int rank, const uint4* gathered,
+static int shard_verify(DecodePlan& plan, const ShardMap& map, int world, int rank, int k1, const uint4* gathered,
                         double* partial, cudaStream_t st) {
   DecodeParams& p = plan.p;
+  k1 = k1_of(plan, k1);
   const int smem = 8 * ((kThreads / 32) * 64 + kMaxHeadDim) + 12 * p.a.budget;
-  int rc = ensure_smem_attr(reinterpret_cast<const void*>(shard_verify_kernel<T>), smem);
+  auto k = p.batched ? shard_verify_kernel<T, true> : shard_verify_kernel<T, false>;
+  int rc = ensure_smem_attr(reinterpret_cast<const void*>(k), smem);
   if (rc != SVA_OK) return rc;
-  shard_verify_kernel<T><<<p.a.n_heads, kThreads, smem, st>>>(p, key_offset, world, rank, gathered, partial);
+  k<<<p.n_probs, kThreads, smem, st>>>(p, map, world, rank, k1, gathered, partial);
   return launch_status();
 }
 
 template <typename T>
 static int shard_combine(DecodePlan& plan, int world, const double* gathered, cudaStream_t st) {
-  shard_combine_kernel<T><<<plan.p.a.n_heads, 128, 0, st>>>(plan.p, world, gathered);
+  auto k = plan.p.batched ? shard_combine_kernel<T, true> : shard_combine_kernel<T, false>;
+  k<<<plan.p.n_probs, 128, 0, st>>>(plan.p, world, gathered);
   return launch_status();
 }
 
 }  // namespace sva
 
-extern "C" size_t sva_shard_workspace_size(const sva_decode_args* args) {
+#define SVA_SHARD_DISPATCH(call) \
+  switch (args->qkv_dtype) {     \
+    case SVA_DTYPE_F32: return call(float);           \
+    case SVA_DTYPE_BF16: return call(__nv_bfloat16);   \
+    default: return call(__half);                      \
+  }
+
+extern "C" size_t sva_shard_batched_workspace_size(const sva_decode_args* args, const sva_batch_layout* layout,
+                                                   const sva_shard_map* map, int32_t exchange_width) {
   sva::DecodePlan plan;
-  if (sva::plan_shard(args, 0, &plan) != SVA_OK) return 0;
+  sva::ShardMap m;
+  if (!args || sva::plan_shard(args, layout, map, exchange_width, &plan, &m) != SVA_OK) return 0;
   return plan.ws_bytes;
 }
 
-extern "C" int sva_shard_summon(const sva_decode_args* args, int64_t key_offset, uint64_t* top_out, void* workspace,
-                                size_t workspace_bytes, void* stream) {
+extern "C" int sva_shard_batched_summon(const sva_decode_args* args, const sva_batch_layout* layout,
+                                        const sva_shard_map* map, int32_t exchange_width, uint64_t* top_out,
+                                        void* workspace, size_t workspace_bytes, void* stream) {
+  if (!args) return sva::set_error(SVA_ERR_SHAPE, "null args");
   sva::DecodePlan plan;
-  int rc = sva::plan_shard(args, key_offset, &plan);
+  sva::ShardMap m;
+  int rc = sva::plan_shard(args, layout, map, exchange_width, &plan, &m);
   if (rc != SVA_OK) return rc;
   if (!top_out) return sva::set_error(SVA_ERR_SHAPE, "top_out is null");
   if (workspace_bytes < plan.ws_bytes || !workspace)
-    return sva::set_error(SVA_ERR_WORKSPACE, "workspace smaller than sva_shard_workspace_size()");
+    return sva::set_error(SVA_ERR_WORKSPACE, "workspace smaller than sva_shard_batched_workspace_size()");
   auto* top = reinterpret_cast<unsigned long long*>(top_out);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  switch (args->qkv_dtype) {
-    case SVA_DTYPE_F32: return sva::shard_summon<float>(plan, key_offset, top, workspace, s);
-    case SVA_DTYPE_BF16: return sva::shard_summon<__nv_bfloat16>(plan, key_offset, top, workspace, s);
-    default: return sva::shard_summon<__half>(plan, key_offset, top, workspace, s);
-  }
+#define CALL(T) sva::shard_summon<T>(plan, m, exchange_width, top, workspace, s)
+  SVA_SHARD_DISPATCH(CALL)
+#undef CALL
 }
 
-extern "C" int sva_shard_rescore(const sva_decode_args* args, int64_t key_offset, int32_t world, int32_t rank,
-                                 const uint64_t* gathered_top, uint32_t* records_out, void* workspace,
-                                 size_t workspace_bytes, void* stream) {
+extern "C" int sva_shard_batched_rescore(const sva_decode_args* args, const sva_batch_layout* layout,
+                                         const sva_shard_map* map, int32_t exchange_width, int32_t world,
+                                         int32_t rank, const uint64_t* gathered_top, uint32_t* records_out,
+                                         int32_t* saturated, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!args) return sva::set_error(SVA_ERR_SHAPE, "null args");
   sva::DecodePlan plan;
-  int rc = sva::plan_shard(args, key_offset, &plan);
+  sva::ShardMap m;
+  int rc = sva::plan_shard(args, layout, map, exchange_width, &plan, &m);
   if (rc == SVA_OK) rc = sva::shard_world_ok(world, rank);
   if (rc != SVA_OK) return rc;
   if (!gathered_top || !records_out) return sva::set_error(SVA_ERR_SHAPE, "null pointer");
   if (workspace_bytes < plan.ws_bytes || !workspace)
-    return sva::set_error(SVA_ERR_WORKSPACE, "workspace smaller than sva_shard_workspace_size()");
+    return sva::set_error(SVA_ERR_WORKSPACE, "workspace smaller than sva_shard_batched_workspace_size()");
   auto* g = reinterpret_cast<const unsigned long long*>(gathered_top);
   auto* r = reinterpret_cast<uint4*>(records_out);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  switch (args->qkv_dtype) {
-    case SVA_DTYPE_F32: return sva::shard_rescore<float>(plan, key_offset, world, rank, g, r, workspace, s);
-    case SVA_DTYPE_BF16: return sva::shard_rescore<__nv_bfloat16>(plan, key_offset, world, rank, g, r, workspace, s);
-    default: return sva::shard_rescore<__half>(plan, key_offset, world, rank, g, r, workspace, s);
-  }
+#define CALL(T) sva::shard_rescore<T>(plan, m, world, rank, exchange_width, g, r, saturated, workspace, s)
+  SVA_SHARD_DISPATCH(CALL)
+#undef CALL
 }
 
-extern "C" int sva_shard_verify(const sva_decode_args* args, int64_t key_offset, int32_t world, int32_t rank,
-                                const uint32_t* gathered_records, double* partial_out, void* stream) {
+extern "C" int sva_shard_batched_verify(const sva_decode_args* args, const sva_batch_layout* layout,
+                                        const sva_shard_map* map, int32_t exchange_width, int32_t world, int32_t rank,
+                                        const uint32_t* gathered_records, double* partial_out, void* stream) {
+  if (!args) return sva::set_error(SVA_ERR_SHAPE, "null args");
   sva::DecodePlan plan;
-  int rc = sva::plan_shard(args, key_offset, &plan);
+  sva::ShardMap m;
+  int rc = sva::plan_shard(args, layout, map, exchange_width, &plan, &m);
   if (rc == SVA_OK) rc = sva::shard_world_ok(world, rank);
   if (rc != SVA_OK) return rc;
   if (!gathered_records || !partial_out) return sva::set_error(SVA_ERR_SHAPE, "null pointer");
   auto* g = reinterpret_cast<const uint4*>(gathered_records);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  switch (args->qkv_dtype) {
-    case SVA_DTYPE_F32: return sva::shard_verify<float>(plan, key_offset, world, rank, g, partial_out, s);
-    case SVA_DTYPE_BF16: return sva::shard_verify<__nv_bfloat16>(plan, key_offset, world, rank, g, partial_out, s);
-    default: return sva::shard_verify<__half>(plan, key_offset, world, rank, g, partial_out, s);
-  }
+#define CALL(T) sva::shard_verify<T>(plan, m, world, rank, exchange_width, g, partial_out, s)
+  SVA_SHARD_DISPATCH(CALL)
+#undef CALL
 }
 
-extern "C" int sva_shard_combine(const sva_decode_args* args, int32_t world, const double* gathered_partials,
-                                 void* stream) {
+extern "C" int sva_shard_batched_combine(const sva_decode_args* args, const sva_batch_layout* layout, int32_t world,
+                                         const double* gathered_partials, void* stream) {
+  if (!args) return sva::set_error(SVA_ERR_SHAPE, "null args");
   sva::DecodePlan plan;
-  int rc = sva::plan_shard(args, 0, &plan);
+  sva::ShardMap m;
+  int rc = sva::plan_shard(args, layout, nullptr, 0, &plan, &m);
   if (rc == SVA_OK) rc = sva::shard_world_ok(world, 0);
   if (rc != SVA_OK) return rc;
   if (!gathered_partials) return sva::set_error(SVA_ERR_SHAPE, "null pointer");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  switch (args->qkv_dtype) {
-    case SVA_DTYPE_F32: return sva::shard_combine<float>(plan, world, gathered_partials, s);
-    case SVA_DTYPE_BF16: return sva::shard_combine<__nv_bfloat16>(plan, world, gathered_partials, s);
-    default: return sva::shard_combine<__half>(plan, world, gathered_partials, s);
-  }
+#define CALL(T) sva::shard_combine<T>(plan, world, gathered_partials, s)
+  SVA_SHARD_DISPATCH(CALL)
+#undef CALL
+}
+
+// The single-sequence key-range entry points: the batched stages with one sequence, the exchange
+// of the whole shortlist and the key offset as the map.
+extern "C" size_t sva_shard_workspace_size(const sva_decode_args* args) {
+  return sva_shard_batched_workspace_size(args, nullptr, nullptr, 0);
+}
+
+extern "C" int sva_shard_summon(const sva_decode_args* args, int64_t key_offset, uint64_t* top_out, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  const sva_shard_map m{key_offset, 0, 0};
+  return sva_shard_batched_summon(args, nullptr, &m, 0, top_out, workspace, workspace_bytes, stream);
+}
+
+extern "C" int sva_shard_rescore(const sva_decode_args* args, int64_t key_offset, int32_t world, int32_t rank,
+                                 const uint64_t* gathered_top, uint32_t* records_out, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  const sva_shard_map m{key_offset, 0, 0};
+  return sva_shard_batched_rescore(args, nullptr, &m, 0, world, rank, gathered_top, records_out, nullptr, workspace,
+                                   workspace_bytes, stream);
+}
+
+extern "C" int sva_shard_verify(const sva_decode_args* args, int64_t key_offset, int32_t world, int32_t rank,
+                                const uint32_t* gathered_records, double* partial_out, void* stream) {
+  const sva_shard_map m{key_offset, 0, 0};
+  return sva_shard_batched_verify(args, nullptr, &m, 0, world, rank, gathered_records, partial_out, stream);
+}
+
+extern "C" int sva_shard_combine(const sva_decode_args* args, int32_t world, const double* gathered_partials,
+                                 void* stream) {
+  return sva_shard_batched_combine(args, nullptr, world, gathered_partials, stream);
 }

@@ -125,6 +125,32 @@ def catalog_encode(keys: torch.Tensor, k_proj: torch.Tensor, codebooks: torch.Te
     _lib.check(rc)
 
 
+def catalog_encode_at(keys: torch.Tensor, k_proj: torch.Tensor, codebooks: torch.Tensor, start: torch.Tensor,
+                      count: int, limit: int, k_low: torch.Tensor, codes: torch.Tensor,
+                      n_heads: int | None = None) -> None:
+    """catalog_encode of rows [start, start + count) with ``start`` an int64 device scalar read by
+    the kernel (sva_catalog_encode_at): capturable in a CUDA graph whose replays append at a moving
+    position.  Rows at or beyond ``limit`` are skipped."""
+    _cuda(keys, "keys")
+    _cuda(start, "start")
+    if start.dtype != torch.int64:
+        raise TypeError("start must be an int64 tensor")
+    if keys.stride(-1) != 1:
+        raise ValueError("keys rows must be contiguous")
+    n_heads = int(k_proj.shape[0]) if n_heads is None else n_heads
+    n_kv, _, head_dim = keys.shape
+    for name, t in (("k_low", k_low), ("codes", codes)):
+        _cuda(t, name)
+        if not (t.stride(-1) == 1 and t.stride(-2) == t.shape[-1]):
+            raise ValueError(f"{name} rows must be contiguous")
+    rc = _lib.load().sva_catalog_encode_at(
+        keys.data_ptr(), dtype_code(keys.dtype), keys.stride(0), keys.stride(1), n_heads, n_kv, head_dim,
+        int(k_proj.shape[-1]), k_proj.data_ptr(), codebooks.data_ptr(), int(codebooks.shape[1]),
+        int(codebooks.shape[2]), start.data_ptr(), int(count), int(limit), k_low.data_ptr(), k_low.stride(0),
+        codes.data_ptr(), codes.stride(0), _stream(keys.device))
+    _lib.check(rc)
+
+
 def assign_centroids(x: torch.Tensor, centroids: torch.Tensor) -> torch.Tensor:
     _cuda(x, "x")
     x = x.float()
@@ -241,25 +267,14 @@ def decode(q: torch.Tensor, q_proj: torch.Tensor, scale: torch.Tensor, codebooks
     return out
 
 
-def decode_batched(q: torch.Tensor, q_proj: torch.Tensor, scale: torch.Tensor, codebooks: torch.Tensor,
-                   codes: torch.Tensor, k_low: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, shortlist: int,
-                   budget: int, *, seq_lens: torch.Tensor | None = None, page_table: torch.Tensor | None = None,
-                   max_len: int | None = None, softmax_scale: float | None = None, logits_mode: int = 0,
-                   allowed_len: torch.Tensor | None = None, allowed_mask: torch.Tensor | None = None,
-                   out: torch.Tensor | None = None, want_shortlist: bool = False, want_final: bool = False,
-                   stats: torch.Tensor | None = None):
-    """Scan decode of B sequences in one call (sva_decode_batched, see include/sva_b200.h).
-
-    q [B, H, T, D]; q_proj / scale / codebooks are shared by the sequences (one layer).
-    Unpaged (``page_table`` None): codes [B, H, L, S], k_low [B, H, L, R], keys / values
-    [B, Hkv, L, D], with L the longest sequence.  Paged: codes [pages, H, page_keys, S], k_low
-    [pages, H, page_keys, R], keys / values [pages, Hkv, page_keys, D] page pools and page_table
-    [B, max_pages] int32 (page of every page_keys-key block of each sequence).  ``seq_lens`` [B]
-    int64 (device) gives each sequence's keys (None: all L, or all ``max_len``); ``max_len`` (host
-    int) bounds them (default: L, or max_pages * page_keys).  ``allowed_len`` [B, T] int64 and
-    ``allowed_mask`` [B * T, >= L] uint8 as for ``decode``.  Returns out [B, H, T, D] (and
-    shortlist / final index tensors [B, H, T, shortlist] / [B, H, T, budget] when requested).
-    """
+def batched_args(q: torch.Tensor, q_proj: torch.Tensor, scale: torch.Tensor, codebooks: torch.Tensor,
+                 codes: torch.Tensor, k_low: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, shortlist: int,
+                 budget: int, *, seq_lens: torch.Tensor | None = None, page_table: torch.Tensor | None = None,
+                 max_len: int | None = None, softmax_scale: float | None = None, logits_mode: int = 0,
+                 allowed_len: torch.Tensor | None = None, allowed_mask: torch.Tensor | None = None,
+                 out: torch.Tensor | None = None, stats: torch.Tensor | None = None):
+    """Validated (sva_decode_args, sva_batch_layout, out) for the tensors of a batched call (see
+    decode_batched for the layouts)."""
     for name, t in (("q", q), ("codes", codes), ("k_low", k_low), ("keys", keys), ("values", values)):
         _cuda(t, name)
     if q.dim() != 4 or codes.dim() != 4 or k_low.dim() != 4 or keys.dim() != 4 or values.dim() != 4:
@@ -321,6 +336,34 @@ def decode_batched(q: torch.Tensor, q_proj: torch.Tensor, scale: torch.Tensor, c
     lay.q_seq_stride, lay.out_seq_stride = q.stride(0), out.stride(0)
     lay.codes_page_stride, lay.k_low_page_stride = codes.stride(0), k_low.stride(0)
     lay.k_page_stride, lay.v_page_stride = keys.stride(0), values.stride(0)
+    return a, lay, out
+
+
+def decode_batched(q: torch.Tensor, q_proj: torch.Tensor, scale: torch.Tensor, codebooks: torch.Tensor,
+                   codes: torch.Tensor, k_low: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, shortlist: int,
+                   budget: int, *, seq_lens: torch.Tensor | None = None, page_table: torch.Tensor | None = None,
+                   max_len: int | None = None, softmax_scale: float | None = None, logits_mode: int = 0,
+                   allowed_len: torch.Tensor | None = None, allowed_mask: torch.Tensor | None = None,
+                   out: torch.Tensor | None = None, want_shortlist: bool = False, want_final: bool = False,
+                   stats: torch.Tensor | None = None):
+    """Scan decode of B sequences in one call (sva_decode_batched, see include/sva_b200.h).
+
+    q [B, H, T, D]; q_proj / scale / codebooks are shared by the sequences (one layer).
+    Unpaged (``page_table`` None): codes [B, H, L, S], k_low [B, H, L, R], keys / values
+    [B, Hkv, L, D], with L the longest sequence.  Paged: codes [pages, H, page_keys, S], k_low
+    [pages, H, page_keys, R], keys / values [pages, Hkv, page_keys, D] page pools and page_table
+    [B, max_pages] int32 (page of every page_keys-key block of each sequence).  ``seq_lens`` [B]
+    int64 (device) gives each sequence's keys (None: all L, or all ``max_len``); ``max_len`` (host
+    int) bounds them (default: L, or max_pages * page_keys).  ``allowed_len`` [B, T] int64 and
+    ``allowed_mask`` [B * T, >= L] uint8 as for ``decode``.  Returns out [B, H, T, D] (and
+    shortlist / final index tensors [B, H, T, shortlist] / [B, H, T, budget] when requested).
+    """
+    a, lay, out = batched_args(q, q_proj, scale, codebooks, codes, k_low, keys, values, shortlist, budget,
+                               seq_lens=seq_lens, page_table=page_table, max_len=max_len,
+                               softmax_scale=softmax_scale, logits_mode=logits_mode, allowed_len=allowed_len,
+                               allowed_mask=allowed_mask, out=out, stats=stats)
+    dev = q.device
+    n_seqs, n_heads, n_q, _ = q.shape
     sl_out = fin_out = None
     if want_shortlist:
         sl_out = torch.empty(n_seqs, n_heads, n_q, int(shortlist), dtype=torch.int32, device=dev)

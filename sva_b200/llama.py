@@ -19,7 +19,7 @@ from typing import Any
 
 import torch
 from torch import nn
-from transformers.cache_utils import Cache
+from transformers.cache_utils import Cache, StaticCache
 from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
 
 from . import _lib, kernels
@@ -30,6 +30,16 @@ from .stats import SVAStats
 # (head, token)); prefill over long caches is split into token chunks that fit it.
 _GRID_WORKSPACE_BUDGET = 2 << 30
 _FUSED_MAX_KEYS = 32768
+
+
+def _grid_schedule(k_len: int, shortlist: int, budget: int) -> bool:
+    """Whether sva_decode runs the million-key (grid) schedule for this cache: over 32768 keys, or
+    when one CTA's shared memory cannot hold every key's ADC key with the shortlist and budget
+    arrays (the planner's rule, with a slightly larger fixed part so that this never says no where
+    the planner says yes; grid calls are split into token chunks)."""
+    sl = min(shortlist, k_len)
+    b = min(budget, sl)
+    return k_len > _FUSED_MAX_KEYS or 4 * k_len + 8 * (sl + b) + 32 * 1024 > 227 * 1024 or k_len > 4096
 
 
 @dataclass(frozen=True)
@@ -102,6 +112,7 @@ class SVALlamaAttention(nn.Module):
         self._cached_signature: tuple | None = None
         self._tc_write_key: tuple | None = None
         self._tc_write = False
+        self._static_sig = None  # static-cache catalog (sva_attention_static), sized by the cache
         # batched catalog (allow_batch): [B, H, cap, R] fp32 / [B, H, cap, S] uint8
         self._bk_low: torch.Tensor | None = None
         self._bcodes: torch.Tensor | None = None
@@ -164,7 +175,11 @@ class SVALlamaAttention(nn.Module):
         query_states, key_states = apply_rotary_pos_emb(query_states, key_states, cos, sin)
         if past_key_values is not None:
             key_states, value_states = past_key_values.update(key_states, value_states, self.layer_idx)
-        attn_output = self.sva_attention(query_states, key_states, value_states, attention_mask)
+        position_ids = kwargs.get("position_ids")
+        if isinstance(past_key_values, StaticCache) and position_ids is not None:
+            attn_output = self.sva_attention_static(query_states, key_states, value_states, position_ids)
+        else:
+            attn_output = self.sva_attention(query_states, key_states, value_states, attention_mask)
         attn_output = attn_output.transpose(1, 2).contiguous().reshape(*input_shape, -1)
         return attn_output, None
 
@@ -231,8 +246,8 @@ class SVALlamaAttention(nn.Module):
         out = torch.empty(n_heads, q_len, head_dim, dtype=query.dtype, device=dev)
         q = query[0]
         chunk = q_len
-        if k_len > _FUSED_MAX_KEYS:
-            chunk = max(1, min(q_len, _GRID_WORKSPACE_BUDGET // max(1, n_heads * k_len * 8)))
+        if _grid_schedule(k_len, self.serving.coarse_shortlist, self.serving.budget):
+            chunk = max(1, min(q_len, _GRID_WORKSPACE_BUDGET // max(1, n_heads * k_len * 8), 65535 // n_heads))
         if self.serving.query_chunk_size:
             chunk = min(chunk, int(self.serving.query_chunk_size))
         for t0 in range(0, q_len, chunk):
@@ -250,6 +265,71 @@ class SVALlamaAttention(nn.Module):
                            allowed_mask=None if allowed_mask is None else allowed_mask[t0:t1],
                            out=out[:, t0:t1], stats=counters)
         return out.unsqueeze(0)
+
+    # ------------------------------------------------------------------------------------
+    def sva_attention_static(self, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                             position_ids: torch.Tensor) -> torch.Tensor:
+        """The scan summon over a Hugging Face ``StaticCache`` (not in the reference, which runs
+        on growing caches).  key / value are the cache's full [B, Hkv, max_len, D] buffers, of
+        which the rows before position_ids[0, -1] + 1 are filled; the batch is taken to be
+        unpadded, so the attention mask is not consulted.  A single-token step reads its position
+        and the valid length from device memory (sva_catalog_encode_at, sva_decode_batched with
+        device lengths), so the whole model step can be captured in a CUDA graph and replayed;
+        every token gets exactly the result of the growing-cache path."""
+        batch, n_heads, q_len, head_dim = query.shape
+        max_len = int(key.shape[2])
+        if query.device.type != "cuda":
+            raise RuntimeError("The B200 SVA adapter runs on CUDA devices only; move the model to a GPU.")
+        if self.serving.summon_mode != "scan":
+            raise ValueError("The static-cache SVA path supports summon_mode='scan' only.")
+        if batch != 1 and not self.serving.allow_batch:
+            raise ValueError("SVA Llama adapter currently expects batch size 1.")
+        dev = query.device
+        rank = self.serving.rank_dim
+        subspaces = int(self.sva_coarse_codebooks.shape[1])
+        sig = (dev, key.dtype, batch, max_len, key.data_ptr())
+        if getattr(self, "_static_sig", None) != sig:
+            # buffers sized for the whole cache, allocated before any capture (at the prefill)
+            self._sk_low = torch.zeros(batch, n_heads, max_len, rank, dtype=torch.float32, device=dev)
+            self._scodes = torch.zeros(batch, n_heads, max_len, subspaces, dtype=torch.uint8, device=dev)
+            self._srep = (self.sva_k_proj.to(dev).repeat(batch, 1, 1).contiguous(),
+                          self.sva_coarse_codebooks.to(dev).repeat(batch, 1, 1, 1).contiguous())
+            self._static_sig = sig
+        n_kv = int(key.shape[1])
+        flat_keys = key.view(batch * n_kv, max_len, head_dim)
+        flat_low = self._sk_low.view(batch * n_heads, max_len, rank)
+        flat_codes = self._scodes.view(batch * n_heads, max_len, subspaces)
+        counters = None if self.stats is None else self.stats.device_counters(int(self.layer_idx or 0), dev)
+        pos = position_ids.reshape(-1, q_len)[0]
+        if q_len == 1:
+            start = pos.to(torch.int64)
+            kernels.catalog_encode_at(flat_keys, self._srep[0], self._srep[1], start, 1, max_len, flat_low, flat_codes,
+                                      n_heads=batch * n_heads)
+            seq_lens = (start + 1).expand(batch).contiguous()
+            return kernels.decode_batched(query, self.sva_q_proj, self.sva_scale, self.sva_coarse_codebooks,
+                                          self._scodes, self._sk_low, key, value, self.serving.coarse_shortlist,
+                                          self.serving.budget, seq_lens=seq_lens, max_len=max_len,
+                                          softmax_scale=self.scaling, logits_mode=1, stats=counters)
+        # prefill (not captured): positions and lengths on the host
+        first, last = int(pos[0]), int(pos[-1])
+        k_len = last + 1
+        kernels.catalog_encode(flat_keys, self._srep[0], self._srep[1], first, k_len - first, flat_low, flat_codes,
+                               n_heads=batch * n_heads)
+        out = torch.empty(batch, n_heads, q_len, head_dim, dtype=query.dtype, device=dev)
+        chunk = q_len
+        if _grid_schedule(k_len, self.serving.coarse_shortlist, self.serving.budget):
+            chunk = max(1, min(q_len, _GRID_WORKSPACE_BUDGET // max(1, batch * n_heads * k_len * 8),
+                               65535 // (batch * n_heads)))
+        if self.serving.query_chunk_size:
+            chunk = min(chunk, int(self.serving.query_chunk_size))
+        for t0 in range(0, q_len, chunk):
+            t1 = min(q_len, t0 + chunk)
+            allowed_len = (pos[t0:t1].to(torch.int64) + 1).expand(batch, t1 - t0).contiguous()
+            kernels.decode_batched(query[:, :, t0:t1], self.sva_q_proj, self.sva_scale, self.sva_coarse_codebooks,
+                                   self._scodes, self._sk_low, key, value, self.serving.coarse_shortlist,
+                                   self.serving.budget, max_len=k_len, softmax_scale=self.scaling, logits_mode=1,
+                                   allowed_len=allowed_len, out=out[:, :, t0:t1], stats=counters)
+        return out
 
     # ------------------------------------------------------------------------------------
     def _sva_attention_batched(self, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
@@ -279,7 +359,7 @@ class SVALlamaAttention(nn.Module):
         counters = None if self.stats is None else self.stats.device_counters(int(self.layer_idx or 0), dev)
         out = torch.empty(batch, n_heads, q_len, head_dim, dtype=query.dtype, device=dev)
         chunk = q_len
-        if k_len > _FUSED_MAX_KEYS:
+        if _grid_schedule(k_len, self.serving.coarse_shortlist, self.serving.budget):
             chunk = max(1, min(q_len, _GRID_WORKSPACE_BUDGET // max(1, batch * n_heads * k_len * 8),
                                65535 // (batch * n_heads)))
         if self.serving.query_chunk_size:

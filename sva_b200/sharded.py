@@ -23,6 +23,7 @@ with CPU ranks (``gloo``) and a host-side backend in the tests; the product back
 from __future__ import annotations
 
 import ctypes
+import math
 from dataclasses import dataclass
 from typing import Any
 
@@ -141,3 +142,113 @@ class ShardedDecoder:
         records = self.backend.rescore(call, self._gather(top), self.world, self.rank)
         partial = self.backend.verify(call, self._gather(records), self.world, self.rank)
         return self.backend.combine(call, self._gather(partial), self.world)
+
+
+def default_exchange_width(shortlist: int, world: int) -> int:
+    """Entries each rank sends per problem in the first exchange: the expected share of the
+    global shortlist, shortlist / world, plus eight standard deviations of a binomial share plus
+    32, capped at the shortlist.  A rank holding more members than that (keys clustered in one
+    shard) makes the decode repeat the exchange at full width, so the width only affects speed."""
+    if world <= 1:
+        return int(shortlist)
+    share = shortlist / world
+    return int(min(shortlist, math.ceil(share + 8.0 * math.sqrt(share) + 32)))
+
+
+class BatchedShardedDecoder:
+    """Exact scan decode of a batch of sequences whose catalogs are sharded across ranks
+    (sva_shard_batched_*, include/sva_b200.h "Batched shards").
+
+    Each call decodes one token of every sequence (q [B, H, 1, D]) in four stages with three
+    all-gathers; the first two exchange ``exchange_width`` entries per problem instead of the
+    whole shortlist.  ``page_dealt`` selects the page-dealt numbering (global page g of every
+    sequence on rank g % world; needs a paged layout) instead of key ranges starting at
+    ``key_offset``.  The shortlist, final sets and outputs equal a one-GPU decode of the whole
+    caches (outputs up to the order of exact fp64 sums); when a rank holds more shortlist members
+    than the exchange width, the rescore stage flags it and the call repeats the first two
+    exchanges at full width (``check_saturation``; each call then reads one flag on the host).
+    """
+
+    def __init__(self, group, shortlist: int, budget: int, device: torch.device, exchange_width: int | None = None,
+                 check_saturation: bool = True) -> None:
+        self.group = group
+        self.world = dist.get_world_size(group) if group is not None else 1
+        self.rank = dist.get_rank(group) if group is not None else 0
+        self.shortlist, self.budget = int(shortlist), int(budget)
+        self.device = device
+        self.width = int(exchange_width) if exchange_width else default_exchange_width(self.shortlist, self.world)
+        self.check_saturation = bool(check_saturation)
+        self._ws = kernels.Workspace()
+        self._nccl = group is not None and dist.get_backend(group) == "nccl"
+        self.fallbacks = 0
+        self.stage_events = None  # optional list of 7 CUDA events recorded between the stages
+
+    def _gather(self, t: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return t.unsqueeze(0)
+        out = torch.empty((self.world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+        if self._nccl:
+            dist.all_gather_into_tensor(out, t.contiguous(), group=self.group)
+        else:
+            dist.all_gather(list(out.unbind(0)), t.contiguous(), group=self.group)
+        return out
+
+    def _mark(self, i: int) -> None:
+        if self.stage_events is not None:
+            self.stage_events[i].record()
+
+    def decode(self, q, q_proj, scale, codebooks, codes, k_low, keys, values, *, seq_lens=None, page_table=None,
+               max_len=None, key_offset: int = 0, page_dealt: bool = False, out=None, logits_mode: int = 0,
+               softmax_scale: float | None = None, stats=None) -> torch.Tensor:
+        """This rank's local arrays in decode_batched's layouts; returns out [B, H, 1, D]."""
+        if q.dim() != 4 or q.shape[2] != 1:
+            raise ValueError("batched sharded decode takes one query token per sequence and head: q [B, H, 1, D]")
+        a, lay, out = kernels.batched_args(q, q_proj, scale, codebooks, codes, k_low, keys, values, self.shortlist,
+                                           self.budget, seq_lens=seq_lens, page_table=page_table, max_len=max_len,
+                                           softmax_scale=softmax_scale, logits_mode=logits_mode, out=out,
+                                           stats=stats)
+        m = _lib.ShardMap()
+        m.key_offset = int(key_offset)
+        m.page_world = self.world if page_dealt else 0
+        m.page_rank = self.rank if page_dealt else 0
+        lib = _lib.load()
+        P = int(q.shape[0] * q.shape[1])
+        D = int(q.shape[3])
+        stream = kernels._stream(q.device)
+        width = min(self.width, self.shortlist)
+        self._mark(0)
+        for attempt in range(2):
+            ws_bytes = int(lib.sva_shard_batched_workspace_size(ctypes.byref(a), ctypes.byref(lay), ctypes.byref(m),
+                                                                width))
+            if ws_bytes == 0:
+                _lib.check(lib.sva_shard_batched_summon(ctypes.byref(a), ctypes.byref(lay), ctypes.byref(m), width,
+                                                        None, None, 0, None))
+            ws = self._ws.get(q.device, ws_bytes)
+            top = torch.empty(P, width, dtype=torch.int64, device=q.device)
+            _lib.check(lib.sva_shard_batched_summon(ctypes.byref(a), ctypes.byref(lay), ctypes.byref(m), width,
+                                                    top.data_ptr(), ws.data_ptr(), ws_bytes, stream))
+            self._mark(1)
+            g_top = self._gather(top)
+            self._mark(2)
+            rec = torch.empty(P, width, 4, dtype=torch.int32, device=q.device)
+            sat = torch.zeros(1, dtype=torch.int32, device=q.device)
+            _lib.check(lib.sva_shard_batched_rescore(ctypes.byref(a), ctypes.byref(lay), ctypes.byref(m), width,
+                                                     self.world, self.rank, g_top.data_ptr(), rec.data_ptr(),
+                                                     sat.data_ptr(), ws.data_ptr(), ws_bytes, stream))
+            self._mark(3)
+            # every rank reads the same flag (it is computed from the same gathered lists)
+            if width >= self.shortlist or not self.check_saturation or int(sat.item()) == 0:
+                break
+            self.fallbacks += 1
+            width = self.shortlist
+        g_rec = self._gather(rec)
+        self._mark(4)
+        part = torch.empty(P, D, dtype=torch.float64, device=q.device)
+        _lib.check(lib.sva_shard_batched_verify(ctypes.byref(a), ctypes.byref(lay), ctypes.byref(m), width,
+                                                self.world, self.rank, g_rec.data_ptr(), part.data_ptr(), stream))
+        g_part = self._gather(part)
+        self._mark(5)
+        _lib.check(lib.sva_shard_batched_combine(ctypes.byref(a), ctypes.byref(lay), self.world, g_part.data_ptr(),
+                                                 stream))
+        self._mark(6)
+        return out

@@ -31,7 +31,7 @@ def test_library_exports_every_declared_symbol():
 def test_struct_layouts_match_header_field_order():
     text = HEADER.read_text()
     for struct, cls in (("sva_decode_args", _lib.DecodeArgs), ("sva_inverted_args", _lib.InvertedArgs),
-                        ("sva_batch_layout", _lib.BatchLayout)):
+                        ("sva_batch_layout", _lib.BatchLayout), ("sva_shard_map", _lib.ShardMap)):
         body = re.search(r"typedef struct " + struct + r" \{(.*?)\} " + struct + ";", text, flags=re.S).group(1)
         body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
         fields = []

@@ -258,3 +258,33 @@ def test_chained_decodes_query_aliases_previous_output():
         torch.cuda.synchronize()
         assert torch.equal(out1, ref1)
         assert torch.equal(out2, ref2)
+
+
+@pytest.mark.parametrize("name", ["cfg1", "cfg2s_4x64"])
+def test_catalog_appends_match_full_build(name):
+    """Decode-step appends (one CTA per key and head for up to 8 keys, host or device start row)
+    write exactly the rows of the full catalog build."""
+    from sva_b200 import kernels
+
+    case, (k_low_ref, codes_ref) = cached_case(name)
+    keys = case.keys[0].cuda()
+    n = 300
+    k_low = torch.zeros(case.n_heads, n, 64, device="cuda")
+    codes = torch.zeros(case.n_heads, n, case.codebooks.shape[1], dtype=torch.uint8, device="cuda")
+    kp, cb = case.k_proj.cuda(), case.codebooks.cuda()
+    pos = 0
+    for i, count in enumerate([1, 2, 3, 8, 5, 1, 7, 4] * 20):
+        if pos >= n:
+            break
+        count = min(count, n - pos)
+        if i % 2:
+            kernels.catalog_encode(keys, kp, cb, pos, count, k_low, codes)
+        else:
+            start = torch.tensor([pos], dtype=torch.int64, device="cuda")
+            kernels.catalog_encode_at(keys, kp, cb, start, count, n, k_low, codes)
+        pos += count
+    # a device start past the limit writes nothing
+    kernels.catalog_encode_at(keys, kp, cb, torch.tensor([n], dtype=torch.int64, device="cuda"), 4, n, k_low, codes)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(k_low.cpu().numpy(), k_low_ref[:, :n])
+    np.testing.assert_array_equal(codes.cpu().numpy(), codes_ref[:, :n].astype(np.uint8))
