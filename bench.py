@@ -2,22 +2,28 @@
 """SVA decode benchmark on B200: microseconds per query at 2^20 cached keys (summon + verify).
 
 Workload (in the 9-head shape the reference publishes its million-key numbers
-on): 2^20 cached keys per head, 9 independent heads, head_dim 64, rank 64, bf16 K/V ~ N(0,1)
-with 64 planted near-duplicates per head, PQ codes 4x64 (default) or 1x256, shortlist 2048,
-budget 512, one query token.  A "query" is one decode token over all 9 heads.
+on): ``--sequences`` independent caches ("sequences", 16 by default) of 2^20 keys per head, 9
+heads each, head_dim 64, rank 64, bf16 K/V ~ N(0,1) with 64 planted near-duplicates per head,
+4x64 codes (default) or 1x256, shortlist 2048, budget 512.  A query is one decode token of one
+sequence over its 9 heads.
 
-A step is one CUDA-graph replay of ``--queries-per-step`` decode calls.  The graph cycles over
-``--sets`` independent 9-head catalogs so that consecutive queries touch disjoint memory (each
-query touches ~44 MB; four sets ~176 MB > the 126 MB L2), i.e. every query runs against a cold
-L2.  Inputs are resident in HBM before timing; the catalog is built by the CUDA write path.
+Headline (``value``, every N): serving mode.  One decode call takes the next token of every
+sequence (16 queries, 144 (head, query) problems); a step is ``--tokens-per-step`` such calls
+(256 queries), and value = step time / queries.  Each call touches 16 x ~44 MB, far more than
+the 126 MB L2.  On one GPU the step is one CUDA-graph replay of sva_decode_batched calls; on N
+GPUs (``torchrun --nproc-per-node N``) every sequence's keys are split by key range and each call
+runs the batched shard stages with three NCCL all-gathers (sva_b200.sharded.BatchedShardedDecoder);
+value is the max over ranks.  Inputs are resident in HBM; catalogs are built by the CUDA write path.
 
-Multi-GPU (``torchrun --nproc-per-node N``): the catalog is sharded by key range; every rank
-summons, rescores and partially verifies its range, and the exact global result comes from three
-NCCL all-gathers between the stages (sva_b200.sharded).  ``value`` is the max over ranks.
+Beside it (one GPU): ``latency``, the decode of one query at a time (a 256-query graph over the
+first four sequences: the single-sequence latency), ``ragged_paged`` (config 5: 64 ragged
+sequences in a paged catalog; at N > 1 page-dealt over the ranks), ``inverted_static`` (the
+static inverted-index summon), ``write_path`` and ``cpu_baseline``.
 
-``--impl reference`` times the CPU restatement of the reference path (oracle/cpu_baseline.py,
+``--impl reference`` times the CPU restatement of the reference path (oracle/cpu_baseline.py;
 the reference itself is PyTorch code that cannot be shipped to the GPU host) on the same
-configuration with all host threads.
+configuration with all host threads.  ``--workload cfg3 / cfg4`` measure model-level decode
+tokens/s instead (see model_arm).
 """
 
 from __future__ import annotations
@@ -54,13 +60,13 @@ def parse_args():
     ap.add_argument("--pq", default="4x64", choices=["4x64", "1x256", "2x256"])
     ap.add_argument("--shortlist", type=int, default=2048)
     ap.add_argument("--budget", type=int, default=512)
-    ap.add_argument("--sets", type=int, default=4)
-    ap.add_argument("--queries-per-step", type=int, default=256)
+    ap.add_argument("--sequences", type=int, default=16, help="independent million-key caches decoded together")
+    ap.add_argument("--tokens-per-step", type=int, default=16, help="serving calls (tokens of every sequence) per step")
+    ap.add_argument("--sets", type=int, default=4, help="sequences the latency measurement rotates over")
+    ap.add_argument("--queries-per-step", type=int, default=256, help="queries per step of the latency measurement")
     ap.add_argument("--e2e-queries", type=int, default=64)
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--throughput-heads", type=int, default=64,
-                    help="heads per launch of the throughput-mode measurement (0: skip)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-inverted", dest="inverted", action="store_false",
                     help="skip the static inverted-index summon measurement")
@@ -251,78 +257,84 @@ def reference_arm(args):
 
 def workload_config(args, world: int) -> dict:
     return {
-        "workload": f"cfg2 million-key decode: {args.keys} keys x {args.heads} heads, {args.pq} codes, "
-                    f"shortlist {args.shortlist}, budget {args.budget}, q=1",
+        "workload": f"cfg2 million-key decode, serving mode: {args.sequences} sequences x {args.keys} keys x "
+                    f"{args.heads} heads, {args.pq} codes, shortlist {args.shortlist}, budget {args.budget}; one call "
+                    f"decodes one token of every sequence, {args.tokens_per_step} calls per step",
         "keys": args.keys, "heads": args.heads, "pq": args.pq, "shortlist": args.shortlist, "budget": args.budget,
-        "head_dim": 64, "rank_dim": 64, "queries_per_step": args.queries_per_step,
+        "head_dim": 64, "rank_dim": 64, "sequences": args.sequences,
+        "queries_per_step": args.sequences * args.tokens_per_step,
         "parallelism": "single GPU" if world == 1 else f"key-range shards x{world}",
-        "l2": f"{args.sets} rotating catalogs per graph ({args.sets} x ~{algorithmic_bytes(args)['total'] / 1e6:.0f} MB "
-              f"touched per cycle > 126 MB L2)",
+        "l2": f"every call touches {args.sequences} x ~{algorithmic_bytes(args)['total'] / 1e6:.0f} MB > 126 MB L2",
     }
 
 
-# ---------------------------------------------------------------------------------------------
-# GPU arm
-# ---------------------------------------------------------------------------------------------
-
-def build_sets(args, device, rank: int, world: int):
-    """Per set: q [H,1,D], K/V [H,L_local,D] bf16, k_low [H,L_local,R], codes [H,L_local,S] for this
-    rank's key range; artifacts shared across ranks (same seed)."""
+def build_batch(args, device, rank: int, world: int, keep_full_first: bool = False):
+    """The serving batch for this rank: q [N, H, 1, D], artifacts shared by the sequences (one
+    layer), and this rank's key range [lo, hi) of every sequence: codes [N, H, L_r, S], k_low
+    [N, H, L_r, R], keys / values [N, H, L_r, D] (one KV head per query head).  Every rank draws
+    the same full caches (seeded per sequence on the device) and keeps its slice, so the shards
+    are exactly the one-GPU data.  With keep_full_first, sequence 0's full arrays are returned too
+    (the parity check of the sharded runs)."""
     import torch
 
     from sva_b200 import kernels
 
-    s, c = pq_shape(args.pq)
-    heads, keys, d, r = args.heads, args.keys, 64, 64
-    lo = keys * rank // world
-    hi = keys * (rank + 1) // world
-    sets = []
-    build_ms = 0.0
-    for si in range(args.sets):
-        cpu_gen = torch.Generator().manual_seed(args.seed * 1000 + si)
-        q = torch.randn(heads, 1, d, generator=cpu_gen).to(torch.bfloat16)
-        q_proj = (torch.randn(heads, d, r, generator=cpu_gen) * 0.125).to(torch.bfloat16).float()
-        k_proj = (torch.randn(heads, d, r, generator=cpu_gen) * 0.125).to(torch.bfloat16).float()
-        cb = torch.randn(heads, s, c, r // s, generator=cpu_gen).to(torch.bfloat16).float()
-        planted = torch.stack([torch.randperm(keys, generator=cpu_gen)[:64] for _ in range(heads)])
-        noise = torch.randn(heads, 64, d, generator=cpu_gen)
-        gen = torch.Generator(device=device).manual_seed(args.seed * 1000 + si + 7)
-        kk = torch.empty(heads, hi - lo, d, dtype=torch.bfloat16, device=device)
-        vv = torch.empty(heads, hi - lo, d, dtype=torch.bfloat16, device=device)
+    s_sub, c = pq_shape(args.pq)
+    n, heads, keys, d, r = args.sequences, args.heads, args.keys, 64, 64
+    lo, hi = keys * rank // world, keys * (rank + 1) // world
+    gen = torch.Generator().manual_seed(args.seed * 1000 + 17)
+    q = torch.randn(n, heads, 1, d, generator=gen).to(torch.bfloat16)
+    q_proj = (torch.randn(heads, d, r, generator=gen) * 0.125).to(torch.bfloat16).float().to(device)
+    k_proj = (torch.randn(heads, d, r, generator=gen) * 0.125).to(torch.bfloat16).float().to(device)
+    cb = torch.randn(heads, s_sub, c, r // s_sub, generator=gen).to(torch.bfloat16).float().to(device)
+    planted = torch.stack([torch.stack([torch.randperm(keys, generator=gen)[:64] for _ in range(heads)])
+                           for _ in range(n)])
+    noise = torch.randn(n, heads, 64, d, generator=gen)
+    L = hi - lo
+    kk = torch.empty(n, heads, L, d, dtype=torch.bfloat16, device=device)
+    vv = torch.empty(n, heads, L, d, dtype=torch.bfloat16, device=device)
+    k_low = torch.empty(n, heads, L, r, dtype=torch.float32, device=device)
+    codes = torch.empty(n, heads, L, s_sub, dtype=torch.uint8, device=device)
+    full_first = None
+    write = {}
+    for i in range(n):
+        dgen = torch.Generator(device=device).manual_seed(args.seed * 1000 + i + 7)
+        fk = torch.empty(heads, keys, d, dtype=torch.bfloat16, device=device)
+        fv = torch.empty(heads, keys, d, dtype=torch.bfloat16, device=device)
         for h in range(heads):
-            kk[h] = torch.randn(hi - lo, d, generator=gen, device=device).to(torch.bfloat16)
-            vv[h] = torch.randn(hi - lo, d, generator=gen, device=device).to(torch.bfloat16)
-            sel = (planted[h] >= lo) & (planted[h] < hi)
-            pos = (planted[h][sel] - lo).to(device)
-            kk[h, pos] = (0.9 * q[h, 0].float()[None, :] + 0.1 * noise[h][sel]).to(torch.bfloat16).to(device)
-        q = q.to(device)
-        q_proj, k_proj, cb = q_proj.to(device), k_proj.to(device), cb.to(device)
-        k_low = torch.empty(heads, hi - lo, r, dtype=torch.float32, device=device)
-        codes = torch.empty(heads, hi - lo, s, dtype=torch.uint8, device=device)
-        tc = kernels.tensor_core_write_ok(kk, k_proj)
-        status = torch.zeros(1, dtype=torch.int32, device=device)
+            fk[h] = torch.randn(keys, d, generator=dgen, device=device).to(torch.bfloat16)
+            fv[h] = torch.randn(keys, d, generator=dgen, device=device).to(torch.bfloat16)
+            fk[h, planted[i, h].to(device)] = (0.9 * q[i, h, 0].float()[None, :] + 0.1 * noise[i, h]).to(
+                torch.bfloat16).to(device)
+        kk[i], vv[i] = fk[:, lo:hi], fv[:, lo:hi]
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        kernels.catalog_encode(kk, k_proj, cb, 0, hi - lo, k_low, codes, tensor_cores=tc, status=status)
+        kernels.catalog_encode(kk[i], k_proj, cb, 0, L, k_low[i], codes[i])
         e1.record()
-        torch.cuda.synchronize()
-        if int(status.item()) != 0:
-            raise RuntimeError("tensor-core write path timed out")
-        build_ms += e0.elapsed_time(e1)
-        if si == 0:
-            # the exact CUDA-core write path, timed once for comparison (into scratch buffers)
-            k2, c2 = torch.empty_like(k_low), torch.empty_like(codes)
-            e0.record()
-            kernels.catalog_encode(kk, k_proj, cb, 0, hi - lo, k2, c2, tensor_cores=False)
-            e1.record()
+        if i == 0:
             torch.cuda.synchronize()
-            exact_ms = e0.elapsed_time(e1)
-            del k2, c2
-        scale = torch.ones(heads, dtype=torch.float32, device=device)
-        sets.append(dict(q=q, q_proj=q_proj, scale=scale, cb=cb, codes=codes, k_low=k_low, keys=kk, values=vv,
-                         out=torch.empty(heads, 1, d, dtype=torch.bfloat16, device=device), offset=lo))
-    write = {"tensor_cores": bool(tc), "ms_per_set": build_ms / args.sets, "exact_ms_per_set": exact_ms}
-    return sets, write, (hi - lo)
+            write["exact_ms_per_set"] = e0.elapsed_time(e1)
+            # the tensor-core write path of the same keys, into scratch buffers (reported only)
+            tc = kernels.tensor_core_write_ok(kk[0], k_proj)
+            write["tensor_cores"] = bool(tc)
+            if tc:
+                k2, c2 = torch.empty_like(k_low[0]), torch.empty_like(codes[0])
+                status = torch.zeros(1, dtype=torch.int32, device=device)
+                e0.record()
+                kernels.catalog_encode(kk[0], k_proj, cb, 0, L, k2, c2, tensor_cores=True, status=status)
+                e1.record()
+                torch.cuda.synchronize()
+                write["tc_ms_per_set"] = e0.elapsed_time(e1)
+                del k2, c2
+            if keep_full_first and world > 1:
+                fl = torch.empty(heads, keys, r, dtype=torch.float32, device=device)
+                fc = torch.empty(heads, keys, s_sub, dtype=torch.uint8, device=device)
+                kernels.catalog_encode(fk, k_proj, cb, 0, keys, fl, fc)
+                full_first = dict(keys=fk, values=fv, k_low=fl, codes=fc)
+        del fk, fv
+    torch.cuda.synchronize()
+    return dict(q=q.to(device), q_proj=q_proj, scale=torch.ones(heads, dtype=torch.float32, device=device), cb=cb,
+                codes=codes, k_low=k_low, keys=kk, values=vv, offset=lo, write=write, full_first=full_first)
 
 
 def inverted_measure(args, sets, device) -> dict:
@@ -357,60 +369,20 @@ def inverted_measure(args, sets, device) -> dict:
     e.record()
     torch.cuda.synchronize()
     st = stats.cpu().tolist()
-    return {"summon": "inverted_static", "us_per_query": round(1000.0 * s.elapsed_time(e) / n, 2),
-            "cells_per_subspace": cells, "budget": args.budget, "queries": n,
-            "cell_visits_per_query": round(st[5] / n, 1), "verified_per_query": round(st[4] / n, 1),
-            "timing": "eager calls over the rotating catalog sets, device clock"}
-
-
-def throughput_measure(args, device, peak: float) -> dict:
-    """Throughput mode (one GPU): many independent (head, query) problems per launch, here
-    ``--throughput-heads`` heads of 2^20 keys decoded by one call, so that the per-problem latency
-    chains overlap and the scan streams at bandwidth.  One catalog of that many heads (its codes
-    alone exceed L2); a CUDA graph of 8 calls; device-timed over 5 replays after 3 warm-ups."""
-    import copy
-
-    import torch
-
-    from sva_b200 import kernels
-
-    targs = copy.copy(args)
-    targs.heads, targs.sets = args.throughput_heads, 1
-    sets, _, _ = build_sets(targs, device, 0, 1)
-    st = sets[0]
-
-    def call():
-        kernels.decode(st["q"], st["q_proj"], st["scale"], st["cb"], st["codes"], st["k_low"], st["keys"],
-                       st["values"], args.shortlist, args.budget, softmax_scale=0.125, logits_mode=1, out=st["out"])
-
-    call()
-    torch.cuda.synchronize()
-    calls = 8
-    graph = torch.cuda.CUDAGraph()
-    stream = torch.cuda.Stream(device)
-    with torch.cuda.stream(stream):
-        with torch.cuda.graph(graph, stream=stream):
-            for _ in range(calls):
-                call()
-    torch.cuda.synchronize()
-    for _ in range(3):
-        graph.replay()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 5
-    e0.record()
-    for _ in range(reps):
-        graph.replay()
-    e1.record()
-    torch.cuda.synchronize()
-    us = 1000.0 * e0.elapsed_time(e1) / (reps * calls)
-    nbytes = algorithmic_bytes(targs)["total"]
+    us = 1000.0 * s.elapsed_time(e) / n
+    # algorithmic bytes: every visited posting entry (4-byte id) and its k_low row (256 bytes), and
+    # the verify's K and V rows of the budget (bf16)
+    entries = st[1] / n
+    nbytes = entries * (4 + 64 * 4) + st[4] / n * 64 * 2 * 2
+    peak, peak_kind = measured_peaks()
     gbs = nbytes / (us * 1e-6) / 1e9
-    del graph, sets, st
-    torch.cuda.empty_cache()
-    return {"heads_per_launch": targs.heads, "us_per_launch": round(us, 2), "us_per_head": round(us / targs.heads, 3),
-            "algorithmic_bytes_per_launch": int(nbytes), "achieved_gbs": round(gbs, 1), "peak_gbs": peak,
-            "frac": round(gbs / peak, 4), "keys": args.keys, "pq": args.pq}
+    return {"summon": "inverted_static", "us_per_query": round(us, 2),
+            "cells_per_subspace": cells, "budget": args.budget, "queries": n,
+            "cell_visits_per_query": round(st[5] / n, 1), "posting_entries_per_query": round(entries, 1),
+            "verified_per_query": round(st[4] / n, 1),
+            "roofline": {"bound": "hbm", "algorithmic_bytes_per_query": int(nbytes), "achieved": round(gbs, 1),
+                         "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 4), "peak_kind": peak_kind},
+            "timing": "eager calls over the rotating catalog sets, device clock"}
 
 
 def ragged_paged_set(device, n_seqs: int = 64, page_keys: int = 256, seed: int = 3, heads: int = 9, kv_heads: int = 3,
@@ -551,15 +523,182 @@ def ragged_measure(args, device, peak: float) -> dict:
             "timing": "CUDA graph of 8 steps, 5 replays after 3 warm-ups, device clock"}
 
 
+def ragged_sharded_measure(args, device, peak: float, group) -> dict:
+    """Config 5 on N GPUs: the pages of every sequence are dealt round-robin over the ranks (global
+    page g of a sequence on rank g % N); each call runs the batched shard stages over the rank's own
+    pages with three NCCL all-gathers (page-dealt BatchedShardedDecoder).  Every rank draws the
+    same page pool and keeps a page table of its own pages only.  Rank 0 checks the result against
+    the one-GPU batched decode of all pages before timing; eager calls, device-timed, max over
+    ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from sva_b200 import kernels, sharded
+
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    st = ragged_paged_set(device)
+    pk = st["page_keys"]
+    n_seqs, heads = st["q"].shape[0], st["q"].shape[1]
+    table = st["table"].cpu()
+    rows, lens = [], []
+    for b, n in enumerate(st["lengths"]):
+        n_pages = (n + pk - 1) // pk
+        mine = list(range(rank, n_pages, world))
+        rows.append([int(table[b, g]) for g in mine])
+        last = n - (n_pages - 1) * pk
+        lens.append(sum(pk if g < n_pages - 1 else last for g in mine))
+    width = max(1, max(len(x) for x in rows))
+    local = torch.zeros(n_seqs, width, dtype=torch.int32)
+    for b, x in enumerate(rows):
+        if x:
+            local[b, :len(x)] = torch.tensor(x, dtype=torch.int32)
+    local = local.to(device)
+    seq_lens = torch.tensor(lens, dtype=torch.int64, device=device)
+    dec = sharded.BatchedShardedDecoder(group, args.shortlist, args.budget, device)
+    out = torch.empty(n_seqs, heads, 1, 64, dtype=torch.bfloat16, device=device)
+
+    def call(saturated=None):
+        dec.decode(st["q"], st["q_proj"], st["scale"], st["cb"], st["codes"], st["k_low"], st["keys"], st["values"],
+                   seq_lens=seq_lens, page_table=local, max_len=width * pk, page_dealt=True, out=out, logits_mode=1,
+                   softmax_scale=0.125, saturated=saturated)
+
+    call()
+    torch.cuda.synchronize()
+    parity = None
+    if rank == 0:
+        ref = kernels.decode_batched(st["q"], st["q_proj"], st["scale"], st["cb"], st["codes"], st["k_low"], st["keys"],
+                                     st["values"], args.shortlist, args.budget, seq_lens=st["seq_lens"],
+                                     page_table=st["table"], max_len=max(st["lengths"]), softmax_scale=0.125,
+                                     logits_mode=1)
+        torch.cuda.synchronize()
+        parity = "ok" if torch.equal(ref, out) else "MISMATCH"
+    # 8 calls (kernels and all-gathers) in one CUDA graph; saturation flags read once per replay
+    calls = 8
+    flags = torch.zeros(calls, dtype=torch.int32, device=device)
+    ev = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(7)]
+    for e in ev:
+        e.record()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    gstream = torch.cuda.Stream(device)
+    with torch.cuda.stream(gstream):
+        call()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=gstream):
+            flags.zero_()
+            for i in range(calls):
+                dec.stage_events = ev if i == 0 else None
+                call(flags[i:i + 1])
+            dec.stage_events = None
+    torch.cuda.synchronize()
+    repeats = 0
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    dist.barrier(group)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+        bad = int(flags.sum().item())
+        if bad:
+            repeats += bad
+            with dec.full_width():
+                for _ in range(bad):
+                    call()
+    e1.record()
+    torch.cuda.synchronize()
+    us = 1000.0 * e0.elapsed_time(e1) / (reps * calls)
+    t = torch.tensor([us], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    us = float(t.item())
+    del graph
+    names = ["summon", "gather_top", "rescore", "gather_records", "verify_gather_partials", "combine"]
+    stages = {n: round(1000.0 * ev[j].elapsed_time(ev[j + 1]), 2) for j, n in enumerate(names)}
+    total_keys = sum(st["lengths"])
+    sl_eff = sum(min(args.shortlist, n) for n in st["lengths"])
+    b_eff = sum(min(args.budget, args.shortlist, n) for n in st["lengths"])
+    nbytes = heads * (total_keys * 4 + sl_eff * 64 * 4 + b_eff * 64 * 2 * 2) + heads * (64 * 64 * 4 + 64 * 64 * 4)
+    gbs = nbytes / (us * 1e-6) / 1e9
+    return {"workload": f"cfg5 ragged paged decode, page-dealt over {world} GPUs: {n_seqs} sequences (total "
+                        f"{total_keys} keys), 9 query / 3 KV heads, 4x64 codes, {pk}-key pages",
+            "us_per_step": round(us, 2), "tokens_per_s": round(n_seqs / (us * 1e-6), 1),
+            "algorithmic_bytes_per_step": int(nbytes), "achieved_gbs_aggregate": round(gbs, 1),
+            "frac_of_n_gpu_peak": round(gbs / (peak * world), 4), "stage_us_rank0_view": stages,
+            "exchange_width": dec.width, "saturation_repeats": repeats, "parity": parity,
+            "timing": "CUDA graph of 8 calls (kernels + NCCL all-gathers), 3 replays after 3 warm-ups, device clock, "
+                      "max over ranks; stage times from events captured in the first call"}
+
+
+def inverted_sharded_measure(args, batch, device, group) -> dict:
+    """The static inverted-index summon with every sequence's static catalog split by key range
+    (ShardedInvertedDecoder: the ranks' top-budget candidate records, then the fp64 partial
+    outputs, two NCCL all-gathers), over the first --sets sequences; posting lists over each
+    rank's keys built once, the global largest list from one all-reduce; eager calls,
+    device-timed, max over ranks.  Rank 0 checks sequence 0 against the one-GPU static decode."""
+    import torch
+    import torch.distributed as dist
+
+    from sva_b200 import kernels, sharded
+
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    C = int(batch["cb"].shape[2])
+    seqs = [seq_view(batch, i) for i in range(args.sets)]
+    posts = [kernels.postings_build(st["codes"], C) for st in seqs]
+    gmax = [sharded.global_max_bucket(pp, group) for pp in posts]
+    dec = sharded.ShardedInvertedDecoder(group, args.budget, cells=8)
+    outs = [torch.empty(st["q"].shape[0], st["q"].shape[2], dtype=st["q"].dtype, device=device) for st in seqs]
+    holds = rank == world - 1
+
+    def one(i):
+        st = seqs[i % len(seqs)]
+        dec.decode(st["q"][:, 0, :], st["q_proj"], st["scale"], st["cb"], st["codes"], posts[i % len(seqs)],
+                   st["k_low"], st["keys"], st["values"], key_offset=batch["offset"], holds_current=holds,
+                   global_max_bucket=gmax[i % len(seqs)], out=outs[i % len(seqs)], softmax_scale=0.125)
+
+    one(0)
+    torch.cuda.synchronize()
+    parity = None
+    if rank == 0 and batch.get("full_first") is not None:
+        f = batch["full_first"]
+        fp = kernels.postings_build(f["codes"], C)
+        ref = kernels.decode_inverted(batch["q"][0][:, 0, :], batch["q_proj"], batch["scale"], batch["cb"], f["codes"],
+                                      fp, f["k_low"], f["keys"], f["values"], args.budget, 8, args.budget, args.budget,
+                                      dynamic=False, softmax_scale=0.125)
+        torch.cuda.synchronize()
+        parity = "ok" if torch.equal(ref, outs[0]) else "MISMATCH"
+    for i in range(3):
+        one(i)
+    torch.cuda.synchronize()
+    dist.barrier(group)
+    n = 16
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(n):
+        one(i)
+    e1.record()
+    torch.cuda.synchronize()
+    us = 1000.0 * e0.elapsed_time(e1) / n
+    t = torch.tensor([us], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    return {"summon": "inverted_static, key-range shards", "us_per_query": round(float(t.item()), 2),
+            "cells_per_subspace": 8, "budget": args.budget, "queries": n, "parity": parity,
+            "timing": "eager calls over the first sequences, device clock, max over ranks"}
+
+
 def write_path_summary(args, write: dict, local_keys: int, peak: float) -> dict:
-    """The catalog write of one set (all heads): keys/s, projection TFLOP/s and the fraction of
+    """The catalog write of one sequence (all heads): keys/s, projection TFLOP/s and the fraction of
     the measured HBM peak its algorithmic bytes reach (K read as bf16, k_low fp32 written, codes)."""
     s, _ = pq_shape(args.pq)
     keys = args.heads * local_keys
     flops = 2.0 * keys * 64 * 64
     nbytes = keys * (64 * 2 + 64 * 4 + s)
-    out = {"path": "tcgen05 projection + CUDA-core assignment" if write["tensor_cores"] else "exact CUDA-core"}
-    for name, ms in (("", write["ms_per_set"]), ("exact_", write["exact_ms_per_set"])):
+    out = {"path": "exact CUDA-core projection and assignment (the adapter's default)"}
+    for name, key in (("exact_", "exact_ms_per_set"), ("tc_", "tc_ms_per_set")):
+        ms = write.get(key)
+        if ms is None:
+            continue
         out[name + "ms_per_set"] = round(ms, 3)
         out[name + "keys_per_s"] = round(keys / (ms * 1e-3), 1)
         out[name + "projection_tflops"] = round(flops / (ms * 1e-3) / 1e12, 3)
@@ -568,10 +707,149 @@ def write_path_summary(args, write: dict, local_keys: int, peak: float) -> dict:
     return out
 
 
+def seq_view(batch, i: int) -> dict:
+    """Sequence i of the serving batch as single-sequence decode arguments."""
+    return dict(q=batch["q"][i], q_proj=batch["q_proj"], scale=batch["scale"], cb=batch["cb"], codes=batch["codes"][i],
+                k_low=batch["k_low"][i], keys=batch["keys"][i], values=batch["values"][i])
+
+
+def profiled_graph(calls, n_calls: int, device, n_prof: int):
+    """A CUDA graph of n_calls calls whose first call records the library's per-kernel events."""
+    import torch
+
+    from sva_b200 import _lib
+
+    prof = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(n_prof + 1)]
+    for e in prof:
+        e.record()
+    torch.cuda.synchronize()
+    handles = ctypes_voidp_array([e.cuda_event for e in prof[1:]])
+    graph = torch.cuda.CUDAGraph()
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        calls(0)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(n_calls):
+                if i == 0:
+                    prof[0].record()
+                    _lib.load().sva_profile_events(handles, n_prof)
+                try:
+                    calls(i)
+                finally:
+                    if i == 0:
+                        _lib.load().sva_profile_events(None, 0)
+    torch.cuda.synchronize()
+    return graph, prof
+
+
+def latency_measure(args, batch, device, peak: float) -> dict:
+    """One query at a time (the single-sequence decode latency): a CUDA graph of
+    --queries-per-step single-sequence decodes cycling over the first --sets sequences (each query
+    touches ~44 MB and the cycle ~176 MB > L2), device-timed after warm-up, with the per-kernel
+    split of the first query and the end-to-end decode with pinned host q and out."""
+    import torch
+
+    from sva_b200 import kernels
+
+    sets = [seq_view(batch, i) for i in range(min(args.sets, args.sequences))]
+    outs = [torch.empty_like(st["q"]) for st in sets]
+
+    def one(i, q=None, out=None):
+        st = sets[i % len(sets)]
+        kernels.decode(st["q"] if q is None else q, st["q_proj"], st["scale"], st["cb"], st["codes"], st["k_low"],
+                       st["keys"], st["values"], args.shortlist, args.budget, softmax_scale=0.125, logits_mode=1,
+                       out=outs[i % len(sets)] if out is None else out)
+
+    qps = args.queries_per_step
+    graph, prof = profiled_graph(one, qps, device, 3)
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = max(2, args.steps // 2)
+    kern = []
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = 1000.0 * e0.elapsed_time(e1) / (reps * qps)
+    graph.replay()
+    torch.cuda.synchronize()
+    kern = {n: round(1000.0 * prof[j].elapsed_time(prof[j + 1]), 2) for j, n in enumerate(["prep", "scan", "finish"])}
+    del graph
+    ab = algorithmic_bytes(args)
+    kb = {"prep": ab["codebooks"] + ab["q_proj"], "scan": ab["codes"], "finish": ab["rescore"] + ab["verify"]}
+    dom = max(kern, key=kern.get)
+    # end to end: pinned host q and out handed to the public op, read / written by its kernels
+    hq = [st["q"].cpu().pin_memory() for st in sets]
+    ho = [torch.empty_like(st["q"], device="cpu").pin_memory() for st in sets]
+    for i in range(4):
+        one(i, hq[i % len(sets)], ho[i % len(sets)])
+    torch.cuda.synchronize()
+    n = args.e2e_queries
+    e0.record()
+    for i in range(n):
+        one(i, hq[i % len(sets)], ho[i % len(sets)])
+    e1.record()
+    torch.cuda.synchronize()
+    e2e = 1000.0 * e0.elapsed_time(e1) / n
+    gbs = ab["total"] / (us * 1e-6) / 1e9
+    return {"us_per_query": round(us, 3), "e2e_us_per_query": round(e2e, 3),
+            "kernel_us_first_query": kern, "kernel_share": {k: round(v / sum(kern.values()), 3) for k, v in kern.items()},
+            "dominant": dom, "dominant_achieved_gbs": round(kb[dom] / (kern[dom] * 1e-6) / 1e9, 1),
+            "algorithmic_bytes_per_query": int(ab["total"]), "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
+            "vs_published_h100": round(us / PUBLISHED_US[args.pq], 5) if args.pq in PUBLISHED_US else None,
+            "timing": f"CUDA graph of {qps} single-query decodes over {len(sets)} sequences, device clock; e2e: "
+                      f"{n} eager calls with pinned host q / out"}
+
+
+def cpu_parity_and_baseline(args, batch, device) -> tuple[dict, str]:
+    """The cpu_baseline leg: the oracle's threaded CPU decoder on sequence 0's own catalog (copied to
+    the host), timed on all host threads over a bounded sample, and its final sets and outputs
+    compared with the GPU's decode of the same sequence (the bench's parity check)."""
+    import torch
+
+    from oracle.cpu_baseline import CpuDecoder
+    from sva_b200 import kernels
+
+    st = seq_view(batch, 0)
+    out, _, fin = kernels.decode(st["q"], st["q_proj"], st["scale"], st["cb"], st["codes"], st["k_low"], st["keys"],
+                                 st["values"], args.shortlist, args.budget, softmax_scale=0.125, logits_mode=1,
+                                 want_final=True)
+    torch.cuda.synchronize()
+    bits = lambda t: t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)  # noqa: E731
+    q = st["q"].float().cpu().numpy()[:, 0]
+    dec = CpuDecoder(st["q_proj"].cpu().numpy(), st["scale"].cpu().numpy(), st["cb"].cpu().numpy(),
+                     st["codes"].cpu().numpy(), st["k_low"].cpu().numpy(), bits(st["keys"]), bits(st["values"]),
+                     groups=1, threads=os.cpu_count() or 1)
+    ref_out, ref_fin = dec(q, args.shortlist, args.budget, 0.125, "bf16", 1, want_final=True)
+    got_fin = fin.cpu().numpy()
+    ok_sets = all(np.array_equal(got_fin[h, 0][got_fin[h, 0] >= 0], ref_fin[h]) for h in range(args.heads))
+    err = float(np.abs(out.float().cpu().numpy()[:, 0] - ref_out).max())
+    parity = ("ok" if ok_sets and err <= 2e-2 else "MISMATCH") + (
+        f": final sets {'bit-exact' if ok_sets else 'differ'} vs the CPU oracle decoder on sequence 0, "
+        f"max |out - oracle| = {err:.2e} (bf16 tolerance 2e-2)")
+    times = []
+    t_end = time.perf_counter() + args.cpu_seconds
+    while True:
+        t0 = time.perf_counter()
+        dec(q, args.shortlist, args.budget, 0.125, "bf16", 1)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() > t_end and len(times) >= 2:
+            break
+    dec.close()
+    cpu_us = 1e6 * sum(times) / len(times)
+    return ({"value": round(cpu_us, 1), "unit": UNIT, "cores": dec.threads, "kind": "port",
+             "sample": f"{len(times)} query tokens x {args.heads} heads x {args.keys} keys ({args.pq}) of sequence 0's "
+                       f"catalog"}, parity)
+
+
 def gpu_arm(args):
     import torch
 
-    from sva_b200 import _lib, kernels
+    from sva_b200 import kernels
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -588,62 +866,92 @@ def gpu_arm(args):
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
         group = dist.group.WORLD
-    lib = _lib.load()
-    sets, write, local_keys = build_sets(args, device, rank, world)
+    batch = build_batch(args, device, rank, world, keep_full_first=(rank == 0))
+    local_keys = int(batch["codes"].shape[2])
+    out = torch.empty_like(batch["q"])
+    peak, peak_kind = measured_peaks()
 
     if world == 1:
-        def one_query(st):
-            kernels.decode(st["q"], st["q_proj"], st["scale"], st["cb"], st["codes"], st["k_low"], st["keys"],
-                           st["values"], args.shortlist, args.budget, softmax_scale=0.125, logits_mode=1, out=st["out"])
+        def serve(i=0, q=None, o=None):
+            return kernels.decode_batched(batch["q"] if q is None else q, batch["q_proj"], batch["scale"], batch["cb"],
+                                          batch["codes"], batch["k_low"], batch["keys"], batch["values"],
+                                          args.shortlist, args.budget, softmax_scale=0.125, logits_mode=1,
+                                          out=out if o is None else o)
+        shard = None
     else:
         from sva_b200 import sharded
 
-        shard = sharded.ShardedDecoder(group, heads=args.heads, head_dim=64, shortlist=args.shortlist,
-                                       budget=args.budget, device=device)
+        shard = sharded.BatchedShardedDecoder(group, args.shortlist, args.budget, device)
 
-        def one_query(st):
-            shard.decode(st["q"], st["q_proj"], st["scale"], st["cb"], st["codes"], st["k_low"], st["keys"],
-                         st["values"], key_offset=st["offset"], out=st["out"], logits_mode=1)
+        def serve(i=0, q=None, o=None):
+            return shard.decode(batch["q"] if q is None else q, batch["q_proj"], batch["scale"], batch["cb"],
+                                batch["codes"], batch["k_low"], batch["keys"], batch["values"],
+                                key_offset=batch["offset"], out=out if o is None else o, logits_mode=1,
+                                softmax_scale=0.125)
 
-    # warm the workspace / communicators outside capture
-    for st in sets:
-        one_query(st)
+    # parity before timing: sequence 0 of a serving call against the one-GPU single-sequence decode
+    serve()
     torch.cuda.synchronize()
+    parity_serve = None
+    if rank == 0:
+        if world == 1:
+            st = seq_view(batch, 0)
+            ref = kernels.decode(st["q"], st["q_proj"], st["scale"], st["cb"], st["codes"], st["k_low"], st["keys"],
+                                 st["values"], args.shortlist, args.budget, softmax_scale=0.125, logits_mode=1)
+        else:
+            f = batch["full_first"]
+            ref = kernels.decode(batch["q"][0], batch["q_proj"], batch["scale"], batch["cb"], f["codes"], f["k_low"],
+                                 f["keys"], f["values"], args.shortlist, args.budget, softmax_scale=0.125,
+                                 logits_mode=1)
+        torch.cuda.synchronize()
+        parity_serve = bool(torch.equal(ref, out[0]))
 
-    grid_schedule = local_keys > 32768 or world > 1  # shards always run prep + scan + top
-    n_prof = 3 if grid_schedule else 1
-    prof = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(n_prof + 1)]
-    for e in prof:  # torch creates the CUDA event on its first record
-        e.record()
-    torch.cuda.synchronize()
-    handles = ctypes_voidp_array([e.cuda_event for e in prof[1:]])
-    if not all(e.cuda_event for e in prof):
-        raise RuntimeError("profiling events were not created")
-    graph = torch.cuda.CUDAGraph()
-    qps = args.queries_per_step
-    stream = torch.cuda.Stream(device)
-    with torch.cuda.stream(stream):
-        with torch.cuda.graph(graph, stream=stream):
-            for i in range(qps):
-                st = sets[i % len(sets)]
-                if i == 0:
-                    prof[0].record()
-                    lib.sva_profile_events(handles, n_prof)
-                try:
-                    one_query(st)
-                finally:
-                    if i == 0:
-                        lib.sva_profile_events(None, 0)
-    torch.cuda.synchronize()
+    calls = args.tokens_per_step
+    n_q = args.sequences * calls
+    kern = None
+    repeats = [0]
+    if world == 1:
+        graph, prof = profiled_graph(lambda i: serve(), calls, device, 3)
+        run_step = graph.replay
+    else:
+        # the step's sharded calls (kernels and NCCL all-gathers) in one CUDA graph; each call ORs
+        # its saturation flag into its own slot, read once per step; a flagged call is repeated
+        # at full width inside the step (exactness), and counted
+        flags = torch.zeros(calls, dtype=torch.int32, device=device)
+        stage_ev = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(7)]
+        for e in stage_ev:
+            e.record()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        gstream = torch.cuda.Stream(device)
+        with torch.cuda.stream(gstream):
+            serve()  # warm the workspaces on the capture stream
+            torch.cuda.synchronize()
+            with torch.cuda.graph(graph, stream=gstream):
+                flags.zero_()
+                for i in range(calls):
+                    shard.stage_events = stage_ev if i == 0 else None
+                    shard.decode(batch["q"], batch["q_proj"], batch["scale"], batch["cb"], batch["codes"],
+                                 batch["k_low"], batch["keys"], batch["values"], key_offset=batch["offset"], out=out,
+                                 logits_mode=1, softmax_scale=0.125, saturated=flags[i:i + 1])
+                shard.stage_events = None
+        torch.cuda.synchronize()
 
+        def run_step():
+            graph.replay()
+            bad = int(flags.sum().item())
+            if bad:
+                repeats[0] += bad
+                with shard.full_width():
+                    for _ in range(bad):
+                        serve()
     for _ in range(args.warmup):
-        graph.replay()
+        run_step()
     torch.cuda.synchronize()
     if group is not None:
         torch.distributed.barrier(group)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    kern = []
     gpu_id = None
     try:
         gpu_id = str(torch.cuda.get_device_properties(device).uuid)
@@ -658,67 +966,55 @@ def gpu_arm(args):
     cur = torch.cuda.current_stream(device)
     for i in range(args.steps):
         starts[i].record(cur)
-        graph.replay()
+        run_step()
         ends[i].record(cur)
-        ends[i].synchronize()
-        kern.append([prof[j].elapsed_time(prof[j + 1]) for j in range(n_prof)])
     torch.cuda.synchronize()
     wall = time.perf_counter() - t_wall
     clocks = sampler.stop()
-    step_ms = [starts[i].elapsed_time(ends[i]) for i in range(args.steps)]
-    ms_step = sum(step_ms) / len(step_ms)
+    ms_step = sum(starts[i].elapsed_time(ends[i]) for i in range(args.steps)) / args.steps
     if group is not None:
         t = torch.tensor([ms_step], device=device)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX, group=group)
         ms_step = float(t.item())
-    us_query = 1000.0 * ms_step / qps
+    us_query = 1000.0 * ms_step / n_q
 
-    # per-kernel timing (first query of every replay)
     ab = algorithmic_bytes(args)
     local_frac = local_keys / args.keys
-    if grid_schedule:
-        # third launch: finish on one GPU (rescore + verify); on shards the local top select
-        # (its rescore / verify stages follow the all-gathers and are not separately timed)
-        names = ["prep", "scan", "finish" if world == 1 else "top"]
-        kernel_bytes = {
-            # prep reads the projections and codebooks (and a 16384-key sample of the codes)
-            "prep": ab["codebooks"] + ab["q_proj"],
-            # scan is the single pass over the codes
-            "scan": ab["codes"] * local_frac,
-            # finish gathers the shortlist's k_low rows and the budget's K and V rows
-            "finish": ab["rescore"] + ab["verify"],
-            # top reads the scan's candidates (about 2x the shortlist, 8 bytes each)
-            "top": 2 * args.shortlist * 8 * args.heads,
-        }
-    else:
-        names = ["fused"]
-        kernel_bytes = {"fused": ab["total"] * local_frac}
-    kmeans = [sum(k[j] for k in kern) / len(kern) for j in range(n_prof)]
-    dom = max(range(n_prof), key=lambda j: kmeans[j])
-    if world > 1:
-        dom = names.index("scan")  # the kernel whose work the shards divide
-    peak, peak_kind = measured_peaks()
-    achieved = kernel_bytes[names[dom]] / (kmeans[dom] * 1e-3) / 1e9
-    workload_key = f"{args.pq}_{args.heads}h_{args.keys}"
-    traffic = profile_traffic(workload_key, names[dom])
-    roofline = {
-        "bound": "hbm", "kernel": names[dom], "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-        "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-        "algorithmic_bytes_per_launch": int(kernel_bytes[names[dom]]), "traffic": traffic,
-        "kernel_us": {n: round(1000 * m, 2) for n, m in zip(names, kmeans)},
-        "kernel_share": {n: round(m / sum(kmeans), 3) for n, m in zip(names, kmeans)},
-    }
-    step_gbs = ab["total"] * local_frac / (us_query * 1e-6) / 1e9
-    step_roofline = {"algorithmic_bytes_per_query": int(ab["total"] * local_frac), "achieved": round(step_gbs, 1),
-                     "frac": round(step_gbs / peak, 4), "peak_kind": peak_kind}
-
-    # end to end through the public op with pinned host buffers
-    host_query = None
+    per_call = {k: v * args.sequences for k, v in ab.items()}
     if world == 1:
-        def host_query(st, hq, ho):
-            kernels.decode(hq, st["q_proj"], st["scale"], st["cb"], st["codes"], st["k_low"], st["keys"],
-                           st["values"], args.shortlist, args.budget, softmax_scale=0.125, logits_mode=1, out=ho)
-    e2e = e2e_measure(args, sets, one_query, device, group, host_query)
+        graph.replay()
+        torch.cuda.synchronize()
+        kus = {n: 1000.0 * prof[j].elapsed_time(prof[j + 1]) for j, n in enumerate(["prep", "scan", "finish"])}
+        kernel_bytes = {"prep": per_call["codebooks"] + per_call["q_proj"], "scan": per_call["codes"],
+                        "finish": per_call["rescore"] + per_call["verify"]}
+        dom = max(kus, key=kus.get)
+        achieved = kernel_bytes[dom] / (kus[dom] * 1e-6) / 1e9
+        roofline = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                    "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                    "algorithmic_bytes_per_launch": int(kernel_bytes[dom]),
+                    "traffic": profile_traffic(f"serve_{args.pq}_{args.sequences}x{args.heads}h_{args.keys}", dom),
+                    "kernel_us": {n: round(v, 2) for n, v in kus.items()},
+                    "kernel_share": {n: round(v / sum(kus.values()), 3) for n, v in kus.items()}}
+        del graph
+    else:
+        # per-stage device times of the first call of a replay (summon = prep + scan + local top;
+        # gathers = NCCL all-gathers), from events captured in the graph
+        graph.replay()
+        torch.cuda.synchronize()
+        ev = stage_ev
+        names = ["summon", "gather_top", "rescore", "gather_records", "verify_gather_partials", "combine"]
+        stages = {n: round(1000.0 * ev[j].elapsed_time(ev[j + 1]), 2) for j, n in enumerate(names)}
+        scan_bytes = per_call["codes"] * local_frac
+        achieved = scan_bytes / (stages["summon"] * 1e-6) / 1e9
+        roofline = {"bound": "hbm", "kernel": "summon (prep + scan + local top, this rank's key range)",
+                    "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                    "peak_kind": peak_kind, "algorithmic_bytes_per_launch": int(scan_bytes), "traffic": None,
+                    "stage_us": stages, "exchange_width": shard.width, "saturation_repeats": repeats[0]}
+    step_bytes = ab["total"] * local_frac
+    step_gbs = step_bytes / (us_query * 1e-6) / 1e9
+    step_roofline = {"algorithmic_bytes_per_query": int(step_bytes), "achieved": round(step_gbs, 1),
+                     "frac": round(step_gbs / peak, 4), "peak_kind": peak_kind}
+    e2e = e2e_measure(args, batch, serve, device, group)
 
     line = {
         "metric": METRIC, "value": round(us_query, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -726,30 +1022,31 @@ def gpu_arm(args):
         "vs_baseline": round(us_query / PUBLISHED_US[args.pq], 5) if args.pq in PUBLISHED_US else None,
         "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16 K/V, 64 planted keys/head, catalog built on GPU)",
         "config": workload_config(args, world),
-        "gpu_launches": None, "roofline": roofline, "step_roofline": step_roofline, "clocks": clocks, "e2e": e2e,
-        "write_path": write_path_summary(args, write, local_keys, peak),
+        "gpu_launches": calls * args.steps * (3 if world == 1 else 6),
+        "roofline": roofline, "step_roofline": step_roofline, "clocks": clocks, "e2e": e2e,
+        "parity": ("ok" if parity_serve else "MISMATCH") + ": sequence 0 of the serving call vs the one-GPU "
+                  "single-sequence decode (bit-identical output)" if rank == 0 else None,
+        "write_path": write_path_summary(args, batch["write"], local_keys, peak),
         "wall_s_timed": round(wall, 3),
     }
-    launches_per_query = 3 if grid_schedule else 1
-    if world > 1:
-        launches_per_query = 3 + shard.extra_launches
-    line["gpu_launches"] = launches_per_query * qps * args.steps
-    if world == 1 and args.throughput_heads > 0:
-        line["throughput"] = throughput_measure(args, device, peak)
-    if world == 1 and args.inverted:
-        line["inverted_static"] = inverted_measure(args, sets, device)
-    if world == 1 and args.ragged:
-        line["ragged_paged"] = ragged_measure(args, device, peak)
+    if world == 1:
+        line["latency"] = latency_measure(args, batch, device, peak)
+        if args.inverted:
+            line["inverted_static"] = inverted_measure(args, [seq_view(batch, i) for i in range(args.sets)], device)
+    elif args.inverted:
+        line["inverted_static"] = inverted_sharded_measure(args, batch, device, group)
+    batch["full_first"] = None
+    torch.cuda.empty_cache()
+    if args.ragged:
+        line["ragged_paged"] = ragged_measure(args, device, peak) if world == 1 else \
+            ragged_sharded_measure(args, device, peak, group)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        times, threads = run_cpu_decoder(args, 1000, 1, args.cpu_seconds)
-        cpu_us = 1e6 * sum(times) / len(times)
-        line["cpu_baseline"] = {"value": round(cpu_us, 1), "unit": UNIT, "cores": threads, "kind": "port",
-                                "sample": f"{len(times)} query tokens x {args.heads} heads x {args.keys} keys "
-                                          f"({args.pq}), random catalog"}
+        line["cpu_baseline"], line["oracle_parity"] = cpu_parity_and_baseline(args, batch, device)
     if rank == 0:
         emit(line)
     if group is not None:
-        del graph
+        del graph  # a graph holding NCCL calls is released before the process group
+        torch.cuda.synchronize()
         torch.distributed.barrier(group)
         torch.distributed.destroy_process_group()
     return 0
@@ -951,38 +1248,37 @@ def ctypes_voidp_array(vals):
     return arr
 
 
-def e2e_measure(args, sets, one_query, device, group, host_query=None):
-    """Each step moves the query token of every head from pinned host memory to the GPU, runs the
-    public decode op, and moves the output back to pinned host memory; time per query on the
-    device clock.  With host_query (one GPU), the public op is given the pinned host tensors
-    themselves and its kernels read q from and write out to host memory; otherwise the step
-    copies them with torch around the op."""
+def e2e_measure(args, batch, serve, device, group):
+    """Serving calls through the public op with every call's queries in pinned host memory and its
+    outputs returned there, device-timed per query.  One GPU: decode_batched is given the pinned
+    host tensors themselves and its kernels read q and write out over PCIe; shards: the queries and
+    outputs are copied with torch around BatchedShardedDecoder.decode."""
     import torch
 
-    n = args.e2e_queries
-    st_list = [sets[i % len(sets)] for i in range(n)]
-    host_q = [st["q"].cpu().pin_memory() for st in sets]
-    host_out = [torch.empty_like(st["out"], device="cpu").pin_memory() for st in sets]
-    for i in range(4):
-        st = st_list[i % len(st_list)]
-        if host_query is not None:
-            host_query(st, host_q[i % len(sets)], host_out[i % len(sets)])
+    host_q = batch["q"].cpu().pin_memory()
+    host_o = torch.empty_like(batch["q"], device="cpu").pin_memory()
+    dev_q = torch.empty_like(batch["q"])
+    dev_o = torch.empty_like(batch["q"])
+    world = 1 if group is None else torch.distributed.get_world_size(group)
+
+    def one():
+        if world == 1:
+            serve(q=host_q, o=host_o)
         else:
-            one_query(st)
+            dev_q.copy_(host_q, non_blocking=True)
+            serve(q=dev_q, o=dev_o)
+            host_o.copy_(dev_o, non_blocking=True)
+
+    for _ in range(3):
+        one()
     torch.cuda.synchronize()
     if group is not None:
         torch.distributed.barrier(group)
+    n = max(1, args.e2e_queries // args.sequences)
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
-    for i in range(n):
-        st = st_list[i]
-        k = i % len(sets)
-        if host_query is not None:
-            host_query(st, host_q[k], host_out[k])
-        else:
-            st["q"].copy_(host_q[k], non_blocking=True)
-            one_query(st)
-            host_out[k].copy_(st["out"], non_blocking=True)
+    for _ in range(n):
+        one()
     e.record()
     torch.cuda.synchronize()
     ms = s.elapsed_time(e)
@@ -990,14 +1286,13 @@ def e2e_measure(args, sets, one_query, device, group, host_query=None):
         t = torch.tensor([ms], device=device)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX, group=group)
         ms = float(t.item())
-    qbytes = sets[0]["q"].numel() * sets[0]["q"].element_size()
-    obytes = sets[0]["out"].numel() * sets[0]["out"].element_size()
-    return {"value": round(1000.0 * ms / n, 3), "unit": UNIT, "h2d_bytes_per_step": qbytes,
-            "d2h_bytes_per_step": obytes, "queries": n,
-            "path": ("sva_b200.kernels.decode (eager calls per query) given pinned host q and out; its kernels "
-                     "read q from and write out to host memory" if host_query is not None else
-                     "sva_b200.sharded.ShardedDecoder.decode (eager calls per query) with torch copies of pinned "
-                     "host q and out around it")}
+    nbytes = batch["q"].numel() * batch["q"].element_size()
+    return {"value": round(1000.0 * ms / (n * args.sequences), 3), "unit": UNIT, "h2d_bytes_per_step": nbytes,
+            "d2h_bytes_per_step": nbytes, "calls": n,
+            "path": ("sva_b200.kernels.decode_batched (eager calls) given pinned host q and out; its kernels read q "
+                     "from and write out to host memory" if world == 1 else
+                     "sva_b200.sharded.BatchedShardedDecoder.decode (eager calls) with torch copies of pinned host q "
+                     "and out around it")}
 
 
 # The JSON line is the only thing bench.py writes to its standard output: file descriptor 1 is

@@ -302,6 +302,19 @@ int sva_postings_build(const uint8_t* codes, int64_t codes_head_stride, int32_t 
                        void* stream);
 
 /* ---------------------------------------------------------------------------------------
+ * Incremental posting lists (replaces sva/llama.py:659-693, _append_postings): keys
+ * [start, start + count) are appended, in key order, to the lists of their codes, so every list
+ * stays ascending and equals what sva_postings_build would give for keys [0, start + count).
+ * The layout is padded: cell c of (head, subspace) owns id slots [offsets[c], offsets[c + 1]),
+ * counts[c] of them used; a key that would pass its cell's end is skipped and *overflow (device
+ * int32) is set, so callers size the cells from a bound on the counts (and rebuild when the bound
+ * reaches the cell size).  *max_bucket is raised to the largest count written.
+ * ------------------------------------------------------------------------------------- */
+int sva_postings_append(const uint8_t* codes, int64_t codes_head_stride, int32_t n_heads, int32_t subspaces,
+                        int32_t codewords, int64_t start, int64_t count, int32_t* counts, const int32_t* offsets,
+                        int32_t* ids, int64_t ids_sub_stride, int32_t* max_bucket, int32_t* overflow, void* stream);
+
+/* ---------------------------------------------------------------------------------------
  * No-alloc variant of sva_postings_build.  No reference counterpart: the reference builds its
  * posting lists with torch ops that allocate as they go (sva/llama.py:626-657).
  *
@@ -391,6 +404,34 @@ typedef struct sva_inverted_args {
 
 size_t sva_inverted_workspace_size(const sva_inverted_args* args);
 int sva_decode_inverted(const sva_inverted_args* args, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Key-range shards of the static inverted-index summon.  Replaces sva/llama.py:427-576 when the
+ * static catalog is split by key range across ranks (the reference is single-device).
+ * Rank r's args describe its own keys, global indices [key_offset, key_offset + key_len), with
+ * posting lists over all of them (postings_len == key_len), dynamic == 0, allowed_len ==
+ * key_len, no allowed_mask and no selection outputs; max_bucket points to the largest posting
+ * list of the whole (global) catalog, and holds_current is 1 on the rank holding the global last
+ * key (the reference's current-key candidate), 0 elsewhere.  key_offset + key_len < 2^28.
+ *   sva_inverted_shard_summon : records_out [H][budget][4] u32: the rank's top-budget unique
+ *                               candidates (rank composite with the global key index and the
+ *                               multiplicity, fp32 verify logit), zero padded.  all-gather.
+ *   sva_inverted_shard_verify : from gathered [W][H][budget][4], the global selection, refill
+ *                               window, adaptive budget and softmax; partial_out [H][head_dim] f64
+ *                               = this rank's share of the output.  Takes the workspace the
+ *                               summon filled.  all-gather.
+ *   sva_inverted_shard_combine: from gathered partials [W][H][head_dim], writes args->out.
+ * The final sets equal sva_decode_inverted's over the concatenated keys; outputs equal it up to
+ * the order of exact fp64 sums.
+ * ------------------------------------------------------------------------------------- */
+size_t sva_inverted_shard_workspace_size(const sva_inverted_args* args);
+int sva_inverted_shard_summon(const sva_inverted_args* args, int64_t key_offset, int32_t holds_current,
+                              uint32_t* records_out, void* workspace, size_t workspace_bytes, void* stream);
+int sva_inverted_shard_verify(const sva_inverted_args* args, int64_t key_offset, int32_t holds_current, int32_t world,
+                              int32_t rank, const uint32_t* gathered_records, double* partial_out, void* workspace,
+                              size_t workspace_bytes, void* stream);
+int sva_inverted_shard_combine(const sva_inverted_args* args, int32_t world, const double* gathered_partials,
+                               void* stream);
 
 /* ---------------------------------------------------------------------------------------
  * Refill-and-dedupe selection on explicit candidate rows.  Replaces sva/llama.py:83-116

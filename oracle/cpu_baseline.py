@@ -81,7 +81,8 @@ class CpuDecoder:
         self.chunks = max(1, self.threads // n_heads)
 
     def __call__(self, q: np.ndarray, shortlist: int, budget: int, scaling: float, dtype: str,
-                 logits_mode: int = 1) -> np.ndarray:
+                 logits_mode: int = 1, want_final: bool = False):
+        """Outputs [H, D] (and, with want_final, every head's final key set, ascending)."""
         n_heads, _, rank = self.q_proj.shape
         key_len = self.codes.shape[1]
         sl_cap = min(shortlist, key_len)
@@ -109,10 +110,13 @@ class CpuDecoder:
             keep = topk_canonical(rs, min(budget, sl.shape[0]))
             fin = sl[keep]
             kv = h // self.groups
-            return verify_one(q[h], _rows(self.keys[kv], fin), _rows(self.values[kv], fin),
-                              np.arange(fin.shape[0]), scaling, dtype, logits_mode)
+            out = verify_one(q[h], _rows(self.keys[kv], fin), _rows(self.values[kv], fin),
+                             np.arange(fin.shape[0]), scaling, dtype, logits_mode)
+            return out, np.sort(fin)
 
-        return np.stack(list(self.pool.map(finish, range(n_heads))))
+        res = list(self.pool.map(finish, range(n_heads)))
+        outs = np.stack([r[0] for r in res])
+        return (outs, [r[1] for r in res]) if want_final else outs
 
     def close(self) -> None:
         self.pool.shutdown(wait=True)

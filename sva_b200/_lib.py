@@ -64,8 +64,13 @@ EXPORTED = (
     "sva_postings_workspace_size",
     "sva_postings_build",
     "sva_postings_build_noalloc",
+    "sva_postings_append",
     "sva_inverted_workspace_size",
     "sva_decode_inverted",
+    "sva_inverted_shard_workspace_size",
+    "sva_inverted_shard_summon",
+    "sva_inverted_shard_verify",
+    "sva_inverted_shard_combine",
     "sva_top_unique",
     "sva_adapter_forward",
 )
@@ -256,8 +261,16 @@ def load() -> ctypes.CDLL:
                                     c_sz, c_vp], ctypes.c_int),
             "sva_postings_build_noalloc": ([c_vp, c_i64, c_i32, c_i32, c_i32, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp,
                                             c_vp], ctypes.c_int),
+            "sva_postings_append": ([c_vp, c_i64, c_i32, c_i32, c_i32, c_i64, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp,
+                                     c_vp, c_vp], ctypes.c_int),
             "sva_inverted_workspace_size": ([ctypes.POINTER(InvertedArgs)], c_sz),
             "sva_decode_inverted": ([ctypes.POINTER(InvertedArgs), c_vp, c_sz, c_vp], ctypes.c_int),
+            "sva_inverted_shard_workspace_size": ([ctypes.POINTER(InvertedArgs)], c_sz),
+            "sva_inverted_shard_summon": ([ctypes.POINTER(InvertedArgs), c_i64, c_i32, c_vp, c_vp, c_sz, c_vp],
+                                          ctypes.c_int),
+            "sva_inverted_shard_verify": ([ctypes.POINTER(InvertedArgs), c_i64, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp,
+                                           c_sz, c_vp], ctypes.c_int),
+            "sva_inverted_shard_combine": ([ctypes.POINTER(InvertedArgs), c_i32, c_vp, c_vp], ctypes.c_int),
             "sva_top_unique": ([c_vp, c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp,
                                 ctypes.POINTER(ctypes.c_int32), c_vp], ctypes.c_int),
             "sva_adapter_forward": ([c_vp, c_i64, c_vp, c_i64, c_i32, c_vp, c_vp, c_vp, c_vp, c_f32, c_i32, c_i32,

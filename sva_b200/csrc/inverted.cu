@@ -56,6 +56,12 @@ struct InvParams {
   int score_blocks;
   int collect_blocks;
   int64_t cand_cap;
+  // key-range shards (sva_inverted_shard_*): every local key is in the posting lists, the
+  // reference's single current-key entry belongs to the rank holding the global last key, and
+  // the window width uses the global largest bucket (args.max_bucket)
+  int shard;
+  int holds_current;
+  int64_t key_offset;
   float* ws_ql;         // [H][64]
   int32_t* ws_seg;      // [H][kInvMaxSeg + 1]
   int32_t* ws_topc;     // [H][kInvMaxSeg]
@@ -142,7 +148,10 @@ __global__ void __launch_bounds__(256) inv_prep_kernel(const InvParams p) {
     const int64_t L = a.key_len;
     int64_t tail_start = a.postings_len < 0 ? 0 : (a.postings_len > L ? L : a.postings_len);
     int64_t n_tail, current;
-    if (!a.dynamic && tail_start < L) {
+    if (p.shard) {
+      n_tail = p.holds_current ? 1 : 0;
+      current = p.holds_current;
+    } else if (!a.dynamic && tail_start < L) {
       n_tail = L - tail_start;
       current = 0;
     } else {
@@ -150,7 +159,8 @@ __global__ void __launch_bounds__(256) inv_prep_kernel(const InvParams p) {
       current = 1;
     }
     const int64_t maxb = a.max_bucket ? static_cast<int64_t>(__ldg(a.max_bucket)) : 0;
-    const int64_t W = static_cast<int64_t>(p.nseg) * (maxb > 1 ? maxb : 1) + n_tail;
+    // shards: the global candidate list has one current-key entry
+    const int64_t W = static_cast<int64_t>(p.nseg) * (maxb > 1 ? maxb : 1) + (p.shard ? 1 : n_tail);
     const int64_t want = (int64_t)a.budget * (a.refill_factor > 1 ? a.refill_factor : 1);
     const int64_t rcnt = W < want ? W : want;
     int64_t* meta = p.ws_meta + (size_t)h * IM_WORDS;
@@ -388,6 +398,54 @@ __host__ __device__ inline InvSmem inv_final_layout(int head_dim, int budget_pow
   return s;
 }
 
+// The k = min(budget, unique candidates) best unique candidates of head h as composites
+// (rank key << 32 | ~(key << 4 | multiplicity)), from the collect stage's part / edge lists (or
+// all candidates when the edge overflowed), sorted best first into comp[0, k); returns k.
+// Block-cooperative; ends with a barrier.
+__device__ int inv_topk_sorted(const InvParams& p, int h, unsigned long long* comp, uint2* tmp, SelectScratch* sc,
+                               int* scratch, int budget_pow2) {
+  const sva_inverted_args& a = p.a;
+  const int tid = threadIdx.x;
+  const uint32_t* ctrl = p.ws_ctrl + (size_t)h * IC_WORDS;
+  const int k = static_cast<int>(__ldcg(ctrl + IC_K));
+  const int n_part = min(static_cast<int>(__ldcg(ctrl + IC_NOUT)), a.budget);
+  const int n_edge = static_cast<int>(__ldcg(ctrl + IC_NEDGE));
+  const int64_t n_cand = imin64(__ldcg(ctrl + IC_NCAND), p.cand_cap);
+  const uint2* gpart = p.ws_part + (size_t)h * a.budget;
+  for (int i = tid; i < n_part; i += blockDim.x) {
+    const uint2 v = __ldcg(gpart + i);
+    comp[i] = composite(v.x, v.y);
+  }
+  if (k > 0 && n_part < k) {
+    const int need = k - n_part;
+    if (n_edge <= kInvEdgeCap) {
+      const uint2* gedge = p.ws_edge + (size_t)h * kInvEdgeCap;
+      for (int i = tid; i < n_edge; i += blockDim.x) tmp[i] = __ldcg(gedge + i);
+      __syncthreads();
+      auto item = [&](int i) -> unsigned long long { return composite(tmp[i].x, tmp[i].y); };
+      const SelectThreshold thr = cta_radix_select(item, n_edge, need, sc);
+      cta_compact(item, n_edge, thr, [&](int pos, int, unsigned long long c) { comp[n_part + pos] = c; }, scratch);
+    } else {
+      const uint2* gc = p.ws_cand + (size_t)h * p.cand_cap;
+      auto item = [&](int i) -> unsigned long long {
+        const uint2 v = __ldcg(gc + i);
+        return composite(v.x, v.y);
+      };
+      const SelectThreshold thr = cta_radix_select(item, static_cast<int>(n_cand), k, sc);
+      cta_compact(item, static_cast<int>(n_cand), thr, [&](int pos, int, unsigned long long c) { comp[pos] = c; },
+                  scratch);
+    }
+  }
+  __syncthreads();
+  // best first: sort the complemented composites ascending
+  for (int i = tid; i < k; i += blockDim.x) comp[i] = ~comp[i];
+  __syncthreads();
+  cta_bitonic_sort_u64(comp, k, budget_pow2);
+  for (int i = tid; i < k; i += blockDim.x) comp[i] = ~comp[i];
+  __syncthreads();
+  return k;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kInvThreads) inv_final_kernel(const InvParams p, const InvSmem lay, int budget_pow2) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -525,6 +583,185 @@ __global__ void __launch_bounds__(kInvThreads) inv_final_kernel(const InvParams 
     atomicAdd(a.stats + SVA_STAT_EXACT_SCORED, static_cast<unsigned long long>(n_fin));
     atomicAdd(a.stats + SVA_STAT_VERIFIED, static_cast<unsigned long long>(n_fin));
     atomicAdd(a.stats + SVA_STAT_CELL_VISITS, static_cast<unsigned long long>(p.nseg));
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// key-range shards of the static inverted summon
+// ---------------------------------------------------------------------------------------------
+// Rank r holds keys [key_offset, key_offset + key_len) with posting lists over them.  The top cells
+// come from the LUT, so they are the same on every rank; a key's multiplicity comes from its own
+// codes; so the global candidate list is the union of the ranks' lists, and the global top-budget
+// unique candidates are among the union of the ranks' top-budget lists.
+//   summon : prep, score, collect as on one GPU, then the local top-budget unique candidates as
+//            records (composite with the global key index, fp32 verify logit) -> all-gather
+//   verify : every rank selects the same global top-budget from the gathered records, applies
+//            the refill window and the adaptive budget, computes the softmax over the final keys'
+//            logits and the fp64 partial output of its own final keys -> all-gather
+//   combine: the output, summing the partials in rank order.
+
+template <typename T>
+__global__ void __launch_bounds__(kInvThreads) inv_shard_top_kernel(const InvParams p, const InvSmem lay,
+                                                                    int budget_pow2, uint4* __restrict__ records) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  float* qf = reinterpret_cast<float*>(smem + lay.qf);
+  SelectScratch* sc = reinterpret_cast<SelectScratch*>(smem + lay.sc);
+  int* scratch = reinterpret_cast<int*>(smem + lay.scratch);
+  unsigned long long* comp = reinterpret_cast<unsigned long long*>(smem + lay.comp);
+  uint2* tmp = reinterpret_cast<uint2*>(smem + lay.tmp);
+  int32_t* rows = reinterpret_cast<int32_t*>(smem + lay.fin);
+  float* lg = reinterpret_cast<float*>(smem + lay.lg);
+  const sva_inverted_args& a = p.a;
+  const int h = blockIdx.x, tid = threadIdx.x, D = a.head_dim;
+  const int kvh = h / p.groups;
+  const T* q = reinterpret_cast<const T*>(a.query) + h * a.q_head_stride;
+  for (int d = tid; d < D; d += blockDim.x) qf[d] = to_f32<T>(q[d]);
+  const int k = inv_topk_sorted(p, h, comp, tmp, sc, scratch, budget_pow2);
+  for (int j = tid; j < k; j += blockDim.x) rows[j] = static_cast<int32_t>((~static_cast<uint32_t>(comp[j])) >> 4);
+  __syncthreads();
+  verify_logits<T>(a.keys, a.k_head_stride, a.k_row_stride, kvh, qf, D, rows, k, a.softmax_scale, 0, lg);
+  for (int j = tid; j < a.budget; j += blockDim.x) {
+    uint4 rec = make_uint4(0u, 0u, 0u, 0u);
+    if (j < k) {
+      const uint32_t low = ~static_cast<uint32_t>(comp[j]);  // (local << 4) | multiplicity
+      const uint32_t g = ((low >> 4) + static_cast<uint32_t>(p.key_offset)) << 4 | (low & 15u);
+      const unsigned long long c = (comp[j] & 0xFFFFFFFF00000000ull) | static_cast<unsigned long long>(~g);
+      rec = make_uint4(static_cast<uint32_t>(c), static_cast<uint32_t>(c >> 32), __float_as_uint(lg[j]), 0u);
+    }
+    records[(size_t)h * a.budget + j] = rec;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kInvThreads) inv_shard_verify_kernel(const InvParams p, const InvSmem lay,
+                                                                       int budget_pow2, int world, int rank,
+                                                                       const uint4* __restrict__ gathered,
+                                                                       double* __restrict__ partial_out) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  SelectScratch* sc = reinterpret_cast<SelectScratch*>(smem + lay.sc);
+  int* scratch = reinterpret_cast<int*>(smem + lay.scratch);
+  unsigned long long* comp = reinterpret_cast<unsigned long long*>(smem + lay.comp);
+  int32_t* fin = reinterpret_cast<int32_t*>(smem + lay.fin);
+  float* lg = reinterpret_cast<float*>(smem + lay.lg);
+  double* acc = reinterpret_cast<double*>(smem + lay.acc);
+  float* wt = reinterpret_cast<float*>(smem + lay.tmp);                     // [budget]
+  int32_t* rows = reinterpret_cast<int32_t*>(smem + lay.tmp) + budget_pow2;  // [budget]
+  __shared__ int n_fin_sh, n_own_sh, budget_sh;
+  const sva_inverted_args& a = p.a;
+  const int h = blockIdx.x, tid = threadIdx.x, D = a.head_dim, B = a.budget;
+  const int kvh = h / p.groups;
+  const int H = a.n_heads;
+  auto rec = [&](int i) -> uint4 {
+    const int r = i / B, j = i - r * B;
+    return __ldcg(gathered + ((size_t)r * H + h) * B + j);
+  };
+  auto item = [&](int i) -> unsigned long long {
+    const uint4 v = rec(i);
+    return (static_cast<unsigned long long>(v.y) << 32) | v.x;
+  };
+  const int N = world * B;
+  int nz = 0;
+  for (int i = tid; i < N; i += blockDim.x) nz += item(i) != 0ull;
+  int tot;
+  (void)block_excl_scan(nz, scratch, &tot);
+  const int k = min(B, tot);
+  const SelectThreshold thr = cta_radix_select(item, N, k, sc);
+  // composites and logits of the selected records; the logit rides in a parallel array after sort
+  cta_compact(item, N, thr, [&](int pos, int i, unsigned long long c) { comp[pos] = c; }, scratch);
+  for (int i = tid; i < k; i += blockDim.x) comp[i] = ~comp[i];
+  __syncthreads();
+  cta_bitonic_sort_u64(comp, k, budget_pow2);
+  for (int i = tid; i < k; i += blockDim.x) comp[i] = ~comp[i];
+  __syncthreads();
+  const int64_t rcnt = p.ws_meta[(size_t)h * IM_WORDS + IM_RCNT];
+  {
+    int running = 0;
+    for (int base = 0; base < k; base += blockDim.x) {
+      const int j = base + tid;
+      int m = 0;
+      if (j < k) m = static_cast<int>((~static_cast<uint32_t>(comp[j])) & 15u);
+      int t2;
+      const int ex = block_excl_scan(m, scratch, &t2);
+      if (j < k) fin[j] = (static_cast<int64_t>(running + ex) < rcnt) ? 1 : 0;
+      running += t2;
+    }
+  }
+  __syncthreads();
+  const int width = static_cast<int>(imin64(B, rcnt));
+  if (tid == 0) {
+    const float fmin = -3.4028234663852886e+38f;
+    auto score_at = [&](int j) -> float {
+      if (j < k && fin[j]) return key_to_float(static_cast<uint32_t>(comp[j] >> 32));
+      return fmin;
+    };
+    int b;
+    if (width > 1) {
+      const int ref = min(a.min_budget, width) - 1;
+      const float margin = __fsub_rn(score_at(0), score_at(ref));
+      if (margin >= a.high_margin) b = a.min_budget;
+      else if (margin >= a.low_margin) b = a.mid_budget;
+      else b = a.budget;
+      b = min(b, width);
+    } else {
+      b = 1;
+    }
+    budget_sh = b;
+    int n = 0;
+    for (int j = 0; j < min(k, width); ++j)
+      if (fin[j] && j < b) fin[n++] = j;  // positions in comp
+    n_fin_sh = n;
+  }
+  __syncthreads();
+  const int n_fin = n_fin_sh;
+  // logits of the final keys in rank order (the one-GPU path's order), from the records
+  for (int j = tid; j < n_fin; j += blockDim.x) {
+    const unsigned long long c = comp[fin[j]];
+    float l = 0.f;
+    for (int i = 0; i < N; ++i) {
+      const uint4 v = rec(i);
+      if (((static_cast<unsigned long long>(v.y) << 32) | v.x) == c) {
+        l = __uint_as_float(v.z);
+        break;
+      }
+    }
+    lg[j] = l;
+  }
+  __syncthreads();
+  float mx, denom;
+  softmax_stats(lg, n_fin, scratch, acc, &mx, &denom);
+  if (tid == 0) {
+    int n = 0;
+    for (int j = 0; j < n_fin; ++j) {
+      const uint32_t g = (~static_cast<uint32_t>(comp[fin[j]])) >> 4;
+      const int64_t l = static_cast<int64_t>(g) - p.key_offset;
+      if (l >= 0 && l < a.key_len) {
+        rows[n] = static_cast<int32_t>(l);
+        wt[n] = round_to<T>(expf(lg[j] - mx) / denom);
+        ++n;
+      }
+    }
+    n_own_sh = n;
+  }
+  __syncthreads();
+  double* sums = acc + (kInvThreads / 32) * 64;
+  accumulate_rows<T>(a.values, a.v_head_stride, a.v_row_stride, kvh, D, rows, wt, n_own_sh, acc, sums);
+  for (int d = tid; d < D; d += blockDim.x) partial_out[(size_t)h * D + d] = sums[d];
+  if (a.stats && rank == 0 && tid == 0) {
+    atomicAdd(a.stats + SVA_STAT_QUERIES, 1ull);
+    atomicAdd(a.stats + SVA_STAT_EXACT_SCORED, static_cast<unsigned long long>(n_fin));
+    atomicAdd(a.stats + SVA_STAT_VERIFIED, static_cast<unsigned long long>(n_fin));
+    atomicAdd(a.stats + SVA_STAT_CELL_VISITS, static_cast<unsigned long long>(p.nseg));
+  }
+}
+
+template <typename T>
+__global__ void inv_shard_combine_kernel(const sva_inverted_args a, int world, const double* __restrict__ gathered) {
+  const int h = blockIdx.x;
+  T* out = reinterpret_cast<T*>(a.out) + h * a.out_head_stride;
+  for (int d = threadIdx.x; d < a.head_dim; d += blockDim.x) {
+    double tot = 0.0;
+    for (int r = 0; r < world; ++r) tot += __ldcg(gathered + ((size_t)r * a.n_heads + h) * a.head_dim + d);
+    out[d] = from_f32<T>(static_cast<float>(tot));
   }
 }
 
@@ -747,6 +984,124 @@ extern "C" int sva_decode_inverted(const sva_inverted_args* args, void* workspac
     case SVA_DTYPE_BF16: return launch_inverted<__nv_bfloat16>(plan, workspace, st);
     default: return launch_inverted<__half>(plan, workspace, st);
   }
+}
+
+static int plan_inverted_shard(const sva_inverted_args* a, int64_t key_offset, int32_t holds_current, InvPlan* plan) {
+  int rc = plan_inverted(a, plan);
+  if (rc != SVA_OK) return rc;
+  if (a->dynamic) return set_error(SVA_ERR_SHAPE, "inverted shards take the static summon (dynamic == 0)");
+  if (a->postings_len != a->key_len)
+    return set_error(SVA_ERR_SHAPE, "inverted shards need posting lists over every local key (postings_len == key_len)");
+  if (a->allowed_len != a->key_len || a->allowed_mask)
+    return set_error(SVA_ERR_SHAPE, "inverted shards take no allowed_len limit or allowed_mask");
+  if (a->sel_idx_out || a->sel_valid_out || a->sel_score_out || a->budget_out)
+    return set_error(SVA_ERR_SHAPE, "inverted shards write no selection outputs");
+  if (key_offset < 0 || key_offset + a->key_len >= (1ll << 28))
+    return set_error(SVA_ERR_SHAPE, "key_offset + key_len must be below 2^28");
+  plan->p.shard = 1;
+  plan->p.holds_current = holds_current ? 1 : 0;
+  plan->p.key_offset = key_offset;
+  return SVA_OK;
+}
+
+static void bind_inverted_workspace(InvParams& p, void* ws) {
+  char* b = static_cast<char*>(ws);
+  p.ws_ql = reinterpret_cast<float*>(b + reinterpret_cast<size_t>(p.ws_ql));
+  p.ws_seg = reinterpret_cast<int32_t*>(b + reinterpret_cast<size_t>(p.ws_seg));
+  p.ws_topc = reinterpret_cast<int32_t*>(b + reinterpret_cast<size_t>(p.ws_topc));
+  p.ws_member = reinterpret_cast<uint32_t*>(b + reinterpret_cast<size_t>(p.ws_member));
+  p.ws_meta = reinterpret_cast<int64_t*>(b + reinterpret_cast<size_t>(p.ws_meta));
+  p.ws_hist = reinterpret_cast<uint32_t*>(b + reinterpret_cast<size_t>(p.ws_hist));
+  p.ws_ctrl = reinterpret_cast<uint32_t*>(b + reinterpret_cast<size_t>(p.ws_ctrl));
+  p.ws_cand = reinterpret_cast<uint2*>(b + reinterpret_cast<size_t>(p.ws_cand));
+  p.ws_part = reinterpret_cast<uint2*>(b + reinterpret_cast<size_t>(p.ws_part));
+  p.ws_edge = reinterpret_cast<uint2*>(b + reinterpret_cast<size_t>(p.ws_edge));
+}
+
+template <typename T>
+static int inverted_shard_summon(InvPlan& plan, void* ws, uint4* records, cudaStream_t st) {
+  InvParams& p = plan.p;
+  bind_inverted_workspace(p, ws);
+  const int H = p.a.n_heads;
+  int rc = ensure_smem_attr(reinterpret_cast<const void*>(inv_prep_kernel<T>), 160 * 1024);
+  if (rc) return rc;
+  inv_prep_kernel<T><<<H, 256, 4 * p.a.head_dim * p.a.rank_dim, st>>>(p);
+  inv_score_kernel<<<dim3(p.score_blocks, H), kInvScoreThreads, 0, st>>>(p);
+  inv_collect_kernel<<<dim3(p.collect_blocks, H), 256, 0, st>>>(p);
+  rc = ensure_smem_attr(reinterpret_cast<const void*>(inv_shard_top_kernel<T>), kMaxDynSmem);
+  if (rc) return rc;
+  inv_shard_top_kernel<T><<<H, kInvThreads, plan.lay.total, st>>>(p, plan.lay, plan.budget_pow2, records);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SVA_OK : set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
+}
+
+template <typename T>
+static int inverted_shard_verify(InvPlan& plan, void* ws, int world, int rank, const uint4* gathered, double* partial,
+                                 cudaStream_t st) {
+  InvParams& p = plan.p;
+  bind_inverted_workspace(p, ws);
+  int rc = ensure_smem_attr(reinterpret_cast<const void*>(inv_shard_verify_kernel<T>), kMaxDynSmem);
+  if (rc) return rc;
+  inv_shard_verify_kernel<T><<<p.a.n_heads, kInvThreads, plan.lay.total, st>>>(p, plan.lay, plan.budget_pow2, world,
+                                                                               rank, gathered, partial);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SVA_OK : set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
+}
+
+extern "C" size_t sva_inverted_shard_workspace_size(const sva_inverted_args* args) {
+  InvPlan plan;
+  if (plan_inverted_shard(args, 0, 0, &plan) != SVA_OK) return 0;
+  return plan.ws_bytes;
+}
+
+extern "C" int sva_inverted_shard_summon(const sva_inverted_args* args, int64_t key_offset, int32_t holds_current,
+                                         uint32_t* records_out, void* workspace, size_t workspace_bytes, void* stream) {
+  InvPlan plan;
+  int rc = plan_inverted_shard(args, key_offset, holds_current, &plan);
+  if (rc != SVA_OK) return rc;
+  if (!records_out) return set_error(SVA_ERR_SHAPE, "records_out is null");
+  if (workspace_bytes < plan.ws_bytes || !workspace) return set_error(SVA_ERR_WORKSPACE, "inverted workspace too small");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto* r = reinterpret_cast<uint4*>(records_out);
+  switch (args->qkv_dtype) {
+    case SVA_DTYPE_F32: return inverted_shard_summon<float>(plan, workspace, r, st);
+    case SVA_DTYPE_BF16: return inverted_shard_summon<__nv_bfloat16>(plan, workspace, r, st);
+    default: return inverted_shard_summon<__half>(plan, workspace, r, st);
+  }
+}
+
+extern "C" int sva_inverted_shard_verify(const sva_inverted_args* args, int64_t key_offset, int32_t holds_current,
+                                         int32_t world, int32_t rank, const uint32_t* gathered_records,
+                                         double* partial_out, void* workspace, size_t workspace_bytes, void* stream) {
+  InvPlan plan;
+  int rc = plan_inverted_shard(args, key_offset, holds_current, &plan);
+  if (rc != SVA_OK) return rc;
+  if (world < 1 || rank < 0 || rank >= world) return set_error(SVA_ERR_SHAPE, "need 0 <= rank < world");
+  if (!gathered_records || !partial_out) return set_error(SVA_ERR_SHAPE, "null pointer");
+  if (workspace_bytes < plan.ws_bytes || !workspace) return set_error(SVA_ERR_WORKSPACE, "inverted workspace too small");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto* g = reinterpret_cast<const uint4*>(gathered_records);
+  switch (args->qkv_dtype) {
+    case SVA_DTYPE_F32: return inverted_shard_verify<float>(plan, workspace, world, rank, g, partial_out, st);
+    case SVA_DTYPE_BF16: return inverted_shard_verify<__nv_bfloat16>(plan, workspace, world, rank, g, partial_out, st);
+    default: return inverted_shard_verify<__half>(plan, workspace, world, rank, g, partial_out, st);
+  }
+}
+
+extern "C" int sva_inverted_shard_combine(const sva_inverted_args* args, int32_t world, const double* gathered_partials,
+                                          void* stream) {
+  if (!args || !args->out || !gathered_partials) return set_error(SVA_ERR_SHAPE, "null pointer");
+  if (world < 1 || args->n_heads <= 0 || args->head_dim <= 0) return set_error(SVA_ERR_SHAPE, "bad sizes");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (args->qkv_dtype) {
+    case SVA_DTYPE_F32: inv_shard_combine_kernel<float><<<args->n_heads, 128, 0, st>>>(*args, world, gathered_partials); break;
+    case SVA_DTYPE_BF16:
+      inv_shard_combine_kernel<__nv_bfloat16><<<args->n_heads, 128, 0, st>>>(*args, world, gathered_partials);
+      break;
+    default: inv_shard_combine_kernel<__half><<<args->n_heads, 128, 0, st>>>(*args, world, gathered_partials); break;
+  }
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SVA_OK : set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
 }
 
 extern "C" int sva_top_unique(const int64_t* idx, const float* scores, const uint8_t* valid, int32_t rows,

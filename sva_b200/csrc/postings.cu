@@ -174,6 +174,39 @@ extern "C" int sva_postings_build(const uint8_t* codes, int64_t codes_head_strid
   return SVA_OK;
 }
 
+// ---- incremental append ------------------------------------------------------------------
+// Keys [start, start + count) are appended to the lists of their codes, in key order, so every
+// list stays ascending: one thread per (head, subspace) walks the new keys.  Each cell c owns the
+// id slots [offsets[c], offsets[c + 1]) (a padded layout); a key that would pass its cell's end is
+// not written and *overflow is set, so a caller sizes the cells from a bound on the counts.
+__global__ void post_append_kernel(const uint8_t* __restrict__ codes, int64_t codes_head_stride, int H, int S, int C,
+                                   int64_t start, int64_t count, int32_t* __restrict__ counts,
+                                   const int32_t* __restrict__ offsets, int32_t* __restrict__ ids,
+                                   int64_t ids_sub_stride, int32_t* __restrict__ max_bucket,
+                                   int32_t* __restrict__ overflow) {
+  const int hs = blockIdx.x * blockDim.x + threadIdx.x;
+  if (hs >= H * S) return;
+  const int h = hs / S, s = hs - h * S;
+  const uint8_t* cb = codes + h * codes_head_stride + s;
+  int32_t* cnt = counts + (size_t)hs * C;
+  const int32_t* off = offsets + (size_t)hs * (C + 1);
+  int32_t* id = ids + (size_t)hs * ids_sub_stride;
+  int biggest = 0;
+  for (int64_t l = start; l < start + count; ++l) {
+    const int c = __ldg(cb + l * S);
+    if (c >= C) continue;
+    const int pos = cnt[c];
+    if (off[c] + pos >= off[c + 1]) {
+      atomicExch(overflow, 1);
+      continue;
+    }
+    id[off[c] + pos] = static_cast<int32_t>(l);
+    cnt[c] = pos + 1;
+    biggest = max(biggest, pos + 1);
+  }
+  if (biggest > 0) atomicMax(max_bucket, biggest);
+}
+
 // ---- no-alloc variant ---------------------------------------------------------------------
 // The chunk histograms come from a fixed buffer inside the library (one per device, created
 // with the module) instead of a caller-provided workspace.  Nothing in it has to start at zero:
@@ -252,4 +285,21 @@ extern "C" int sva_postings_build_noalloc(const uint8_t* codes, int64_t codes_he
   }
   return sva_postings_build(codes, codes_head_stride, n_heads, subspaces, codewords, key_len, counts, offsets, ids,
                             ids_sub_stride, max_bucket, scratch, need, stream);
+}
+
+extern "C" int sva_postings_append(const uint8_t* codes, int64_t codes_head_stride, int32_t n_heads, int32_t subspaces,
+                                   int32_t codewords, int64_t start, int64_t count, int32_t* counts,
+                                   const int32_t* offsets, int32_t* ids, int64_t ids_sub_stride, int32_t* max_bucket,
+                                   int32_t* overflow, void* stream) {
+  if (n_heads <= 0 || subspaces <= 0 || subspaces > kMaxSubspaces || codewords <= 0 || codewords > kMaxCodewords)
+    return set_error(SVA_ERR_SHAPE, "bad postings shape");
+  if (start < 0 || count < 0 || start + count > 0x7FFFFFFFll) return set_error(SVA_ERR_SHAPE, "key range out of range");
+  if (!codes || !counts || !offsets || !ids || !max_bucket || !overflow) return set_error(SVA_ERR_SHAPE, "null pointer");
+  if (count == 0) return SVA_OK;
+  const int hs = n_heads * subspaces;
+  post_append_kernel<<<(hs + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      codes, codes_head_stride, n_heads, subspaces, codewords, start, count, counts, offsets, ids, ids_sub_stride,
+      max_bucket, overflow);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SVA_OK : set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
 }

@@ -275,11 +275,14 @@ def batched_args(q: torch.Tensor, q_proj: torch.Tensor, scale: torch.Tensor, cod
                  out: torch.Tensor | None = None, stats: torch.Tensor | None = None):
     """Validated (sva_decode_args, sva_batch_layout, out) for the tensors of a batched call (see
     decode_batched for the layouts)."""
-    for name, t in (("q", q), ("codes", codes), ("k_low", k_low), ("keys", keys), ("values", values)):
+    for name, t in (("codes", codes), ("k_low", k_low), ("keys", keys), ("values", values)):
         _cuda(t, name)
+    _cuda_or_host(q, "q")
+    if out is not None:
+        _cuda_or_host(out, "out")
     if q.dim() != 4 or codes.dim() != 4 or k_low.dim() != 4 or keys.dim() != 4 or values.dim() != 4:
         raise ValueError("decode_batched takes 4-d q, codes, k_low, keys and values")
-    dev = q.device
+    dev = codes.device
     n_seqs, n_heads, n_q, head_dim = q.shape
     n_kv = int(keys.shape[1])
     rank = int(q_proj.shape[-1])
@@ -357,12 +360,13 @@ def decode_batched(q: torch.Tensor, q_proj: torch.Tensor, scale: torch.Tensor, c
     int) bounds them (default: L, or max_pages * page_keys).  ``allowed_len`` [B, T] int64 and
     ``allowed_mask`` [B * T, >= L] uint8 as for ``decode``.  Returns out [B, H, T, D] (and
     shortlist / final index tensors [B, H, T, shortlist] / [B, H, T, budget] when requested).
+    As for ``decode``, q and out may be page-locked host tensors that the GPU can address.
     """
     a, lay, out = batched_args(q, q_proj, scale, codebooks, codes, k_low, keys, values, shortlist, budget,
                                seq_lens=seq_lens, page_table=page_table, max_len=max_len,
                                softmax_scale=softmax_scale, logits_mode=logits_mode, allowed_len=allowed_len,
                                allowed_mask=allowed_mask, out=out, stats=stats)
-    dev = q.device
+    dev = codes.device
     n_seqs, n_heads, n_q, _ = q.shape
     sl_out = fin_out = None
     if want_shortlist:
@@ -395,11 +399,14 @@ _inv_ws = Workspace()
 
 
 class Postings:
-    """Device CSR posting lists of one catalog (see sva_postings_build)."""
+    """Device posting lists of one catalog: CSR (sva_postings_build) or, with ``cap``, the padded
+    layout of sva_postings_append (cell c of every (head, subspace) owns ``cap`` id slots)."""
 
-    def __init__(self, counts, offsets, ids, max_bucket, key_len: int):
+    def __init__(self, counts, offsets, ids, max_bucket, key_len: int, cap: int | None = None):
         self.counts, self.offsets, self.ids, self.max_bucket = counts, offsets, ids, max_bucket
         self.key_len = int(key_len)
+        self.cap = cap
+        self.overflow = None
 
 
 def postings_build(codes: torch.Tensor, codewords: int, key_len: int | None = None) -> Postings:
@@ -424,18 +431,58 @@ def postings_build(codes: torch.Tensor, codewords: int, key_len: int | None = No
     return Postings(counts, offsets, ids, max_bucket, key_len)
 
 
-def decode_inverted(q: torch.Tensor, q_proj: torch.Tensor, scale: torch.Tensor, codebooks: torch.Tensor,
-                    codes: torch.Tensor, postings: Postings, k_low: torch.Tensor, keys: torch.Tensor,
-                    values: torch.Tensor, budget: int, cells: int, min_budget: int, mid_budget: int,
-                    low_margin: float = 0.35, high_margin: float = 0.70, dynamic: bool = False,
-                    refill_factor: int = 2, allowed_len: int | None = None, allowed_mask: torch.Tensor | None = None,
-                    softmax_scale: float | None = None,
-                    out: torch.Tensor | None = None, want_selection: bool = False, stats: torch.Tensor | None = None):
-    """Inverted-index decode of one token per head (reference sva/llama.py:427-576 / :330-425).
+def postings_padded(codes: torch.Tensor, codewords: int, key_len: int, cap: int | None = None) -> Postings:
+    """Posting lists of keys [0, key_len) in the padded layout with ``cap`` slots per cell (at least
+    the largest list; None: twice the largest list, at least 64 more): the CSR build, then each
+    list moved to its cell's slots.  Reads the largest list size on the host."""
+    csr = postings_build(codes, codewords, key_len=key_len)
+    largest = int(csr.max_bucket.item())
+    if cap is None:
+        cap = max(2 * largest, largest + 64)
+    if largest > cap:
+        raise ValueError(f"postings_padded: the largest list has {largest} keys, more than cap={cap}")
+    n_heads, subspaces, _ = csr.counts.shape
+    dev = codes.device
+    offsets = (torch.arange(codewords + 1, device=dev, dtype=torch.int32) * cap).expand(n_heads, subspaces, -1)
+    offsets = offsets.contiguous()
+    ids = torch.zeros(n_heads, subspaces, codewords * cap, dtype=torch.int32, device=dev)
+    if key_len > 0:
+        pos = torch.arange(key_len, device=dev, dtype=torch.int32).expand(n_heads, subspaces, -1).contiguous()
+        # cell of every CSR position, and its slot inside the cell
+        cell = torch.searchsorted(csr.offsets[..., 1:].contiguous(), pos, right=True)
+        slot = pos - torch.gather(csr.offsets, 2, cell)
+        ids.scatter_(2, (cell * cap + slot).to(torch.int64), csr.ids[..., :key_len])
+    out = Postings(csr.counts, offsets, ids, csr.max_bucket, key_len, cap=int(cap))
+    out.overflow = torch.zeros(1, dtype=torch.int32, device=dev)
+    out.largest_at_build = largest
+    return out
 
-    q [H, D]; codes [H, >=postings_len, S]; k_low [H, L, R]; keys/values [Hkv, L, D].  ``budget``,
-    ``min_budget`` and ``mid_budget`` are already clamped as the reference clamps them.
-    """
+
+def postings_append(codes: torch.Tensor, postings: Postings, start: int, count: int) -> None:
+    """Appends keys [start, start + count) of codes [H, L, S] to padded posting lists in place
+    (sva_postings_append; reference sva/llama.py:659-693)."""
+    if postings.cap is None:
+        raise ValueError("postings_append needs the padded layout (postings_padded)")
+    n_heads, _, subspaces = codes.shape
+    codewords = int(postings.counts.shape[-1])
+    rc = _lib.load().sva_postings_append(codes.data_ptr(), codes.stride(0), n_heads, subspaces, codewords, int(start),
+                                         int(count), postings.counts.data_ptr(), postings.offsets.data_ptr(),
+                                         postings.ids.data_ptr(), postings.ids.shape[-1],
+                                         postings.max_bucket.data_ptr(), postings.overflow.data_ptr(),
+                                         _stream(codes.device))
+    _lib.check(rc)
+    postings.key_len = int(start + count)
+
+
+def inverted_args(q: torch.Tensor, q_proj: torch.Tensor, scale: torch.Tensor, codebooks: torch.Tensor,
+                  codes: torch.Tensor, postings: Postings, k_low: torch.Tensor, keys: torch.Tensor,
+                  values: torch.Tensor, budget: int, cells: int, min_budget: int, mid_budget: int,
+                  low_margin: float = 0.35, high_margin: float = 0.70, dynamic: bool = False, refill_factor: int = 2,
+                  allowed_len: int | None = None, allowed_mask: torch.Tensor | None = None,
+                  softmax_scale: float | None = None, out: torch.Tensor | None = None,
+                  stats: torch.Tensor | None = None, max_bucket: torch.Tensor | None = None):
+    """Validated (sva_inverted_args, out) for decode_inverted's tensors; ``max_bucket`` (device int32)
+    overrides the postings' own largest bucket (the shards pass the global one)."""
     for name, t in (("q", q), ("codes", codes), ("k_low", k_low), ("keys", keys), ("values", values)):
         _cuda(t, name)
     dev = q.device
@@ -460,11 +507,32 @@ def decode_inverted(q: torch.Tensor, q_proj: torch.Tensor, scale: torch.Tensor, 
     a.codes, a.codes_head_stride = codes.data_ptr(), codes.stride(0)
     a.post_counts, a.post_offsets = postings.counts.data_ptr(), postings.offsets.data_ptr()
     a.post_ids, a.post_ids_sub_stride = postings.ids.data_ptr(), postings.ids.shape[-1]
-    a.max_bucket = postings.max_bucket.data_ptr()
+    a.max_bucket = (postings.max_bucket if max_bucket is None else max_bucket).data_ptr()
     a.k_low, a.k_low_head_stride = k_low.data_ptr(), k_low.stride(0)
     a.keys, a.k_head_stride, a.k_row_stride = keys.data_ptr(), keys.stride(0), keys.stride(1)
     a.values, a.v_head_stride, a.v_row_stride = values.data_ptr(), values.stride(0), values.stride(1)
     a.out, a.out_head_stride = out.data_ptr(), out.stride(0)
+    a.stats = _ptr(stats)
+    return a, out
+
+
+def decode_inverted(q: torch.Tensor, q_proj: torch.Tensor, scale: torch.Tensor, codebooks: torch.Tensor,
+                    codes: torch.Tensor, postings: Postings, k_low: torch.Tensor, keys: torch.Tensor,
+                    values: torch.Tensor, budget: int, cells: int, min_budget: int, mid_budget: int,
+                    low_margin: float = 0.35, high_margin: float = 0.70, dynamic: bool = False,
+                    refill_factor: int = 2, allowed_len: int | None = None, allowed_mask: torch.Tensor | None = None,
+                    softmax_scale: float | None = None,
+                    out: torch.Tensor | None = None, want_selection: bool = False, stats: torch.Tensor | None = None):
+    """Inverted-index decode of one token per head (reference sva/llama.py:427-576 / :330-425).
+
+    q [H, D]; codes [H, >=postings_len, S]; k_low [H, L, R]; keys/values [Hkv, L, D].  ``budget``,
+    ``min_budget`` and ``mid_budget`` are already clamped as the reference clamps them.
+    """
+    a, out = inverted_args(q, q_proj, scale, codebooks, codes, postings, k_low, keys, values, budget, cells,
+                           min_budget, mid_budget, low_margin, high_margin, dynamic, refill_factor, allowed_len,
+                           allowed_mask, softmax_scale, out, stats)
+    dev = q.device
+    n_heads = q.shape[0]
     sel = None
     if want_selection:
         sel = (torch.empty(n_heads, int(budget), dtype=torch.int32, device=dev),
@@ -472,7 +540,6 @@ def decode_inverted(q: torch.Tensor, q_proj: torch.Tensor, scale: torch.Tensor, 
                torch.empty(n_heads, int(budget), dtype=torch.float32, device=dev),
                torch.empty(n_heads, dtype=torch.int32, device=dev))
         a.sel_idx_out, a.sel_valid_out, a.sel_score_out, a.budget_out = (t.data_ptr() for t in sel)
-    a.stats = _ptr(stats)
     lib = _lib.load()
     ws_bytes = int(lib.sva_inverted_workspace_size(ctypes.byref(a)))
     if ws_bytes == 0:

@@ -106,6 +106,7 @@ class SVALlamaAttention(nn.Module):
         self._k_low_buf: torch.Tensor | None = None   # [H, cap, R] fp32
         self._codes_buf: torch.Tensor | None = None   # [H, cap, S] uint8
         self._postings: kernels.Postings | None = None
+        self._post_bound = 0
         self._codes_len = 0
         self._cached_postings_key_len = 0
         self._cached_key_len = 0
@@ -432,6 +433,22 @@ class SVALlamaAttention(nn.Module):
         self._postings = kernels.postings_build(self._codes_buf, int(self.sva_coarse_codebooks.shape[2]), key_len=key_len)
         self._cached_postings_key_len = key_len
 
+    def _append_postings(self, start: int, count: int) -> None:
+        """Dynamic inverted mode: append the new keys' ids to their cells (reference
+        sva/llama.py:659-693) instead of rebuilding every list.  The lists use the padded layout;
+        the host keeps an upper bound of the largest list (its size at the last rebuild plus the
+        keys appended since), and rebuilds with twice the room when the bound reaches the cell
+        size, so appends never overflow and cost O(new keys) between rebuilds."""
+        post = self._postings
+        if post is None or post.cap is None or self._post_bound + count > post.cap:
+            self._postings = kernels.postings_padded(self._codes_buf, int(self.sva_coarse_codebooks.shape[2]),
+                                                     start + count)
+            self._post_bound = self._postings.largest_at_build  # one host read per rebuild
+        else:
+            kernels.postings_append(self._codes_buf, post, start, count)
+            self._post_bound += count
+        self._cached_postings_key_len = start + count
+
     def _tensor_core_write(self, keys: torch.Tensor) -> bool:
         """Whether new keys go through the tcgen05 projection (serving option ``write_path``)."""
         if self.serving.write_path == "exact":
@@ -464,7 +481,7 @@ class SVALlamaAttention(nn.Module):
         if can_append:
             if mode == "inverted":
                 self._codes_len = k_len
-                self._rebuild_postings(k_len)
+                self._append_postings(start, k_len - start)
             elif mode == "inverted_static" and q_len == 1:
                 interval = max(1, int(self.serving.static_tail_rebuild_interval))
                 if self._postings is None or k_len - self._cached_postings_key_len >= interval:

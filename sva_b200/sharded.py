@@ -183,6 +183,21 @@ class BatchedShardedDecoder:
         self.fallbacks = 0
         self.stage_events = None  # optional list of 7 CUDA events recorded between the stages
 
+    def full_width(self):
+        """Context manager: calls inside it exchange the whole shortlist (never saturate)."""
+        import contextlib
+
+        @contextlib.contextmanager
+        def ctx():
+            saved = self.width
+            self.width = self.shortlist
+            try:
+                yield self
+            finally:
+                self.width = saved
+
+        return ctx()
+
     def _gather(self, t: torch.Tensor) -> torch.Tensor:
         if self.world == 1:
             return t.unsqueeze(0)
@@ -199,8 +214,14 @@ class BatchedShardedDecoder:
 
     def decode(self, q, q_proj, scale, codebooks, codes, k_low, keys, values, *, seq_lens=None, page_table=None,
                max_len=None, key_offset: int = 0, page_dealt: bool = False, out=None, logits_mode: int = 0,
-               softmax_scale: float | None = None, stats=None) -> torch.Tensor:
-        """This rank's local arrays in decode_batched's layouts; returns out [B, H, 1, D]."""
+               softmax_scale: float | None = None, stats=None, saturated: torch.Tensor | None = None) -> torch.Tensor:
+        """This rank's local arrays in decode_batched's layouts; returns out [B, H, 1, D].
+
+        With ``saturated`` (an int32 device tensor of one element, zeroed by the caller) the call
+        reads nothing back on the host: it runs at the exchange width only and ORs the rescore
+        stage's flag into ``saturated``, so that it can be captured in a CUDA graph; a caller that
+        finds the flag set must repeat the call with ``full_width()`` in effect.
+        """
         if q.dim() != 4 or q.shape[2] != 1:
             raise ValueError("batched sharded decode takes one query token per sequence and head: q [B, H, 1, D]")
         a, lay, out = kernels.batched_args(q, q_proj, scale, codebooks, codes, k_low, keys, values, self.shortlist,
@@ -231,13 +252,14 @@ class BatchedShardedDecoder:
             g_top = self._gather(top)
             self._mark(2)
             rec = torch.empty(P, width, 4, dtype=torch.int32, device=q.device)
-            sat = torch.zeros(1, dtype=torch.int32, device=q.device)
+            sat = saturated if saturated is not None else torch.zeros(1, dtype=torch.int32, device=q.device)
             _lib.check(lib.sva_shard_batched_rescore(ctypes.byref(a), ctypes.byref(lay), ctypes.byref(m), width,
                                                      self.world, self.rank, g_top.data_ptr(), rec.data_ptr(),
                                                      sat.data_ptr(), ws.data_ptr(), ws_bytes, stream))
             self._mark(3)
             # every rank reads the same flag (it is computed from the same gathered lists)
-            if width >= self.shortlist or not self.check_saturation or int(sat.item()) == 0:
+            if (saturated is not None or width >= self.shortlist or not self.check_saturation
+                    or int(sat.item()) == 0):
                 break
             self.fallbacks += 1
             width = self.shortlist
@@ -252,3 +274,72 @@ class BatchedShardedDecoder:
                                                  stream))
         self._mark(6)
         return out
+
+
+class ShardedInvertedDecoder:
+    """Exact static inverted-index decode (reference sva/llama.py:427-576) over a key-range sharded
+    static catalog (sva_inverted_shard_*, include/sva_b200.h): one token per head, two
+    all-gathers (the ranks' top-budget candidate records, then the fp64 partial outputs).
+
+    Each rank passes its own codes / k_low / keys / values and posting lists over its keys
+    [key_offset, key_offset + L_r); ``global_max_bucket`` is the largest posting list of the whole
+    catalog (``global_max_bucket(postings, group)`` computes it once per catalog), and the rank
+    holding the global last key must pass ``holds_current=True``.
+    """
+
+    def __init__(self, group, budget: int, cells: int = 8, min_budget: int | None = None,
+                 mid_budget: int | None = None, low_margin: float = 0.35, high_margin: float = 0.70) -> None:
+        self.group = group
+        self.world = dist.get_world_size(group) if group is not None else 1
+        self.rank = dist.get_rank(group) if group is not None else 0
+        self.budget, self.cells = int(budget), int(cells)
+        self.min_budget = int(min_budget or budget)
+        self.mid_budget = int(mid_budget or max(self.min_budget, budget // 2))
+        self.low_margin, self.high_margin = float(low_margin), float(high_margin)
+        self._ws = kernels.Workspace()
+        self._nccl = group is not None and dist.get_backend(group) == "nccl"
+
+    def _gather(self, t: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return t.unsqueeze(0)
+        out = torch.empty((self.world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+        if self._nccl:
+            dist.all_gather_into_tensor(out, t.contiguous(), group=self.group)
+        else:
+            dist.all_gather(list(out.unbind(0)), t.contiguous(), group=self.group)
+        return out
+
+    def decode(self, q, q_proj, scale, codebooks, codes, postings, k_low, keys, values, *, key_offset: int,
+               holds_current: bool, global_max_bucket: torch.Tensor, out=None, softmax_scale=None, stats=None):
+        a, out = kernels.inverted_args(q, q_proj, scale, codebooks, codes, postings, k_low, keys, values, self.budget,
+                                       self.cells, self.min_budget, self.mid_budget, self.low_margin,
+                                       self.high_margin, False, 2, None, None, softmax_scale, out, stats,
+                                       max_bucket=global_max_bucket)
+        lib = _lib.load()
+        ws_bytes = int(lib.sva_inverted_shard_workspace_size(ctypes.byref(a)))
+        if ws_bytes == 0:
+            _lib.check(lib.sva_inverted_shard_summon(ctypes.byref(a), int(key_offset), int(holds_current), None, None,
+                                                     0, None))
+        ws = self._ws.get(q.device, ws_bytes)
+        stream = kernels._stream(q.device)
+        H = int(q.shape[0])
+        rec = torch.empty(H, self.budget, 4, dtype=torch.int32, device=q.device)
+        _lib.check(lib.sva_inverted_shard_summon(ctypes.byref(a), int(key_offset), int(holds_current), rec.data_ptr(),
+                                                 ws.data_ptr(), ws_bytes, stream))
+        g_rec = self._gather(rec)
+        part = torch.empty(H, int(q.shape[1]), dtype=torch.float64, device=q.device)
+        _lib.check(lib.sva_inverted_shard_verify(ctypes.byref(a), int(key_offset), int(holds_current), self.world,
+                                                 self.rank, g_rec.data_ptr(), part.data_ptr(), ws.data_ptr(), ws_bytes,
+                                                 stream))
+        g_part = self._gather(part)
+        _lib.check(lib.sva_inverted_shard_combine(ctypes.byref(a), self.world, g_part.data_ptr(), stream))
+        return out
+
+
+def global_max_bucket(postings, group) -> torch.Tensor:
+    """The largest posting list of a key-range sharded catalog: the maximum over (head, subspace,
+    cell) of the cell sizes summed over the ranks (one all-reduce of the counts)."""
+    counts = postings.counts.to(torch.int64).clone()
+    if group is not None and dist.get_world_size(group) > 1:
+        dist.all_reduce(counts, op=dist.ReduceOp.SUM, group=group)
+    return counts.max().to(torch.int32).reshape(1)

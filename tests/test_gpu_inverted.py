@@ -155,3 +155,53 @@ def test_top_unique_matches_oracle(width, budget):
         np.testing.assert_array_equal(sv[r].cpu().numpy(), o_sv[r])
         np.testing.assert_array_equal(sel[r].cpu().numpy()[o_sv[r]], o_sel[r][o_sv[r]])
         np.testing.assert_array_equal(sc[r].cpu().numpy()[o_sv[r]], o_sc[r][o_sv[r]])
+
+
+def test_incremental_postings_match_rebuild():
+    """Appending keys one or a few at a time (sva_postings_append, the dynamic mode's per-token
+    update, reference sva/llama.py:659-693) leaves every cell's list equal to a fresh build over
+    all keys, ascending; a dynamic inverted decode over the appended lists equals one over the
+    rebuilt lists; and an append past a cell's room is refused through the overflow flag."""
+    from sva_b200 import kernels
+
+    case = config1(key_len=6000)
+    k_low, codes = gpu_catalog(case)
+    C = int(case.codebooks.shape[2])
+    start = 5000
+    post = kernels.postings_padded(codes, C, start)
+    cap0 = post.cap
+    pos, steps = start, [1, 3, 1, 7, 2]
+    while pos < 6000:
+        n = min(steps[pos % len(steps)], 6000 - pos)
+        kernels.postings_append(codes, post, pos, n)
+        pos += n
+    ref = kernels.postings_build(codes, C, key_len=6000)
+    torch.cuda.synchronize()
+    assert int(post.overflow.item()) == 0
+    assert torch.equal(post.counts, ref.counts)
+    assert int(post.max_bucket.item()) == int(ref.max_bucket.item())
+    cnt, off = ref.counts.cpu().numpy(), ref.offsets.cpu().numpy()
+    ids_a, ids_r = post.ids.cpu().numpy(), ref.ids.cpu().numpy()
+    for h in range(cnt.shape[0]):
+        for s in range(cnt.shape[1]):
+            for c in range(C):
+                n = cnt[h, s, c]
+                np.testing.assert_array_equal(ids_a[h, s, c * cap0:c * cap0 + n],
+                                              ids_r[h, s, off[h, s, c]:off[h, s, c] + n])
+    dev = codes.device
+    args = (case.q[0][:, 0].to(dev), case.q_proj.to(dev), kernels.sva_scale(case.logit_scale).to(dev),
+            case.codebooks.to(dev), codes)
+    tail = (k_low, case.keys[0].to(dev), case.values[0].to(dev), 512, 8, 512, 512)
+    got = kernels.decode_inverted(*args, post, *tail, dynamic=True, softmax_scale=0.125)
+    want = kernels.decode_inverted(*args, ref, *tail, dynamic=True, softmax_scale=0.125)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    # cells sized for the first 5000 keys: an append past a cell's room is refused and flagged
+    cap = int(kernels.postings_build(codes, C, key_len=5000).max_bucket.item())
+    tight = kernels.postings_padded(codes, C, 5000, cap=cap)
+    kernels.postings_append(codes, tight, 5000, 1000)
+    torch.cuda.synchronize()
+    assert int(tight.overflow.item()) == int(bool((ref.counts > cap).any()))
+    assert bool((tight.counts <= cap).all())
+    with pytest.raises(ValueError):
+        kernels.postings_padded(codes, C, 6000, cap=cap - 1)
