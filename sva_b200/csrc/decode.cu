@@ -873,8 +873,8 @@ __host__ __device__ inline int wide_prep_smem_bytes() {
   return static_cast<int>(sizeof(SelectScratch)) + 4 * (kMaxHeadDim + kMaxRank + kMaxLut + kWideSample);
 }
 
-template <typename T, bool kB>
-__global__ void __launch_bounds__(kWidePrepThreads, 2) decode_prep_wide_kernel(const DecodeParams p) {
+template <typename T, bool kB, int NT = kWidePrepThreads>
+__global__ void __launch_bounds__(NT, NT >= 512 ? 1 : 2) decode_prep_wide_kernel(const DecodeParams p) {
   extern __shared__ __align__(16) unsigned char wdyn[];
   SelectScratch& sel = *reinterpret_cast<SelectScratch*>(wdyn);
   float* qf = reinterpret_cast<float*>(wdyn + sizeof(SelectScratch));
@@ -1596,9 +1596,11 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
 // footprint, so several problems share each SM and the gathers of many problems overlap:
 // shortlist select, rank rescore, budget select, verify -- the same steps, selections and
 // arithmetic as the cluster finish (and as the fused kernel).
-constexpr int kWideThreads = 256;
+constexpr int kWideThreads = 256;     // threads of a wide finish CTA when many problems share each SM
+constexpr int kWideMaxThreads = 512;  // ... and when there is about one problem per SM
 constexpr int kWideCands = 4096;  // candidates selected in shared memory (more are streamed from L2)
 constexpr int kWideMinProblems = 64;  // problems per launch from which the wide finish is used
+constexpr int kNumSmsHint = 148;      // B200 SMs: launches with at most this many problems give each 512 threads
 
 struct WideSmem {
   int qf, ql, sc, scratch, sl, rk, fin, lg, acc, cand, total;
@@ -1621,14 +1623,15 @@ __host__ __device__ inline WideSmem wide_smem_layout(int head_dim, int sl_cap, i
   s.rk = o;      o = align16(o + 4 * sl_cap);
   s.fin = o;     o = align16(o + 4 * b_cap);
   s.lg = o;      o = align16(o + 4 * b_cap);
-  s.acc = o;     o = align16(o + 8 * ((kWideThreads / 32) * 64 + kMaxHeadDim));
+  s.acc = o;     o = align16(o + 8 * ((kWideMaxThreads / 32) * 64 + kMaxHeadDim));
   s.cand = o;    o = align16(o + 8 * cand);
   s.total = o;
   return s;
 }
 
-template <typename T, bool kB>
-__global__ void __launch_bounds__(kWideThreads, 3) decode_finish_wide_kernel(const DecodeParams p, const WideSmem lay) {
+template <typename T, bool kB, int NT = kWideThreads>
+__global__ void __launch_bounds__(NT, NT >= 512 ? 1 : 3) decode_finish_wide_kernel(const DecodeParams p,
+                                                                                  const WideSmem lay) {
   extern __shared__ __align__(16) unsigned char smem[];
   float* qf = reinterpret_cast<float*>(smem + lay.qf);
   float* ql = reinterpret_cast<float*>(smem + lay.ql);
@@ -1948,11 +1951,15 @@ static int launch_prep_scan(DecodeParams& p, cudaStream_t stream) {
   const int P = p.n_probs;
   int rc;
   if (P >= kWideMinProblems) {
-    auto k = p.batched ? decode_prep_wide_kernel<T, true> : decode_prep_wide_kernel<T, false>;
+    // up to one problem per SM: 512 threads each (the latency of one problem bounds the launch);
+    // more: 256 threads, two problems per SM
+    const bool big = P <= kNumSmsHint;
+    auto k = big ? (p.batched ? decode_prep_wide_kernel<T, true, 512> : decode_prep_wide_kernel<T, false, 512>)
+                 : (p.batched ? decode_prep_wide_kernel<T, true> : decode_prep_wide_kernel<T, false>);
     const int smem = wide_prep_smem_bytes();
     rc = ensure_smem_attr(reinterpret_cast<const void*>(k), smem);
     if (rc != SVA_OK) return rc;
-    const cudaError_t e = launch_dependent(k, dim3(P), dim3(kWidePrepThreads), smem, stream, p);
+    const cudaError_t e = launch_dependent(k, dim3(P), dim3(big ? 512 : kWidePrepThreads), smem, stream, p);
     if (e != cudaSuccess) return set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
     profile_mark(0, stream);
     return launch_scan_for(p, P, stream);
@@ -1992,10 +1999,14 @@ static int launch_decode(DecodePlan& plan, void* ws, cudaStream_t stream) {
     if (rc != SVA_OK) return rc;
     cudaError_t le;
     if (plan.wide) {
-      auto wk = p.batched ? decode_finish_wide_kernel<T, true> : decode_finish_wide_kernel<T, false>;
+      const bool big = P <= kNumSmsHint;
+      auto wk = big ? (p.batched ? decode_finish_wide_kernel<T, true, kWideMaxThreads>
+                                 : decode_finish_wide_kernel<T, false, kWideMaxThreads>)
+                    : (p.batched ? decode_finish_wide_kernel<T, true> : decode_finish_wide_kernel<T, false>);
       rc = ensure_smem_attr(reinterpret_cast<const void*>(wk), plan.wide_lay.total);
       if (rc != SVA_OK) return rc;
-      le = launch_dependent(wk, dim3(P), dim3(kWideThreads), plan.wide_lay.total, stream, p, plan.wide_lay);
+      le = launch_dependent(wk, dim3(P), dim3(big ? kWideMaxThreads : kWideThreads), plan.wide_lay.total, stream, p,
+                            plan.wide_lay);
     } else {
       auto nk = p.batched ? decode_finish_kernel<T, true> : decode_finish_kernel<T, false>;
       rc = ensure_smem_attr(reinterpret_cast<const void*>(nk), static_cast<int>(plan.smem_bytes));
