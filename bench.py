@@ -694,6 +694,15 @@ def write_path_summary(args, write: dict, local_keys: int, peak: float) -> dict:
     keys = args.heads * local_keys
     flops = 2.0 * keys * 64 * 64
     nbytes = keys * (64 * 2 + 64 * 4 + s)
+    import torch
+
+    c = pq_shape(args.pq)[1]
+    # the exact path is bound by fp32 CUDA-core issue: every product and every sum is its own
+    # rounded instruction (no fused multiply-add), per key and head 2*D*R for the projection,
+    # 2*R*C for the codeword dot products, 2*R for |x|^2 and 3*S*C for the distances
+    ops = keys * (2.0 * 64 * 64 + 2.0 * 64 * c + 2.0 * 64 + 3.0 * s * c)
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    op_peak = sms * 128 * 1.965e9
     out = {"path": "exact CUDA-core projection and assignment (the adapter's default)"}
     for name, key in (("exact_", "exact_ms_per_set"), ("tc_", "tc_ms_per_set")):
         ms = write.get(key)
@@ -703,6 +712,10 @@ def write_path_summary(args, write: dict, local_keys: int, peak: float) -> dict:
         out[name + "keys_per_s"] = round(keys / (ms * 1e-3), 1)
         out[name + "projection_tflops"] = round(flops / (ms * 1e-3) / 1e12, 3)
         out[name + "hbm_frac"] = round(nbytes / (ms * 1e-3) / 1e9 / peak, 4)
+    if write.get("exact_ms_per_set"):
+        out["exact_fp32_ops_per_set"] = int(ops)
+        out["exact_cuda_core_frac"] = round(ops / (write["exact_ms_per_set"] * 1e-3) / op_peak, 4)
+        out["cuda_core_peak"] = f"{sms} SMs x 128 fp32 lanes x 1.965 GHz (nominal max clock)"
     out["algorithmic_bytes_per_set"] = int(nbytes)
     return out
 

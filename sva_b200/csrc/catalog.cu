@@ -179,6 +179,121 @@ __global__ void __launch_bounds__(kCatKeys) catalog_encode_kernel(const CatalogP
   if (p.k_low) store_k_low(p, h, l0, nrows, kl);
 }
 
+// Bulk path for head_dim = rank_dim = 64 and subspaces of SUB = 8, 16 or 32 values: the same
+// canonical arithmetic as catalog_encode_kernel (every projection output and every distance is
+// one thread's sequential fp32 dot product, the nearest codeword the first minimum in codeword
+// order), organised for occupancy: a thread holds its key row in registers and produces one
+// subspace at a time (SUB projection outputs, then that subspace's code), so shared memory holds
+// only the projection and the codebook (~33 KB) and several CTAs share each SM.  A CTA stages the
+// head's tables once and walks key tiles of kRegKeys keys.
+constexpr int kRegKeys = 128;
+constexpr int kRegCtasPerSm = 4;
+
+template <typename T, int SUB>
+__global__ void __launch_bounds__(kRegKeys, kRegCtasPerSm) catalog_encode_reg_kernel(const CatalogParams p,
+                                                                                   int vec_keys, int vec_out) {
+  constexpr int D = 64, R = 64, S = R / SUB;
+  extern __shared__ __align__(16) float sm[];
+  float* P = sm;                  // [D][R]
+  float* cbt = sm + D * R;        // [S][SUB][C]  (transposed codebook)
+  float* cn = cbt + R * p.C;      // [S][C]
+  const int h = blockIdx.y;
+  const int kvh = h / p.groups;
+  const int tid = threadIdx.x;
+  const int C = p.C;
+  const int64_t start = p.start_dev ? __ldg(p.start_dev) + p.start : p.start;
+  const int64_t l_end = min(start + p.count, p.limit);
+  if (start < 0 || start >= l_end) return;  // uniform over the grid
+  const int64_t n_tiles = (l_end - start + kRegKeys - 1) / kRegKeys;
+  if (blockIdx.x >= n_tiles) return;
+  const float* Pg = p.k_proj + (size_t)h * D * R;
+  for (int e = tid; e < D * R / 4; e += blockDim.x)
+    reinterpret_cast<float4*>(P)[e] = __ldg(reinterpret_cast<const float4*>(Pg) + e);
+  if (p.codes) stage_codebooks(p, h, cbt);
+  __syncthreads();
+  if (p.codes) codeword_norms(p, cbt, cn);
+  __syncthreads();
+  const T* kb = reinterpret_cast<const T*>(p.keys) + kvh * p.key_head_stride;
+  for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+    const int64_t l = start + tile * kRegKeys + tid;
+    if (l >= l_end) continue;
+    const T* kr = kb + l * p.key_row_stride;
+    float x[D];
+    if (vec_keys) {
+      constexpr int kPer = 16 / static_cast<int>(sizeof(T));  // elements per 16-byte load
+#pragma unroll
+      for (int v = 0; v < D / kPer; ++v) {
+        const uint4 w = __ldg(reinterpret_cast<const uint4*>(kr) + v);
+        const T* e = reinterpret_cast<const T*>(&w);
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) x[v * kPer + k] = to_f32<T>(e[k]);
+      }
+    } else {
+#pragma unroll
+      for (int d = 0; d < D; ++d) x[d] = to_f32<T>(kr[d]);
+    }
+    float* kout = p.k_low ? p.k_low + h * p.k_low_head_stride + l * R : nullptr;
+    uint8_t* crow = p.codes ? p.codes + h * p.codes_head_stride + l * S : nullptr;
+#pragma unroll 1
+    for (int s = 0; s < S; ++s) {
+      float y[SUB];
+#pragma unroll
+      for (int j = 0; j < SUB; ++j) y[j] = 0.f;
+#pragma unroll
+      for (int d = 0; d < D; ++d) {
+        const float xv = x[d];
+        const float4* prow = reinterpret_cast<const float4*>(P + d * R + s * SUB);
+#pragma unroll
+        for (int j = 0; j < SUB / 4; ++j) {
+          const float4 pv = prow[j];
+          y[4 * j] = mac(y[4 * j], xv, pv.x);
+          y[4 * j + 1] = mac(y[4 * j + 1], xv, pv.y);
+          y[4 * j + 2] = mac(y[4 * j + 2], xv, pv.z);
+          y[4 * j + 3] = mac(y[4 * j + 3], xv, pv.w);
+        }
+      }
+      if (kout) {
+        if (vec_out) {
+#pragma unroll
+          for (int j = 0; j < SUB / 4; ++j)
+            reinterpret_cast<float4*>(kout + s * SUB)[j] = make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < SUB; ++j) kout[s * SUB + j] = y[j];
+        }
+      }
+      if (crow) {
+        float xn = 0.f;
+#pragma unroll
+        for (int j = 0; j < SUB; ++j) xn = mac(xn, y[j], y[j]);
+        int best = 0;
+        float bestd = 0.f;
+        for (int c = 0; c < C; c += 4) {  // C is a multiple of 4
+          float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+#pragma unroll
+          for (int j = 0; j < SUB; ++j) {
+            const float4 cw = *reinterpret_cast<const float4*>(cbt + (s * SUB + j) * C + c);
+            d0 = mac(d0, y[j], cw.x);
+            d1 = mac(d1, y[j], cw.y);
+            d2 = mac(d2, y[j], cw.z);
+            d3 = mac(d3, y[j], cw.w);
+          }
+          const float dd[4] = {d0, d1, d2, d3};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float dist = __fadd_rn(__fsub_rn(xn, __fmul_rn(2.f, dd[q])), cn[s * C + c + q]);
+            if ((c + q) == 0 || dist < bestd) {
+              bestd = dist;
+              best = c + q;
+            }
+          }
+        }
+        crow[s] = static_cast<uint8_t>(best);
+      }
+    }
+  }
+}
+
 // Append path for a few keys (decode steps): one CTA per (key, head), so a one-key append is
 // spread over the threads of many CTAs instead of one thread of a 128-key tile.  Same canonical
 // arithmetic as catalog_encode_kernel: every projection output and every distance is one thread's
@@ -560,6 +675,43 @@ static int catalog_encode_impl(const void* keys, int32_t key_dtype, int64_t key_
     }
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? SVA_OK : set_error(SVA_ERR_CUDA, cudaGetErrorString(e));
+  }
+  if (head_dim == 64 && rank_dim == 64 && codewords % 4 == 0 &&
+      (p.sub == 8 || p.sub == 16 || p.sub == 32) && reinterpret_cast<uintptr_t>(k_proj) % 16 == 0 &&
+      (!codes || reinterpret_cast<uintptr_t>(codebooks) % 16 == 0)) {
+    const int esz = key_dtype == SVA_DTYPE_F32 ? 4 : 2;
+    const int vec_keys = (reinterpret_cast<uintptr_t>(keys) % 16 == 0 && (key_head_stride * esz) % 16 == 0 &&
+                          (key_row_stride * esz) % 16 == 0)
+                             ? 1
+                             : 0;
+    const int vec_out = (!k_low || (reinterpret_cast<uintptr_t>(k_low) % 16 == 0 && k_low_head_stride % 4 == 0)) ? 1 : 0;
+    const size_t rsmem = sizeof(float) * (64 * 64 + (size_t)64 * codewords + (size_t)subspaces * codewords);
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaGetLastError();
+    // tiles of the whole range (a device start may shift it by at most the rows past `start`)
+    const int64_t span = start_dev ? std::min<int64_t>(count, std::max<int64_t>(limit, 0)) : count;
+    const int64_t n_tiles = (span + kRegKeys - 1) / kRegKeys;
+    const int64_t want = std::max<int64_t>(1, (int64_t)sms * kRegCtasPerSm * 2 / n_heads);
+    dim3 rgrid((unsigned)std::max<int64_t>(1, std::min<int64_t>(n_tiles, want)), (unsigned)n_heads);
+    auto launch = [&](auto kernel) -> int {
+      const int rc2 = ensure_smem_attr(reinterpret_cast<const void*>(kernel), static_cast<int>(rsmem));
+      if (rc2) return rc2;
+      kernel<<<rgrid, kRegKeys, rsmem, s>>>(p, vec_keys, vec_out);
+      const cudaError_t e2 = cudaGetLastError();
+      return e2 == cudaSuccess ? SVA_OK : set_error(SVA_ERR_CUDA, cudaGetErrorString(e2));
+    };
+    switch (key_dtype * 3 + (p.sub == 8 ? 0 : p.sub == 16 ? 1 : 2)) {
+      case 0: return launch(catalog_encode_reg_kernel<float, 8>);
+      case 1: return launch(catalog_encode_reg_kernel<float, 16>);
+      case 2: return launch(catalog_encode_reg_kernel<float, 32>);
+      case 3: return launch(catalog_encode_reg_kernel<__nv_bfloat16, 8>);
+      case 4: return launch(catalog_encode_reg_kernel<__nv_bfloat16, 16>);
+      case 5: return launch(catalog_encode_reg_kernel<__nv_bfloat16, 32>);
+      case 6: return launch(catalog_encode_reg_kernel<__half, 8>);
+      case 7: return launch(catalog_encode_reg_kernel<__half, 16>);
+      default: return launch(catalog_encode_reg_kernel<__half, 32>);
+    }
   }
   catalog_layout(p);
   const size_t smem = sizeof(float) * p.total_floats;

@@ -319,16 +319,16 @@ template <int S>
 __device__ __forceinline__ Codes4<S> load_codes4(const uint8_t* base, int64_t i) {
   Codes4<S> r;
   if (S == 1) {
-    r.a.x = __ldg(reinterpret_cast<const uint32_t*>(base + i));
+    r.a.x = __ldcs(reinterpret_cast<const uint32_t*>(base + i));
   } else if (S == 2) {
-    const uint2 w = __ldg(reinterpret_cast<const uint2*>(base + 2 * i));
+    const uint2 w = __ldcs(reinterpret_cast<const uint2*>(base + 2 * i));
     r.a.x = w.x;
     r.a.y = w.y;
   } else if (S == 4) {
-    r.a = __ldg(reinterpret_cast<const uint4*>(base + 4 * i));
+    r.a = __ldcs(reinterpret_cast<const uint4*>(base + 4 * i));
   } else {
-    r.a = __ldg(reinterpret_cast<const uint4*>(base + 8 * i));
-    r.b = __ldg(reinterpret_cast<const uint4*>(base + 8 * i + 16));
+    r.a = __ldcs(reinterpret_cast<const uint4*>(base + 8 * i));
+    r.b = __ldcs(reinterpret_cast<const uint4*>(base + 8 * i + 16));
   }
   return r;
 }
@@ -899,6 +899,7 @@ __global__ void __launch_bounds__(NT, NT >= 512 ? 1 : 2) decode_prep_wide_kernel
       for (int d = tid; d < D; d += blockDim.x) qf[d] = to_f32<T>(q[d]);
   }
   __syncthreads();
+  if (tid == 0) stamp(p, prob, 0);
   const float* qp = p.a.q_proj + (size_t)h * D * R;
   for (int r = tid; r < R; r += blockDim.x) {
     float acc = 0.f;
@@ -917,13 +918,15 @@ __global__ void __launch_bounds__(NT, NT >= 512 ? 1 : 2) decode_prep_wide_kernel
       p.ws_ctrl[(size_t)prob * CTRL_WORDS + CTRL_MAXKEY] = 0u;
     }
   }
+  if (tid == 0) stamp(p, prob, 9);
   // sample: kWideRuns runs of kWideRunKeys keys evenly spaced over the allowed range
   int nv = 0;
   float smin = INFINITY, smax = -INFINITY;
-  for (int i = tid; i < kWideSample; i += blockDim.x) {
+  auto sample_key = [&](int i) -> int64_t {
     const int run = i / kWideRunKeys, off = i - run * kWideRunKeys;
-    const int64_t key = ((len_t * run) / kWideRuns) + off;
-    const uint32_t k = (key < len_t) ? adc_key<kB>(p, codes, lut, b, t, key, len_t) : 0u;
+    return ((len_t * run) / kWideRuns) + off;
+  };
+  auto note = [&](int i, uint32_t k) {
     skeys[i] = k;
     if (k != 0u) {
       const float sc = key_to_float(k);
@@ -931,7 +934,39 @@ __global__ void __launch_bounds__(NT, NT >= 512 ? 1 : 2) decode_prep_wide_kernel
       smax = fmaxf(smax, sc);
       ++nv;
     }
+  };
+  if (S2 == 4 && p.vec_codes && p.a.allowed_mask == nullptr) {
+    // four subspaces, rows 4-byte aligned: a thread loads the code words of kBatch sample keys
+    // before scoring any of them, so their latencies overlap (same sum as adc_key)
+    constexpr int kPer = kWideSample / NT;
+    constexpr int kBatch = kPer < 16 ? kPer : 16;
+    for (int m0 = 0; m0 < kPer; m0 += kBatch) {
+      uint32_t w[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int64_t key = sample_key(tid + (m0 + u) * NT);
+        w[u] = key < len_t ? __ldg(reinterpret_cast<const uint32_t*>(key_codes<kB>(p, codes, b, key))) : 0u;
+      }
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int i = tid + (m0 + u) * NT;
+        uint32_t k = 0u;
+        if (sample_key(i) < len_t) {
+          float sum = 0.f;
+#pragma unroll
+          for (int s = 0; s < 4; ++s) sum = __fadd_rn(sum, lut[s * C + ((w[u] >> (8 * s)) & 0xFFu)]);
+          k = ordered_key(finish_score(sum, p));
+        }
+        note(i, k);
+      }
+    }
+  } else {
+    for (int i = tid; i < kWideSample; i += blockDim.x) {
+      const int64_t key = sample_key(i);
+      note(i, (key < len_t) ? adc_key<kB>(p, codes, lut, b, t, key, len_t) : 0u);
+    }
   }
+  if (tid == 0) stamp(p, prob, 10);
   nv = __reduce_add_sync(0xFFFFFFFFu, nv);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -986,6 +1021,7 @@ __global__ void __launch_bounds__(NT, NT >= 512 ? 1 : 2) decode_prep_wide_kernel
     }
   }
   if (tid < kPrepCtas) p.ws_ctrl[(size_t)prob * CTRL_WORDS + CTRL_T0 + tid] = t0 > 1u ? t0 : 1u;
+  if (tid == 0) stamp(p, prob, 1);
 }
 
 // LUT lookup of key j in the bank-replicated table: entry e lives at lut[e * 32 + lane], so
@@ -1054,7 +1090,6 @@ __device__ __forceinline__ float adc_rep(const Codes4<S>& c, int j, uint32_t lan
 template <int S, int C, bool POW2, bool PAGED>
 __global__ void __launch_bounds__(kScanThreads, 2) decode_scan_kernel(const DecodeParams p) {
   constexpr bool kRep = (S > 0) && (C > 0) && (S * C <= kRepEntries);
-  constexpr int kInFlight = S == 8 ? 2 : kGroupsInFlight;  // 4-key groups loaded ahead per thread
   // the LUT lives in dynamic shared memory (scan_lut_bytes), its start rounded up at run time to
   // a multiple of its row field so that lookups can or the lane into the offset
   extern __shared__ __align__(16) unsigned char scan_dyn[];
@@ -1146,7 +1181,9 @@ __global__ void __launch_bounds__(kScanThreads, 2) decode_scan_kernel(const Deco
         if constexpr (POW2) return __fmul_rn(sum, scale);
         else return __fdiv_rn(sum, p.sqrt_r);
       };
-      const int tile = kScanThreads * kInFlight;
+      // software pipeline: a thread scores kPipe groups while its next kPipe groups load
+      constexpr int kPipe = S == 8 ? 1 : 2;
+      const int tile = kScanThreads * kPipe;
       const int nfull = ngroups - ngroups % tile;
       auto main_loop = [&](auto or_tag) {
         constexpr bool kOr = decltype(or_tag)::value;
@@ -1157,15 +1194,21 @@ __global__ void __launch_bounds__(kScanThreads, 2) decode_scan_kernel(const Deco
           if constexpr (POW2) return __fmul_rn(sum, scale);
           else return __fdiv_rn(sum, p.sqrt_r);
         };
+        Codes4<S> cur[kPipe];
+        if (tid < nfull) {
+#pragma unroll
+          for (int u = 0; u < kPipe; ++u) cur[u] = group_codes(tid + u * kScanThreads);
+        }
         for (int gb = tid; gb < nfull; gb += tile) {
-          Codes4<S> c[kInFlight];
+          Codes4<S> nxt[kPipe];
+          const int gn = gb + tile;
 #pragma unroll
-          for (int u = 0; u < kInFlight; ++u) c[u] = group_codes(gb + u * kScanThreads);
+          for (int u = 0; u < kPipe; ++u) nxt[u] = gn < nfull ? group_codes(gn + u * kScanThreads) : cur[u];
 #pragma unroll
-          for (int u = 0; u < kInFlight; ++u) {
+          for (int u = 0; u < kPipe; ++u) {
             float sc[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) sc[j] = score_fast(c[u], j);
+            for (int j = 0; j < 4; ++j) sc[j] = score_fast(cur[u], j);
             // one compare per group of four keys; candidates are rare
             if (fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3])) >= t0f) {
 #pragma unroll
@@ -1173,6 +1216,8 @@ __global__ void __launch_bounds__(kScanThreads, 2) decode_scan_kernel(const Deco
                 if (sc[j] >= t0f) take(ordered_key(sc[j]), i0 + 4 * (gb + u * kScanThreads) + j);
             }
           }
+#pragma unroll
+          for (int u = 0; u < kPipe; ++u) cur[u] = nxt[u];
         }
       };
       if (or_ok) main_loop(std::true_type{});
@@ -1599,19 +1644,23 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
 constexpr int kWideThreads = 256;     // threads of a wide finish CTA when many problems share each SM
 constexpr int kWideMaxThreads = 512;  // ... and when there is about one problem per SM
 constexpr int kWideCands = 4096;  // candidates selected in shared memory (more are streamed from L2)
+constexpr int kWideBigCands = 12288;  // ... when there is about one problem per SM
 constexpr int kWideMinProblems = 64;  // problems per launch from which the wide finish is used
 constexpr int kNumSmsHint = 148;      // B200 SMs: launches with at most this many problems give each 512 threads
 
 struct WideSmem {
   int qf, ql, sc, scratch, sl, rk, fin, lg, acc, cand, total;
+  int cand_cap;  // candidates selected in shared memory
 };
 
-__host__ __device__ inline WideSmem wide_smem_layout(int head_dim, int sl_cap, int b_cap, int dbg_cap) {
+__host__ __device__ inline WideSmem wide_smem_layout(int head_dim, int sl_cap, int b_cap, int dbg_cap,
+                                                     int cand_cap = kWideCands) {
   WideSmem s;
   int o = 0;
   // the candidate area also holds the LUT of the exact fallback (kMaxLut floats), the budget
   // select's composites (8 bytes per shortlist key) and the debug outputs' sort buffer
-  int cand = kWideCands;
+  int cand = cand_cap;
+  s.cand_cap = cand_cap;
   if (cand * 2 < kMaxLut) cand = kMaxLut / 2;
   if (cand < sl_cap) cand = sl_cap;
   if (cand < dbg_cap) cand = dbg_cap;
@@ -1663,9 +1712,14 @@ __global__ void __launch_bounds__(NT, NT >= 512 ? 1 : 3) decode_finish_wide_kern
     for (int r = tid; r < p.a.rank_dim; r += blockDim.x) ql[r] = __ldcg(p.ws_qlow + (size_t)prob * kMaxRank + r);
   }
   __syncthreads();
+  if (tid == 0) stamp(p, prob, 2);
   const int n_sl =
-      select_shortlist<kB>(p, prob, b, h, t, len_t, cand, lut, sc, scratch, sl, nullptr, true, kWideCands);
-  rescore_rows<8, kB>(p, b, h, ql, sl, n_sl, rk);
+      select_shortlist<kB>(p, prob, b, h, t, len_t, cand, lut, sc, scratch, sl, nullptr, true, lay.cand_cap);
+  if (tid == 0) stamp(p, prob, 3);
+  // four rows in flight per half-warp: one CTA runs this code once per problem, so a shorter
+  // unrolled body (fewer instruction fetches) beats more loads in flight
+  rescore_rows<4, kB>(p, b, h, ql, sl, n_sl, rk);
+  if (tid == 0) stamp(p, prob, 4);
   // budget select over (rank key, key index) composites with the known rank-key range
   uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
   unsigned long long* c64 = reinterpret_cast<unsigned long long*>(cand);
@@ -1698,8 +1752,10 @@ __global__ void __launch_bounds__(NT, NT >= 512 ? 1 : 3) decode_finish_wide_kern
   const int n_fin = compact_u64(c64, n_sl, thr, fin, scratch);  // shortlist positions
   for (int pos = tid; pos < n_fin; pos += blockDim.x) fin[pos] = sl[fin[pos]];
   __syncthreads();
-  verify_rows_fn<T>(k_rows<T, kB>(p, b, kvh, fin), v_rows<T, kB>(p, b, kvh, fin), qf, D, n_fin, p.a.softmax_scale,
-                    p.a.logits_mode, lg, acc, scratch, out_row<T, kB>(p, b, h, t));
+  if (tid == 0) stamp(p, prob, 5);
+  verify_rows_fn<T, 4>(k_rows<T, kB>(p, b, kvh, fin), v_rows<T, kB>(p, b, kvh, fin), qf, D, n_fin,
+                       p.a.softmax_scale, p.a.logits_mode, lg, acc, scratch, out_row<T, kB>(p, b, h, t));
+  if (tid == 0) stamp(p, prob, 6);
   unsigned long long* tmp = reinterpret_cast<unsigned long long*>(cand);
   if (p.a.shortlist_out) write_sorted(sl, n_sl, p.a.shortlist, p.a.shortlist_out + (size_t)prob * p.a.shortlist, tmp);
   if (p.a.final_out) write_sorted(fin, n_fin, p.a.budget, p.a.final_out + (size_t)prob * p.a.budget, tmp);
@@ -1877,7 +1933,8 @@ static int plan_decode(const sva_decode_args* a, DecodePlan* plan, bool force_gr
     plan->smem_bytes = static_cast<size_t>(plan->fin_lay.total);
     // with many problems per launch, one CTA per problem keeps more problems in flight than
     // one cluster per problem
-    plan->wide_lay = wide_smem_layout(a->head_dim, p.sl_cap, p.b_cap, dbg_cap);
+    plan->wide_lay = wide_smem_layout(a->head_dim, p.sl_cap, p.b_cap, dbg_cap,
+                                      P <= kNumSmsHint ? kWideBigCands : kWideCands);
     plan->wide = P >= kWideMinProblems && plan->wide_lay.total <= kMaxDynSmem;
     auto take = [&](size_t bytes) {
       size_t o = ws;

@@ -137,8 +137,10 @@ __global__ void __launch_bounds__(kThreads)
   if (tid < world && per_rank[tid] == k1 && k1 < p.a.shortlist && saturated) atomicOr(saturated, 1);
   const GatheredTop own{gathered, P, k1, prob, rank * k1};
   const int m = cta_compact(own, k1, thr, OwnShortlistEmit{rows, gidx, map}, scratch);
-  rescore_rows<8, kB>(p, b, h, ql, rows, m, rk);
-  verify_logits_fn<T>(k_rows<T, kB>(p, b, kvh, rows), qf, p.a.head_dim, m, p.a.softmax_scale, p.a.logits_mode, lg);
+  // four rows in flight per half-warp (a shorter body: this code runs once per problem)
+  rescore_rows<4, kB>(p, b, h, ql, rows, m, rk);
+  verify_logits_fn<T, false, 4>(k_rows<T, kB>(p, b, kvh, rows), qf, p.a.head_dim, m, p.a.softmax_scale,
+                                p.a.logits_mode, lg);
   uint4* out = records + (size_t)prob * k1;
   for (int j = tid; j < k1; j += blockDim.x) {
     if (j < m) {
@@ -199,7 +201,7 @@ __global__ void __launch_bounds__(kThreads)
                                 },
                                 scratch);
   double* sums = acc + (kThreads / 32) * 64;
-  accumulate_rows_fn<T>(v_rows<T, kB>(p, b, kvh, rows), D, w, n_own, acc, sums);
+  accumulate_rows_fn<T, false, 4>(v_rows<T, kB>(p, b, kvh, rows), D, w, n_own, acc, sums);
   for (int d = tid; d < D; d += blockDim.x) partial_out[(size_t)prob * D + d] = sums[d];
   if (p.a.stats && rank == 0 && tid == 0) {
     atomicAdd(p.a.stats + SVA_STAT_QUERIES, 1ull);

@@ -43,13 +43,13 @@ struct NoPrefetch {
 // logits of n selected keys: lg[j] = q . K[row(j)] * softmax_scale (see the file comment).
 // `vrow` (optional): the V rows of the same keys are prefetched into L2 while the K rows load,
 // so that the weighted sum that follows reads them from L2.
-// kShared: the rows live in shared memory (staged copies), read with plain loads.
-template <typename T, bool kShared = false, class KRow, class VRow = NoPrefetch>
+// kShared: the rows live in shared memory (staged copies), read with plain loads.  U: rows in
+// flight per half-warp.
+template <typename T, bool kShared = false, int U = kVerifyUnroll, class KRow, class VRow = NoPrefetch>
 __device__ void verify_logits_fn(const KRow& krow, const float* qf, int D, int n, float softmax_scale,
                                  int logits_mode, float* lg, const VRow& vrow = VRow(), bool prefetch_v = false) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   const int half = lane >> 4, l16 = lane & 15;
-  constexpr int U = kVerifyUnroll;
   for (int base = warp * 2 * U; base < n; base += nwarps * 2 * U) {
     float part[U];
 #pragma unroll
@@ -166,12 +166,11 @@ __device__ void softmax_weights(float* lg, int n, float mx, float denom) {
 }
 
 // out[d] = sum_j round_T(w[j] * V[row(j)][d]) in fp64 for d < D (written by threads 0..63 per
-// 64-wide chunk).  `acc` needs (blockDim.x / 32) * 64 doubles.
-template <typename T, bool kShared = false, class VRow>
+// 64-wide chunk).  `acc` needs (blockDim.x / 32) * 64 doubles.  U: rows in flight per half-warp.
+template <typename T, bool kShared = false, int U = kVerifyUnroll, class VRow>
 __device__ void accumulate_rows_fn(const VRow& vrow, int D, const float* w, int n, double* acc, double* out) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   const int half = lane >> 4, l16 = lane & 15;
-  constexpr int U = kVerifyUnroll;
   const int nchunks = (D + 63) / 64;
   for (int c = 0; c < nchunks; ++c) {
     const int e = c * 64 + 4 * l16;
@@ -227,17 +226,18 @@ __device__ void accumulate_rows(const void* values, int64_t v_head_stride, int64
 }
 
 // The whole verify inside one CTA.  Shared memory: lg[n_fin] floats; acc[(nwarps * 64) +
-// nwarps + 1] doubles; red[kMaxHeadDim] doubles for the output sums; scratch[64] ints.
-template <typename T, class KRow, class VRow>
+// nwarps + 1] doubles; red[kMaxHeadDim] doubles for the output sums; scratch[64] ints.  U: rows
+// in flight per half-warp.
+template <typename T, int U = kVerifyUnroll, class KRow, class VRow>
 __device__ void verify_rows_fn(const KRow& krow, const VRow& vrow, const float* qf, int D, int n_fin,
                                float softmax_scale, int logits_mode, float* lg, double* acc, int* scratch, T* out) {
-  verify_logits_fn<T>(krow, qf, D, n_fin, softmax_scale, logits_mode, lg);
+  verify_logits_fn<T, false, U>(krow, qf, D, n_fin, softmax_scale, logits_mode, lg);
   float mx, denom;
   const int nwarps = blockDim.x >> 5;
   softmax_stats(lg, n_fin, scratch, acc, &mx, &denom);
   softmax_weights<T>(lg, n_fin, mx, denom);
   double* sums = acc + nwarps * 64;  // D doubles after the per-warp partials
-  accumulate_rows_fn<T>(vrow, D, lg, n_fin, acc, sums);
+  accumulate_rows_fn<T, false, U>(vrow, D, lg, n_fin, acc, sums);
   for (int d = threadIdx.x; d < D; d += blockDim.x) out[d] = from_f32<T>(n_fin > 0 ? static_cast<float>(sums[d]) : 0.f);
   __syncthreads();
 }
