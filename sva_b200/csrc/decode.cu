@@ -1331,7 +1331,9 @@ static __device__ __forceinline__ int select_shortlist(const DecodeParams& p, in
       copy_batched(c64, gc, n_cand);
       if (tid == 0) stamp(p, prob, 12);
       const SelectThreshold thr = select_u64(c64, n_cand, k, lo, hi, sc);
+      if (tid == 0) stamp(p, prob, 13);
       n_sl = compact_u64(c64, n_cand, thr, out_idx, scratch);
+      if (tid == 0) stamp(p, prob, 14);
       for (int pos = tid; pos < n_sl; pos += blockDim.x) {
         const unsigned long long c = c64[out_idx[pos]];
         out_idx[pos] = static_cast<int32_t>(~static_cast<uint32_t>(c));

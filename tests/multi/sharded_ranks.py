@@ -22,6 +22,47 @@ from tests.golden.inputs import config2  # noqa: E402
 from tests.helpers import gpu_catalog, gpu_decode  # noqa: E402
 
 
+def batched_ranks(rank: int, world: int, dev: torch.device) -> bool:
+    """BatchedShardedDecoder over a bf16 batch, eager and captured in a CUDA graph (kernels and
+    NCCL all-gathers), must equal the one-GPU batched decode bit for bit."""
+    from sva_b200.sharded import BatchedShardedDecoder
+    from tests.test_gpu_batched import make_batch
+    from tests.test_gpu_sharded_batched import key_range_ranks, one_gpu
+
+    batch = make_batch([60000, 60000, 56000, 64000], seed=41)
+    want = one_gpu(batch)
+    x = key_range_ranks(batch, world)[rank]
+    dec = BatchedShardedDecoder(dist.group.WORLD, 2048, 512, dev)
+
+    def call(saturated=None, out=None):
+        return dec.decode(x["q"], x["q_proj"], x["scale"], x["cb"], x["codes"], x["k_low"], x["keys"], x["values"],
+                          seq_lens=x["seq_lens"], max_len=x["max_len"], key_offset=x["key_offset"], out=out,
+                          logits_mode=1, softmax_scale=0.125, saturated=saturated)
+
+    eager = call()
+    torch.cuda.synchronize()
+    # captured: the ranks' shares of these shortlists fit the exchange width (no saturation)
+    sat = torch.zeros(1, dtype=torch.int32, device=dev)
+    out = torch.empty_like(eager)
+    stream = torch.cuda.Stream(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        call(sat, out)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=stream):
+            call(sat, out)
+    sat.zero_()
+    out.zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    flagged = int(sat.item())
+    good = torch.equal(eager, want) and (flagged == 1 or torch.equal(out, want))
+    print(f"rank {rank}: batched eager_equal={torch.equal(eager, want)} graph_equal={torch.equal(out, want)} "
+          f"saturated={flagged}", flush=True)
+    del graph
+    return good
+
+
 def main() -> int:
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -46,6 +87,7 @@ def main() -> int:
         equal = float((a == b).float().mean())
         print(f"rank {rank}: allclose={close} bit_equal_fraction={equal:.4f}", flush=True)
         ok = close and equal >= 0.99
+        ok = batched_ranks(rank, world, dev) and ok
         flag = torch.tensor([1 if ok else 0], device=dev)
         dist.all_reduce(flag, op=dist.ReduceOp.MIN)
         return 0 if int(flag.item()) == 1 else 1

@@ -1,7 +1,9 @@
 """Key-range sharded decode on 2 GPUs over NCCL (skipped with fewer than 2 GPUs).
 
 Runs tests/multi/sharded_ranks.py under torchrun (127.0.0.1, a short process-group timeout, an
-outer time limit, NVLS off): every rank's output must match the one-GPU decode over all keys.
+outer time limit, NVLS off): every rank's output must match the one-GPU decode over all keys,
+for a single sequence (ShardedDecoder) and for a batch of sequences (BatchedShardedDecoder,
+eager and captured in a CUDA graph with its NCCL all-gathers).
 """
 
 from __future__ import annotations
