@@ -68,6 +68,8 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-1x256", dest="alt_pq", action="store_false",
+                    help="skip the 1x256-code serving and latency measurement of the same sequences")
     ap.add_argument("--no-inverted", dest="inverted", action="store_false",
                     help="skip the static inverted-index summon measurement")
     ap.add_argument("--no-ragged", dest="ragged", action="store_false",
@@ -334,7 +336,8 @@ def build_batch(args, device, rank: int, world: int, keep_full_first: bool = Fal
         del fk, fv
     torch.cuda.synchronize()
     return dict(q=q.to(device), q_proj=q_proj, scale=torch.ones(heads, dtype=torch.float32, device=device), cb=cb,
-                codes=codes, k_low=k_low, keys=kk, values=vv, offset=lo, write=write, full_first=full_first)
+                codes=codes, k_low=k_low, keys=kk, values=vv, offset=lo, write=write, full_first=full_first,
+                k_proj=k_proj)
 
 
 def inverted_measure(args, sets, device) -> dict:
@@ -818,6 +821,72 @@ def latency_measure(args, batch, device, peak: float) -> dict:
                       f"{n} eager calls with pinned host q / out"}
 
 
+def pq_1x256_measure(args, batch, device, peak: float) -> dict:
+    """The same sequences with 1x256 codes (the reference's best published PQ setting, 0.649 ms on
+    an H100): a 1x256 codebook per head, every sequence's codes written by the library, then the
+    serving call (CUDA graph of --tokens-per-step calls) and the single-query latency (CUDA graph
+    of 64 queries over --sets sequences), device-timed after warm-ups; sequence 0 of a serving
+    call is checked against its single-sequence decode."""
+    import argparse
+
+    import torch
+
+    from sva_b200 import kernels
+
+    heads, n, L = args.heads, args.sequences, int(batch["codes"].shape[2])
+    gen = torch.Generator().manual_seed(args.seed * 1000 + 256)
+    cb = torch.randn(heads, 1, 256, 64, generator=gen).to(torch.bfloat16).float().to(device)
+    codes = torch.empty(n, heads, L, 1, dtype=torch.uint8, device=device)
+    for i in range(n):
+        kernels.catalog_encode(batch["keys"][i], batch["k_proj"], cb, 0, L, None, codes[i])
+    out = torch.empty_like(batch["q"])
+
+    def serve(i=0):
+        kernels.decode_batched(batch["q"], batch["q_proj"], batch["scale"], cb, codes, batch["k_low"], batch["keys"],
+                               batch["values"], args.shortlist, args.budget, softmax_scale=0.125, logits_mode=1,
+                               out=out)
+
+    def timed(graph, reps):
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        return 1000.0 * e0.elapsed_time(e1) / reps
+
+    calls = args.tokens_per_step
+    graph, _ = profiled_graph(lambda i: serve(), calls, device, 3)
+    serve_us = timed(graph, max(2, args.steps // 2)) / (calls * n)
+    del graph
+    st0 = dict(seq_view(batch, 0), cb=cb, codes=codes[0])
+    ref = kernels.decode(st0["q"], st0["q_proj"], st0["scale"], cb, codes[0], st0["k_low"], st0["keys"], st0["values"],
+                         args.shortlist, args.budget, softmax_scale=0.125, logits_mode=1)
+    torch.cuda.synchronize()
+    parity = bool(torch.equal(ref, out[0]))
+    sets = [dict(seq_view(batch, i), codes=codes[i]) for i in range(min(args.sets, n))]
+    outs = [torch.empty_like(x["q"]) for x in sets]
+
+    def one(i):
+        x = sets[i % len(sets)]
+        kernels.decode(x["q"], x["q_proj"], x["scale"], cb, x["codes"], x["k_low"], x["keys"], x["values"],
+                       args.shortlist, args.budget, softmax_scale=0.125, logits_mode=1, out=outs[i % len(sets)])
+
+    graph, _ = profiled_graph(one, 64, device, 3)
+    lat_us = timed(graph, max(2, args.steps // 2)) / 64
+    del graph, codes
+    ab = algorithmic_bytes(argparse.Namespace(**{**vars(args), "pq": "1x256"}))
+    return {"serving_us_per_query": round(serve_us, 3), "latency_us_per_query": round(lat_us, 3),
+            "vs_published_h100": round(lat_us / PUBLISHED_US["1x256"], 5),
+            "algorithmic_bytes_per_query": int(ab["total"]),
+            "serving_frac": round(ab["total"] / (serve_us * 1e-6) / 1e9 / peak, 4),
+            "parity": ("ok" if parity else "MISMATCH") + ": sequence 0 of the serving call vs its single-sequence decode",
+            "timing": f"CUDA graphs ({calls} serving calls of {n} sequences; 64 single queries), device clock"}
+
+
 def cpu_parity_and_baseline(args, batch, device) -> tuple[dict, str]:
     """The cpu_baseline leg: the oracle's threaded CPU decoder on sequence 0's own catalog (copied to
     the host), timed on all host threads over a bounded sample, and its final sets and outputs
@@ -1044,6 +1113,8 @@ def gpu_arm(args):
     }
     if world == 1:
         line["latency"] = latency_measure(args, batch, device, peak)
+        if args.pq == "4x64" and args.alt_pq:
+            line["pq_1x256"] = pq_1x256_measure(args, batch, device, peak)
         if args.inverted:
             line["inverted_static"] = inverted_measure(args, [seq_view(batch, i) for i in range(args.sets)], device)
     elif args.inverted:

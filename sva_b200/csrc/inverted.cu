@@ -260,20 +260,29 @@ __global__ void __launch_bounds__(kInvScoreThreads) inv_score_kernel(const InvPa
     }
     if (tid == 0 && n_round > 0) res_base = atomicAdd(ctrl + IC_NCAND, static_cast<uint32_t>(n_round));
     __syncthreads();
-    // rank-score the queued keys: one half-warp per key
+    // rank-score the queued keys: one half-warp per key, kRows rows in flight per half-warp
     const int half = lane >> 4, l16 = lane & 15;
     const float4 q4 = make_float4(ql[4 * l16], ql[4 * l16 + 1], ql[4 * l16 + 2], ql[4 * l16 + 3]);
-    for (int j0 = warp * 2; j0 < n_round; j0 += nwarps * 2) {
-      const int j = j0 + half;
-      float4 r4 = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (j < n_round && 4 * l16 < R) r4 = load4<float>(klb + (int64_t)qkey[j] * R, 4 * l16, R);
-      const float s = tree16(lane4(r4, q4));
-      if (j < n_round && l16 == 0) {
-        const uint32_t k32 = ordered_key(inv_finish(s, p));
-        const uint32_t slot = res_base + j;
-        if (slot < p.cand_cap)
-          cand[slot] = make_uint2(k32, (static_cast<uint32_t>(qkey[j]) << 4) | static_cast<uint32_t>(qm[j]));
-        atomicAdd(&hist[k32 >> 20], 1u);
+    constexpr int kRows = 4;
+    for (int j0 = warp * 2 * kRows; j0 < n_round; j0 += nwarps * 2 * kRows) {
+      float4 r4[kRows];
+#pragma unroll
+      for (int u = 0; u < kRows; ++u) {
+        const int j = j0 + 2 * u + half;
+        r4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (j < n_round && 4 * l16 < R) r4[u] = load4<float>(klb + (int64_t)qkey[j] * R, 4 * l16, R);
+      }
+#pragma unroll
+      for (int u = 0; u < kRows; ++u) {
+        const int j = j0 + 2 * u + half;
+        const float s = tree16(lane4(r4[u], q4));
+        if (j < n_round && l16 == 0) {
+          const uint32_t k32 = ordered_key(inv_finish(s, p));
+          const uint32_t slot = res_base + j;
+          if (slot < p.cand_cap)
+            cand[slot] = make_uint2(k32, (static_cast<uint32_t>(qkey[j]) << 4) | static_cast<uint32_t>(qm[j]));
+          atomicAdd(&hist[k32 >> 20], 1u);
+        }
       }
     }
     __syncthreads();
