@@ -315,8 +315,11 @@ static __device__ __forceinline__ SelectThreshold radix_select_u64(const unsigne
   return cta_radix_select(U64Items{a}, n, k, sc);
 }
 
-// cta_select_linear over a[0, n) (fallback: radix_select_u64).
-static __device__ __forceinline__ SelectThreshold select_u64(const unsigned long long* a, int n, int k, float lo,
+// cta_select_linear over a[0, n) (fallback: radix_select_u64).  Not inlined: a kernel that selects
+// twice (shortlist, then budget) runs one copy of the code, so the second select finds its
+// instructions already fetched (a one-CTA-per-problem finish runs each phase once per problem,
+// and instruction fetch is a large part of such a phase).
+static __device__ __noinline__ SelectThreshold select_u64(const unsigned long long* a, int n, int k, float lo,
                                                             float hi, SelectScratch* sc) {
   return cta_select_linear(U64Items{a}, n, k, lo, hi, sc, [&]() { return radix_select_u64(a, n, k, sc); });
 }
@@ -399,7 +402,7 @@ namespace sva {
 
 // Stable compaction of the selected items of a[0, n): out[pos] = i for the pos-th selected item
 // i in item order.  Returns the count; ends with a barrier.
-static __device__ __forceinline__ int compact_u64(const unsigned long long* a, int n, SelectThreshold thr, int32_t* out,
+static __device__ __noinline__ int compact_u64(const unsigned long long* a, int n, SelectThreshold thr, int32_t* out,
                                                   int* scratch) {
   return cta_compact(U64Items{a}, n, thr, [&](int pos, int i, unsigned long long) { out[pos] = i; }, scratch);
 }
