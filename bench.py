@@ -129,14 +129,27 @@ class ClockSampler:
             return
         self._thread = threading.Thread(target=self._read, daemon=True)
         self._thread.start()
+        # nvidia-smi can take a second to start on a many-GPU box: wait for its first sample
+        deadline = time.time() + 10.0
+        while not self.lines and time.time() < deadline and self.proc.poll() is None:
+            time.sleep(0.01)
 
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
+    def mark(self) -> None:
+        """Call at the start of the timed region: stop() reports the samples taken from here on."""
+        self._mark = len(self.lines)
+
     def stop(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        # a short timed region may end between two samples: take at least two after the mark
+        first = getattr(self, "_mark", 0)
+        deadline = time.time() + 1.0
+        while len(self.lines) < first + 2 and time.time() < deadline and self.proc.poll() is None:
+            time.sleep(0.01)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -146,7 +159,7 @@ class ClockSampler:
             self._thread.join(timeout=2)
         sm, mx, power, reasons = [], [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in self.lines[first:]:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -1044,6 +1057,7 @@ def gpu_arm(args):
     sampler.start()
     time.sleep(0.3)
     torch.cuda.synchronize()
+    sampler.mark()
     t_wall = time.perf_counter()
     cur = torch.cuda.current_stream(device)
     for i in range(args.steps):
@@ -1293,6 +1307,7 @@ def model_arm(args):
         handle.reset_catalogs()
         sampler = ClockSampler(None)
         sampler.start()
+        sampler.mark()
         pf, dm, em, toks = graphed_decode(model, prompt, steps, device)
         clocks = sampler.stop()
         summary = handle.stats.summary()
