@@ -96,13 +96,19 @@ struct OwnShortlistEmit {
 // composite lo, hi, logit bits, 0).  A rank that sent k1 entries all inside the global shortlist
 // may hold more members it did not send: the problem is then flagged in *saturated and the host
 // repeats the exchange with k1 = SL.
+// The gathered lists are staged in shared memory when they fit (`staged`, kShardStageItems): the
+// select then runs the linear-bin select over the known key range (the same non-inlined code as
+// the finish kernels) on shared memory instead of a radix select whose every level re-reads L2.
+constexpr int kShardStageItems = 8192;
+
 template <typename T, bool kB>
 __global__ void __launch_bounds__(kThreads)
     shard_rescore_kernel(const DecodeParams p, const ShardMap map, int world, int rank, int k1,
                          const unsigned long long* __restrict__ gathered, uint4* __restrict__ records,
-                         int* __restrict__ saturated) {
+                         int* __restrict__ saturated, int staged) {
   extern __shared__ __align__(16) unsigned char smem[];
-  int32_t* rows = reinterpret_cast<int32_t*>(smem);
+  unsigned long long* g64 = reinterpret_cast<unsigned long long*>(smem);  // world * k1 when staged
+  int32_t* rows = reinterpret_cast<int32_t*>(smem + (staged ? 8 * (size_t)world * k1 : 0));
   uint32_t* gidx = reinterpret_cast<uint32_t*>(rows + k1);
   uint32_t* rk = gidx + k1;
   float* lg = reinterpret_cast<float*>(rk + k1);
@@ -125,18 +131,65 @@ __global__ void __launch_bounds__(kThreads)
   }
   const GatheredTop item{gathered, P, k1, prob, 0};
   const int N = world * k1;
-  int nz = 0;
-  for (int i = tid; i < N; i += blockDim.x) nz += item(i) != 0ull;
-  nz = block_sum_int(nz, scratch);
-  const int k = min(p.a.shortlist, nz);
-  const SelectThreshold thr = cta_radix_select(item, N, k, &sc);
-  // members per rank; a rank whose k1 sent entries are all members may hold unsent members
-  for (int i = tid; i < N; i += blockDim.x)
-    if (is_selected(thr, item(i))) atomicAdd(&per_rank[i / k1], 1);
-  __syncthreads();
-  if (tid < world && per_rank[tid] == k1 && k1 < p.a.shortlist && saturated) atomicOr(saturated, 1);
-  const GatheredTop own{gathered, P, k1, prob, rank * k1};
-  const int m = cta_compact(own, k1, thr, OwnShortlistEmit{rows, gidx, map}, scratch);
+  int m;
+  if (staged) {
+    constexpr int kBatch = 8;
+    for (int i0 = tid; i0 < N; i0 += kBatch * blockDim.x) {
+      unsigned long long c[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) c[u] = i0 + u * blockDim.x < N ? item(i0 + u * blockDim.x) : 0ull;
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u)
+        if (i0 + u * blockDim.x < N) g64[i0 + u * blockDim.x] = c[u];
+    }
+    __syncthreads();
+    // count and key range of the non-zero composites
+    int nz = 0;
+    uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
+    for (int i = tid; i < N; i += blockDim.x) {
+      const unsigned long long c = g64[i];
+      if (c != 0ull) {
+        ++nz;
+        kmin = min(kmin, static_cast<uint32_t>(c >> 32));
+        kmax = max(kmax, static_cast<uint32_t>(c >> 32));
+      }
+    }
+    kmin = __reduce_min_sync(0xFFFFFFFFu, kmin);
+    kmax = __reduce_max_sync(0xFFFFFFFFu, kmax);
+    if ((tid & 31) == 0) {
+      sc.lo_part[tid >> 5] = kmin;
+      sc.hi_part[tid >> 5] = kmax;
+    }
+    nz = block_sum_int(nz, scratch);  // ends with a barrier: lo_part / hi_part are visible
+    uint32_t lo = 0xFFFFFFFFu, hi = 0u;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) {
+      lo = min(lo, static_cast<uint32_t>(sc.lo_part[w]));
+      hi = max(hi, static_cast<uint32_t>(sc.hi_part[w]));
+    }
+    __syncthreads();
+    const int k = min(p.a.shortlist, nz);
+    const SelectThreshold thr =
+        nz > 0 ? select_u64(g64, N, k, key_to_float(lo), key_to_float(hi), &sc) : SelectThreshold{~0ull, 0ull};
+    // members per rank; a rank whose k1 sent entries are all members may hold unsent members
+    for (int i = tid; i < N; i += blockDim.x)
+      if (is_selected(thr, g64[i])) atomicAdd(&per_rank[i / k1], 1);
+    __syncthreads();
+    if (tid < world && per_rank[tid] == k1 && k1 < p.a.shortlist && saturated) atomicOr(saturated, 1);
+    m = cta_compact(U64Items{g64 + (size_t)rank * k1}, k1, thr, OwnShortlistEmit{rows, gidx, map}, scratch);
+  } else {
+    int nz = 0;
+    for (int i = tid; i < N; i += blockDim.x) nz += item(i) != 0ull;
+    nz = block_sum_int(nz, scratch);
+    const int k = min(p.a.shortlist, nz);
+    const SelectThreshold thr = cta_radix_select(item, N, k, &sc);
+    // members per rank; a rank whose k1 sent entries are all members may hold unsent members
+    for (int i = tid; i < N; i += blockDim.x)
+      if (is_selected(thr, item(i))) atomicAdd(&per_rank[i / k1], 1);
+    __syncthreads();
+    if (tid < world && per_rank[tid] == k1 && k1 < p.a.shortlist && saturated) atomicOr(saturated, 1);
+    const GatheredTop own{gathered, P, k1, prob, rank * k1};
+    m = cta_compact(own, k1, thr, OwnShortlistEmit{rows, gidx, map}, scratch);
+  }
   // four rows in flight per half-warp (a shorter body: this code runs once per problem)
   rescore_rows<4, kB>(p, b, h, ql, rows, m, rk);
   verify_logits_fn<T, false, 4>(k_rows<T, kB>(p, b, kvh, rows), qf, p.a.head_dim, m, p.a.softmax_scale,
@@ -157,13 +210,17 @@ __global__ void __launch_bounds__(kThreads)
 template <typename T, bool kB>
 __global__ void __launch_bounds__(kThreads)
     shard_verify_kernel(const DecodeParams p, const ShardMap map, int world, int rank, int k1,
-                        const uint4* __restrict__ gathered, double* __restrict__ partial_out) {
+                        const uint4* __restrict__ gathered, double* __restrict__ partial_out, int staged) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int B = p.a.budget;
   double* acc = reinterpret_cast<double*>(smem);  // (kThreads / 32) * 64 + kMaxHeadDim doubles
   float* lgs = reinterpret_cast<float*>(acc + (kThreads / 32) * 64 + kMaxHeadDim);
   int32_t* rows = reinterpret_cast<int32_t*>(lgs + B);
   float* w = reinterpret_cast<float*>(rows + B);
+  // staged: the gathered records' composites and logits (world * k1 of each) after w, 8-aligned
+  unsigned long long* g64 = reinterpret_cast<unsigned long long*>(
+      (reinterpret_cast<uintptr_t>(w + B) + 7u) & ~static_cast<uintptr_t>(7u));
+  float* glg = reinterpret_cast<float*>(g64 + (staged ? (size_t)world * k1 : 0));
   __shared__ SelectScratch sc;
   __shared__ int scratch[64];
   const int prob = blockIdx.x;
@@ -182,24 +239,80 @@ __global__ void __launch_bounds__(kThreads)
     return (static_cast<unsigned long long>(v.y) << 32) | v.x;
   };
   const int N = world * k1;
-  int nz = 0;
-  for (int i = tid; i < N; i += blockDim.x) nz += item(i) != 0ull;
-  const int n_sl = block_sum_int(nz, scratch);
-  const int nb = min(B, n_sl);
-  const SelectThreshold thr = cta_radix_select(item, N, nb, &sc);
-  const int n_fin = cta_compact(item, N, thr,
-                                [&](int pos, int i, unsigned long long) { lgs[pos] = __uint_as_float(rec(i).z); },
-                                scratch);
+  int n_sl, n_fin, n_own;
   float mx, denom;
-  softmax_stats(lgs, n_fin, scratch, acc, &mx, &denom);
-  auto own = [&](int j) -> unsigned long long { return item(rank * k1 + j); };
-  const int n_own = cta_compact(own, k1, thr,
-                                [&](int pos, int j, unsigned long long c) {
-                                  rows[pos] = static_cast<int32_t>(map.to_local(~static_cast<uint32_t>(c)));
-                                  const float lj = __uint_as_float(rec(rank * k1 + j).z);
-                                  w[pos] = round_to<T>(expf(lj - mx) / denom);
-                                },
-                                scratch);
+  if (staged) {
+    constexpr int kBatch = 8;
+    for (int i0 = tid; i0 < N; i0 += kBatch * blockDim.x) {
+      uint4 v[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u)
+        v[u] = i0 + u * blockDim.x < N ? rec(i0 + u * blockDim.x) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int i = i0 + u * blockDim.x;
+        if (i < N) {
+          g64[i] = (static_cast<unsigned long long>(v[u].y) << 32) | v[u].x;
+          glg[i] = __uint_as_float(v[u].z);
+        }
+      }
+    }
+    __syncthreads();
+    int nz = 0;
+    uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
+    for (int i = tid; i < N; i += blockDim.x) {
+      const unsigned long long c = g64[i];
+      if (c != 0ull) {
+        ++nz;
+        kmin = min(kmin, static_cast<uint32_t>(c >> 32));
+        kmax = max(kmax, static_cast<uint32_t>(c >> 32));
+      }
+    }
+    kmin = __reduce_min_sync(0xFFFFFFFFu, kmin);
+    kmax = __reduce_max_sync(0xFFFFFFFFu, kmax);
+    if ((tid & 31) == 0) {
+      sc.lo_part[tid >> 5] = kmin;
+      sc.hi_part[tid >> 5] = kmax;
+    }
+    n_sl = block_sum_int(nz, scratch);
+    uint32_t lo = 0xFFFFFFFFu, hi = 0u;
+    for (int wi = 0; wi < static_cast<int>(blockDim.x >> 5); ++wi) {
+      lo = min(lo, static_cast<uint32_t>(sc.lo_part[wi]));
+      hi = max(hi, static_cast<uint32_t>(sc.hi_part[wi]));
+    }
+    __syncthreads();
+    const int nb = min(B, n_sl);
+    const SelectThreshold thr =
+        n_sl > 0 ? select_u64(g64, N, nb, key_to_float(lo), key_to_float(hi), &sc) : SelectThreshold{~0ull, 0ull};
+    n_fin = cta_compact(U64Items{g64}, N, thr, [&](int pos, int i, unsigned long long) { lgs[pos] = glg[i]; },
+                        scratch);
+    softmax_stats(lgs, n_fin, scratch, acc, &mx, &denom);
+    const float* own_lg = glg + (size_t)rank * k1;
+    n_own = cta_compact(U64Items{g64 + (size_t)rank * k1}, k1, thr,
+                        [&](int pos, int j, unsigned long long c) {
+                          rows[pos] = static_cast<int32_t>(map.to_local(~static_cast<uint32_t>(c)));
+                          w[pos] = round_to<T>(expf(own_lg[j] - mx) / denom);
+                        },
+                        scratch);
+  } else {
+    int nz = 0;
+    for (int i = tid; i < N; i += blockDim.x) nz += item(i) != 0ull;
+    n_sl = block_sum_int(nz, scratch);
+    const int nb = min(B, n_sl);
+    const SelectThreshold thr = cta_radix_select(item, N, nb, &sc);
+    n_fin = cta_compact(item, N, thr,
+                        [&](int pos, int i, unsigned long long) { lgs[pos] = __uint_as_float(rec(i).z); },
+                        scratch);
+    softmax_stats(lgs, n_fin, scratch, acc, &mx, &denom);
+    auto own = [&](int j) -> unsigned long long { return item(rank * k1 + j); };
+    n_own = cta_compact(own, k1, thr,
+                        [&](int pos, int j, unsigned long long c) {
+                          rows[pos] = static_cast<int32_t>(map.to_local(~static_cast<uint32_t>(c)));
+                          const float lj = __uint_as_float(rec(rank * k1 + j).z);
+                          w[pos] = round_to<T>(expf(lj - mx) / denom);
+                        },
+                        scratch);
+  }
   double* sums = acc + (kThreads / 32) * 64;
   accumulate_rows_fn<T, false, 4>(v_rows<T, kB>(p, b, kvh, rows), D, w, n_own, acc, sums);
   for (int d = tid; d < D; d += blockDim.x) partial_out[(size_t)prob * D + d] = sums[d];
@@ -297,11 +410,12 @@ static int shard_rescore(DecodePlan& plan, const ShardMap& map, int world, int r
   DecodeParams& p = plan.p;
   bind_workspace(p, ws);
   k1 = k1_of(plan, k1);
-  const int smem = 16 * k1;
+  const int staged = world * k1 <= kShardStageItems ? 1 : 0;
+  const int smem = 16 * k1 + (staged ? 8 * world * k1 : 0);
   auto k = p.batched ? shard_rescore_kernel<T, true> : shard_rescore_kernel<T, false>;
   int rc = ensure_smem_attr(reinterpret_cast<const void*>(k), smem);
   if (rc != SVA_OK) return rc;
-  k<<<p.n_probs, kThreads, smem, st>>>(p, map, world, rank, k1, gathered, records, saturated);
+  k<<<p.n_probs, kThreads, smem, st>>>(p, map, world, rank, k1, gathered, records, saturated, staged);
   return launch_status();
 }
 
@@ -310,11 +424,12 @@ static int shard_verify(DecodePlan& plan, const ShardMap& map, int world, int ra
                         double* partial, cudaStream_t st) {
   DecodeParams& p = plan.p;
   k1 = k1_of(plan, k1);
-  const int smem = 8 * ((kThreads / 32) * 64 + kMaxHeadDim) + 12 * p.a.budget;
+  const int staged = world * k1 <= kShardStageItems ? 1 : 0;
+  const int smem = 8 * ((kThreads / 32) * 64 + kMaxHeadDim) + 12 * p.a.budget + 8 + (staged ? 12 * world * k1 : 0);
   auto k = p.batched ? shard_verify_kernel<T, true> : shard_verify_kernel<T, false>;
   int rc = ensure_smem_attr(reinterpret_cast<const void*>(k), smem);
   if (rc != SVA_OK) return rc;
-  k<<<p.n_probs, kThreads, smem, st>>>(p, map, world, rank, k1, gathered, partial);
+  k<<<p.n_probs, kThreads, smem, st>>>(p, map, world, rank, k1, gathered, partial, staged);
   return launch_status();
 }
 
