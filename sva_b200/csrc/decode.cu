@@ -1663,7 +1663,10 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
 // arithmetic as the cluster finish (and as the fused kernel).
 constexpr int kWideThreads = 256;     // threads of a wide finish CTA when many problems share each SM
 constexpr int kWideMaxThreads = 512;  // ... and when there is about one problem per SM
-constexpr int kWideCands = 4096;  // candidates selected in shared memory (more are streamed from L2)
+// candidates selected in shared memory (more are streamed from L2): 8192 (64 KB) with two CTAs
+// per SM; ragged batches hold short sequences whose candidates are all of their keys, and a
+// shared-memory select of those beats a third CTA per SM streaming them from L2
+constexpr int kWideCands = 8192;
 constexpr int kWideBigCands = 12288;  // ... when there is about one problem per SM
 constexpr int kWideMinProblems = 64;  // problems per launch from which the wide finish is used
 constexpr int kNumSmsHint = 148;      // B200 SMs: launches with at most this many problems give each 512 threads
@@ -1699,7 +1702,7 @@ __host__ __device__ inline WideSmem wide_smem_layout(int head_dim, int sl_cap, i
 }
 
 template <typename T, bool kB, int NT = kWideThreads>
-__global__ void __launch_bounds__(NT, NT >= 512 ? 1 : 3) decode_finish_wide_kernel(const DecodeParams p,
+__global__ void __launch_bounds__(NT, NT >= 512 ? 1 : 2) decode_finish_wide_kernel(const DecodeParams p,
                                                                                   const WideSmem lay) {
   extern __shared__ __align__(16) unsigned char smem[];
   float* qf = reinterpret_cast<float*>(smem + lay.qf);
