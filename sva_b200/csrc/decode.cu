@@ -1777,8 +1777,37 @@ __global__ void __launch_bounds__(NT, NT >= 512 ? 1 : 2) decode_finish_wide_kern
   for (int pos = tid; pos < n_fin; pos += blockDim.x) fin[pos] = sl[fin[pos]];
   __syncthreads();
   if (tid == 0) stamp(p, prob, 5);
-  verify_rows_fn<T, 4>(k_rows<T, kB>(p, b, kvh, fin), v_rows<T, kB>(p, b, kvh, fin), qf, D, n_fin,
-                       p.a.softmax_scale, p.a.logits_mode, lg, acc, scratch, out_row<T, kB>(p, b, h, t));
+  // the candidate area is free from here on: when the final set's V rows fit there (and the
+  // rows are 16-byte aligned), copy them to shared memory while the logits and the softmax are
+  // computed, so that the weighted sum reads shared memory (the same arithmetic as verify_rows_fn)
+  const bool v_stage =
+      p.kv_stage != 0 && static_cast<size_t>(n_fin) * D * sizeof(T) <= static_cast<size_t>(lay.total - lay.cand);
+  if (v_stage) {
+    T* vst = reinterpret_cast<T*>(smem + lay.cand);
+    const T* vb = values_base<T, kB>(p, b, kvh);
+    constexpr int kPer = 16 / static_cast<int>(sizeof(T));  // elements per 16-byte copy
+    const int cpr = D / kPer;
+    for (int e = tid; e < n_fin * cpr; e += blockDim.x) {
+      const int jj = e / cpr, q = e - jj * cpr;
+      cp_async16(vst + jj * D + q * kPer, key_row<T, kB>(p, vb, b, fin[jj], p.v_page_stride, p.a.v_row_stride) + q * kPer);
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+    verify_logits_fn<T, false, 4>(k_rows<T, kB>(p, b, kvh, fin), qf, D, n_fin, p.a.softmax_scale, p.a.logits_mode,
+                                  lg);
+    float mx, denom;
+    softmax_stats(lg, n_fin, scratch, acc, &mx, &denom);
+    softmax_weights<T>(lg, n_fin, mx, denom);
+    asm volatile("cp.async.wait_all;\n" ::: "memory");
+    __syncthreads();
+    double* sums = acc + (blockDim.x >> 5) * 64;
+    accumulate_rows_fn<T, true, 4>(StridedRows<T>{vst, D, nullptr}, D, lg, n_fin, acc, sums);
+    T* o = out_row<T, kB>(p, b, h, t);
+    for (int d = tid; d < D; d += blockDim.x) o[d] = from_f32<T>(n_fin > 0 ? static_cast<float>(sums[d]) : 0.f);
+    __syncthreads();
+  } else {
+    verify_rows_fn<T, 4>(k_rows<T, kB>(p, b, kvh, fin), v_rows<T, kB>(p, b, kvh, fin), qf, D, n_fin,
+                         p.a.softmax_scale, p.a.logits_mode, lg, acc, scratch, out_row<T, kB>(p, b, h, t));
+  }
   if (tid == 0) stamp(p, prob, 6);
   unsigned long long* tmp = reinterpret_cast<unsigned long long*>(cand);
   if (p.a.shortlist_out) write_sorted(sl, n_sl, p.a.shortlist, p.a.shortlist_out + (size_t)prob * p.a.shortlist, tmp);
